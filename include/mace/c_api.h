@@ -1,0 +1,49 @@
+/* MACE MH1 C ABI of the B200 build.
+ *
+ * The first six entry points are the reference's ABI with identical signatures and
+ * semantics (mace/include/mace/c_api.h:7-15, mace/src/c_api.cpp:18-98): return 0 on
+ * success, -1 on failure with a thread-local message from mace_last_error(); create
+ * returns NULL on failure; handles are single-flight; outputs are caller-owned, in input
+ * atom order, and valid on return; an error does not poison the handle.
+ * Backend: 0 Auto, 1 BruteForce, 2 CellList.
+ */
+#pragma once
+#include <mace/export.h>
+#include <stddef.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+/* Replaces mace_create_mh1 (mace/include/mace/c_api.h:8). */
+MACE_EXPORT void *mace_create_mh1(const char *archive, int backend);
+/* Replaces mace_create_mh1_head (mace/include/mace/c_api.h:10).  Archives carry one
+ * head; a non-empty head is rejected for them like the reference does. */
+MACE_EXPORT void *mace_create_mh1_head(const char *model, int backend, const char *head);
+/* Replaces mace_destroy (mace/include/mace/c_api.h:11). */
+MACE_EXPORT void mace_destroy(void *handle);
+/* Replaces mace_last_error (mace/include/mace/c_api.h:12); thread-local. */
+MACE_EXPORT const char *mace_last_error(void);
+/* Replaces mace_calculate (mace/include/mace/c_api.h:13-14).  xyz n x 3 Angstrom, cell
+ * 3 x 3 rows, virial 3 x 3 row major = -dE/dstrain (eV).  Null pointers only when n == 0. */
+MACE_EXPORT int mace_calculate(void *handle, int n, const float *xyz, const int *elements, const float *cell,
+                               double *energy, float *per_atom, float *force, float *virial);
+/* Replaces mace_diagnostics (mace/include/mace/c_api.h:15): JSON into buffer. */
+MACE_EXPORT int mace_diagnostics(void *handle, char *buffer, size_t capacity);
+
+/* ---- B200 build additions (no counterpart in the reference ABI) ---- */
+
+/* Like mace_create_mh1 but binds the handle to CUDA device `device` (the reference binds
+ * to whatever device is current at creation). */
+MACE_EXPORT void *mace_create_mh1_device(const char *archive, int backend, int device);
+/* mace_calculate with DEVICE-resident xyz/elements (device pointers on the handle's GPU);
+ * results still land in the caller's host arrays.  Lets a caller that keeps structures in
+ * HBM skip the host-to-device copy. */
+MACE_EXPORT int mace_calculate_device(void *handle, int n, const float *xyz_device, const int *elements_device,
+                                      const float *cell, double *energy, float *per_atom, float *force,
+                                      float *virial);
+/* Directed edges of the last successful call, in input atom indices: out[5 * k] =
+ * (receiver, sender, sx, sy, sz) for k < min(count, capacity), canonically sorted.
+ * Returns the edge count (which may exceed capacity) or -1. */
+MACE_EXPORT long long mace_last_edges(void *handle, int *out, long long capacity);
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,20 @@
+// mace::MH1 -- the C++ model API (same surface as mace/include/mace/mh1.hpp:6-19).
+#pragma once
+#include <lapis/runtime.hpp>
+#include <mace/export.h>
+#include <memory>
+namespace mace {
+class MACE_EXPORT MH1 final : public lapis::Calculator {
+  struct Model;
+  std::unique_ptr<Model> model_;
+  lapis::Result evaluate() override;
+
+public:
+  // PWMH1001 archive.  An empty head is required for archives (they carry one head).
+  explicit MH1(const std::string &model, lapis::Options options = {});
+  MH1(const std::string &model, lapis::Options options, const std::string &head);
+  ~MH1() override;
+  size_t parameter_bytes() const;
+  lapis::Result calculate_file(const std::string &path, size_t frame = 0);
+};
+} // namespace mace
