@@ -94,7 +94,7 @@ class Context {
   std::map<std::string, Buffer> buffers_;
   void *pinned_ = nullptr;
   size_t pinned_capacity_ = 0;
-  void build_connectivity(bool brute_selected, bool choose_on_device);
+  const int *input_elements_ = nullptr; // device copy of the input-order atomic numbers
 
 public:
   cudaStream_t stream{};
@@ -124,8 +124,10 @@ public:
   }
   void prepare(const Structure &, float, const Options &);
   // Reorders per-node energies/forces into input order and reduces energy and virial in
-  // float64 on the device; node_virials is the per-node 3x3 virial [n][9].
-  Result finish(float *energies, float *forces, float *node_virials);
+  // float64 on the device; node_virials is the per-node 3x3 virial [n][9].  When
+  // e0_by_z (device, indexed by atomic number) is given, each atom's baseline energy is
+  // added to its energy and to the total, in float64 for the total.
+  Result finish(float *energies, float *forces, float *node_virials, const float *e0_by_z = nullptr);
   void synchronize();
   int status_code(); // device status word (0 ok, 1 zero distance, 2 unknown element)
 };

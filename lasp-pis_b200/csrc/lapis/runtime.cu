@@ -1,0 +1,646 @@
+// Lapis L0 runtime for B200: device workspaces, on-device geometry preparation, the
+// receiver-major CSR neighbour list, and the deterministic output reduction.
+//
+// Reference behaviour followed (LipidL/LASP-PIS):
+//   lapis/src/runtime.cu:80-203  cell validation, H^-1 (adjugate), plane heights, grid
+//                                dims/images, grid coarsening, float64 wrap + winding + bin,
+//                                occupancy work estimate and the Auto backend rule;
+//   lapis/include/lapis/pair.cuh:58-62,99-171  float32 displacement, inclusive cutoff,
+//                                all periodic images, (i, i, 0) excluded, 27-bin stencil;
+//   lapis/src/runtime.cu:269-313 output order restore, finiteness checks, float64 sums.
+// Where the reference runs a host loop per atom (wrap/bin) this build runs a kernel whose
+// float64 operations use explicit round-to-nearest intrinsics in the same order, so the
+// wrapped float32 positions -- and therefore the edge set -- are bit-identical.  The Auto
+// backend rule is evaluated on the device from exact integer occupancy sums, so prepare()
+// needs one host synchronisation (to size the edge arrays) instead of two.
+#include "lapis/runtime.hpp"
+#include <algorithm>
+#include <climits>
+#include <cmath>
+#include <cstring>
+
+namespace lapis {
+namespace {
+constexpr int kStatusBadElement = 3, kStatusNonfinite = 4, kStatusWinding = 5, kStatusReverse = 6;
+
+struct WrapParams {
+  double inv[9], h[9];
+  int dims[3];
+};
+
+__global__ void wrap_atoms(int n, const float *xyz, const int *z, WrapParams p, float *wxyz, int *wind,
+                           int *bin, int *counts, int *status) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n)
+    return;
+  int zi = z[i];
+  if (zi < 1 || zi > 118)
+    atomicCAS(status, 0, kStatusBadElement);
+  double f[3];
+  int b[3];
+  float q[3] = {xyz[3 * i], xyz[3 * i + 1], xyz[3 * i + 2]};
+  if (!isfinite(q[0]) || !isfinite(q[1]) || !isfinite(q[2])) {
+    atomicCAS(status, 0, kStatusNonfinite);
+    q[0] = q[1] = q[2] = 0;
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    double v = __dmul_rn(double(q[0]), p.inv[k]);
+    v = __dadd_rn(v, __dmul_rn(double(q[1]), p.inv[3 + k]));
+    v = __dadd_rn(v, __dmul_rn(double(q[2]), p.inv[6 + k]));
+    double w = floor(v);
+    if (fabs(w) > double(INT_MAX / 4)) {
+      atomicCAS(status, 0, kStatusWinding);
+      w = 0;
+    }
+    wind[3 * i + k] = int(w);
+    f[k] = __dsub_rn(v, w);
+    int bb = int(__dmul_rn(f[k], double(p.dims[k])));
+    b[k] = min(p.dims[k] - 1, bb);
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    double x = __dmul_rn(f[0], p.h[k]);
+    x = __dadd_rn(x, __dmul_rn(f[1], p.h[3 + k]));
+    x = __dadd_rn(x, __dmul_rn(f[2], p.h[6 + k]));
+    wxyz[3 * i + k] = __double2float_rn(x);
+  }
+  int bi = (b[0] * p.dims[1] + b[1]) * p.dims[2] + b[2];
+  bin[i] = bi;
+  atomicAdd(counts + bi, 1);
+}
+
+// Exclusive scan of n ints by one CTA of 1024 threads; out[n] receives the total.
+__global__ void scan_exclusive(const int *in, int *out, int n, long long *total) {
+  __shared__ long long partial[1024];
+  int t = threadIdx.x;
+  long long chunk = (n + 1023) / 1024;
+  long long begin = t * chunk < n ? t * chunk : n;
+  long long end = begin + chunk < n ? begin + chunk : n, s = 0;
+  for (long long k = begin; k < end; ++k)
+    s += in[k];
+  partial[t] = s;
+  __syncthreads();
+  for (int step = 1; step < 1024; step *= 2) {
+    long long v = t >= step ? partial[t - step] : 0;
+    __syncthreads();
+    partial[t] += v;
+    __syncthreads();
+  }
+  long long run = t ? partial[t - 1] : 0;
+  for (long long k = begin; k < end; ++k) {
+    out[k] = int(run);
+    run += in[k];
+  }
+  if (t == 1023) {
+    out[n] = int(partial[1023]);
+    if (total)
+      *total = partial[1023];
+  }
+}
+
+__global__ void place_atoms(int n, const int *bin, const int *offsets, int *cursor, int *i2o) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n)
+    i2o[offsets[bin[i]] + atomicAdd(cursor + bin[i], 1)] = i;
+}
+
+// Within each bin, order atoms by input index: a deterministic internal order.
+__global__ void order_bins(int nb, const int *offsets, int *i2o) {
+  int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= nb)
+    return;
+  int begin = offsets[b], end = offsets[b + 1];
+  for (int k = begin + 1; k < end; ++k) {
+    int v = i2o[k], q = k - 1;
+    while (q >= begin && i2o[q] > v) {
+      i2o[q + 1] = i2o[q];
+      --q;
+    }
+    i2o[q + 1] = v;
+  }
+}
+
+__global__ void gather_atoms(int n, const int *i2o, const float *wxyz, const int *z, const int *bin,
+                             const int *wind, float *sx, int *sz, int *sb, int *sw, int *o2i) {
+  int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n)
+    return;
+  int i = i2o[k];
+  o2i[i] = k;
+  sz[k] = z[i];
+  sb[k] = bin[i];
+  for (int q = 0; q < 3; ++q) {
+    sx[3 * k + q] = wxyz[3 * i + q];
+    sw[3 * k + q] = wind[3 * i + q];
+  }
+}
+
+struct ConnStats {
+  long long total_edges;
+  unsigned long long work;
+  int occupied, max_occupancy, status, cell;
+};
+
+// Occupancy-estimated cell-list work (sum over occupied bins of occupancy times stencil
+// occupancy), occupied-bin count and maximum occupancy -- exact integers.
+__global__ void bin_stats(int nb, int gx, int gy, int gz, const int *offsets, ConnStats *st) {
+  int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= nb)
+    return;
+  int occ = offsets[b + 1] - offsets[b];
+  if (!occ)
+    return;
+  atomicAdd(&st->occupied, 1);
+  atomicMax(&st->max_occupancy, occ);
+  int z = b % gz, y = (b / gz) % gy, x = b / (gy * gz);
+  unsigned long long s = 0;
+  for (int dx = -1; dx <= 1; ++dx)
+    for (int dy = -1; dy <= 1; ++dy)
+      for (int dz = -1; dz <= 1; ++dz) {
+        int c = (((x + dx + gx) % gx) * gy + (y + dy + gy) % gy) * gz + (z + dz + gz) % gz;
+        s += (unsigned long long)occ * (offsets[c + 1] - offsets[c]);
+      }
+  atomicAdd(&st->work, s);
+}
+
+// Backend rule of the reference (runtime.cu:183-191): cell list when every plane height is
+// at least the cutoff and the occupancy work is below 0.9 x the brute-force candidates.
+__global__ void decide_backend(ConnStats *st, int mode, int grid_ok, double brute) {
+  if (mode == 1)
+    st->cell = 0;
+  else if (mode == 2)
+    st->cell = 1;
+  else
+    st->cell = grid_ok && double(st->work) < brute * .9;
+}
+
+__device__ __forceinline__ int floor_div(int a, int b) {
+  int q = a / b, r = a % b;
+  return q - (r < 0);
+}
+
+struct Traverse {
+  int n, grid[3], images[3];
+  float h[9], cutoff2;
+  const float *xyz;
+  const int *bins, *offsets, *winding;
+  const ConnStats *stats; // stats->cell selects the 27-bin stencil or all atoms x images
+};
+
+// One warp per internal receiver.  Candidate order is fixed (stencil or image order, then
+// bin order), so the edge order inside a receiver is deterministic.  Count pass when
+// out_sender == nullptr, fill pass otherwise.
+__global__ void neighbour_pass(Traverse g, int *counts, const int *row, int *out_sender, int *out_shift,
+                               float4 *out_vec) {
+  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= g.n)
+    return;
+  int i = warp;
+  bool cell = g.stats->cell;
+  float xi = g.xyz[3 * i], yi = g.xyz[3 * i + 1], zi = g.xyz[3 * i + 2];
+  int wi0 = g.winding[3 * i], wi1 = g.winding[3 * i + 1], wi2 = g.winding[3 * i + 2];
+  int bx = 0, by = 0, bz = 0;
+  if (cell) {
+    int b = g.bins[i];
+    bz = b % g.grid[2];
+    b /= g.grid[2];
+    by = b % g.grid[1];
+    bx = b / g.grid[1];
+  }
+  int nx = cell ? 1 : g.images[0], ny = cell ? 1 : g.images[1], nz = cell ? 1 : g.images[2];
+  int count = 0, base_out = out_sender ? row[i] : 0;
+  for (int x = -nx; x <= nx; ++x)
+    for (int y = -ny; y <= ny; ++y)
+      for (int z = -nz; z <= nz; ++z) {
+        int sx = x, sy = y, sz = z, begin = 0, end = g.n;
+        if (cell) {
+          sx = floor_div(bx + x, g.grid[0]);
+          sy = floor_div(by + y, g.grid[1]);
+          sz = floor_div(bz + z, g.grid[2]);
+          int c = ((bx + x - sx * g.grid[0]) * g.grid[1] + by + y - sy * g.grid[1]) * g.grid[2] + bz + z -
+                  sz * g.grid[2];
+          begin = g.offsets[c];
+          end = g.offsets[c + 1];
+        }
+        for (int base = begin; base < end; base += 32) {
+          int j = base + lane;
+          bool valid = j < end;
+          float dx = 0, dy = 0, dz = 0, r2 = 0;
+          if (valid) {
+            // Same expression and evaluation order as the reference displacement().
+            dx = g.xyz[3 * j] + sx * g.h[0] + sy * g.h[3] + sz * g.h[6] - xi;
+            dy = g.xyz[3 * j + 1] + sx * g.h[1] + sy * g.h[4] + sz * g.h[7] - yi;
+            dz = g.xyz[3 * j + 2] + sx * g.h[2] + sy * g.h[5] + sz * g.h[8] - zi;
+            r2 = dx * dx + dy * dy + dz * dz;
+            valid = r2 <= g.cutoff2 && !(i == j && sx == 0 && sy == 0 && sz == 0);
+          }
+          unsigned mask = __ballot_sync(0xffffffffu, valid);
+          if (out_sender && valid) {
+            int e = base_out + count + __popc(mask & ((1u << lane) - 1));
+            out_sender[e] = j;
+            out_shift[3 * e] = sx + wi0 - g.winding[3 * j];
+            out_shift[3 * e + 1] = sy + wi1 - g.winding[3 * j + 1];
+            out_shift[3 * e + 2] = sz + wi2 - g.winding[3 * j + 2];
+            out_vec[e] = make_float4(dx, dy, dz, sqrtf(r2));
+          }
+          count += __popc(mask);
+        }
+      }
+  if (!out_sender && lane == 0)
+    counts[i] = count;
+}
+
+// For edge e = (i <- j, s) find the edge (j <- i, -s) in j's row.
+__global__ void reverse_edges(const int *row, const int *sender, const int *shift, int *reverse, int *status) {
+  int i = blockIdx.x;
+  for (int e = row[i] + threadIdx.x; e < row[i + 1]; e += blockDim.x) {
+    int j = sender[e], s0 = -shift[3 * e], s1 = -shift[3 * e + 1], s2 = -shift[3 * e + 2], found = -1;
+    for (int q = row[j]; q < row[j + 1]; ++q)
+      if (sender[q] == i && shift[3 * q] == s0 && shift[3 * q + 1] == s1 && shift[3 * q + 2] == s2) {
+        found = q;
+        break;
+      }
+    if (found < 0)
+      atomicCAS(status, 0, kStatusReverse);
+    reverse[e] = found < 0 ? e : found;
+  }
+}
+
+// Output staging: per input atom (energy [+ baseline], force) in input order and per-CTA
+// float64 partial sums of energy and the 9 virial components over a fixed range of input
+// indices; a second single-CTA pass sums the partials in a fixed order (deterministic).
+constexpr int kReduceBlocks = 120;
+__global__ void restore_outputs(int n, const int *o2i, const float *e, const float *f, const float *v,
+                                const float *e0, const int *z, float *out, double *partial) {
+  __shared__ double red[10][256];
+  int t = threadIdx.x;
+  long long per = (n + kReduceBlocks - 1) / kReduceBlocks;
+  long long begin = (long long)blockIdx.x * per < n ? (long long)blockIdx.x * per : n;
+  long long end = begin + per < n ? begin + per : n;
+  double acc[10] = {};
+  for (long long o = begin + t; o < end; o += blockDim.x) {
+    int k = o2i[o];
+    float base = e0 ? e0[z[o]] : 0.f;
+    float ev = e[k];
+    out[o] = ev + base;
+    acc[0] += double(ev) + double(base);
+    for (int q = 0; q < 3; ++q)
+      out[n + 3 * o + q] = f[3 * k + q];
+    for (int q = 0; q < 9; ++q)
+      acc[1 + q] += double(v[9 * k + q]);
+  }
+  for (int q = 0; q < 10; ++q)
+    red[q][t] = acc[q];
+  __syncthreads();
+  for (int step = 128; step; step >>= 1) {
+    if (t < step)
+      for (int q = 0; q < 10; ++q)
+        red[q][t] += red[q][t + step];
+    __syncthreads();
+  }
+  if (t < 10)
+    partial[blockIdx.x * 10 + t] = red[t][0];
+}
+__global__ void sum_partials(const double *partial, double *out) {
+  int q = threadIdx.x;
+  if (q < 10) {
+    double s = 0;
+    for (int b = 0; b < kReduceBlocks; ++b)
+      s += partial[b * 10 + q];
+    out[q] = s;
+  }
+}
+} // namespace
+
+bool Buffer::reserve(size_t bytes) {
+  if (bytes <= capacity)
+    return false;
+  void *fresh = nullptr;
+  check(cudaMalloc(&fresh, bytes));
+  if (data)
+    cudaFree(data);
+  data = fresh;
+  capacity = bytes;
+  return true;
+}
+
+Context::Context() {
+  check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+  check(cudaEventCreate(&start));
+  check(cudaEventCreate(&stop));
+}
+
+Context::~Context() {
+  cudaStreamSynchronize(stream);
+  if (pinned_)
+    cudaFreeHost(pinned_);
+  cudaEventDestroy(start);
+  cudaEventDestroy(stop);
+  cudaStreamDestroy(stream);
+}
+
+void *Context::reserve(const std::string &name, size_t bytes) {
+  auto &b = buffers_[name];
+  size_t previous = b.capacity;
+  size_t during = diagnostics.allocated_bytes + (bytes > previous ? bytes : 0);
+  b.reserve(bytes ? bytes : 1);
+  diagnostics.allocated_bytes += b.capacity - previous;
+  diagnostics.peak_bytes = std::max({diagnostics.peak_bytes, diagnostics.allocated_bytes, during});
+  return b.data;
+}
+
+static void grow_pinned(void *&pinned, size_t &capacity, size_t bytes) {
+  if (bytes <= capacity)
+    return;
+  void *fresh = nullptr;
+  check(cudaMallocHost(&fresh, bytes));
+  if (pinned)
+    cudaFreeHost(pinned);
+  pinned = fresh;
+  capacity = bytes;
+}
+
+void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
+  resources.clear();
+  if (s.size < 0 || s.size > INT_MAX / 16 || !std::isfinite(cutoff) || cutoff <= 0 ||
+      !std::isfinite(cutoff * cutoff))
+    throw Error("Invalid atom count or cutoff");
+  if (!s.pbc[0] || !s.pbc[1] || !s.pbc[2])
+    throw Error("v1 requires three periodic axes");
+  bool on_device = device_positions != nullptr;
+  if (s.size && !on_device && (!s.positions || !s.elements))
+    throw Error("Null structure data");
+  if (opts.grid_to_atom_budget < 1 || opts.grid_byte_budget < 16)
+    throw Error("Invalid grid budget");
+  double h[9];
+  for (int k = 0; k < 9; ++k) {
+    h[k] = s.cell[k];
+    if (!std::isfinite(h[k]))
+      throw Error("Nonfinite cell");
+  }
+  double det = h[0] * (h[4] * h[8] - h[5] * h[7]) - h[1] * (h[3] * h[8] - h[5] * h[6]) +
+               h[2] * (h[3] * h[7] - h[4] * h[6]);
+  double scale = 0;
+  for (double a : h)
+    scale = std::max(scale, std::abs(a));
+  if (!std::isfinite(det) || scale == 0 || std::abs(det) < 1e-10 * scale * scale * scale)
+    throw Error("Singular or ill-conditioned cell");
+  WrapParams wp;
+  double *inv = wp.inv;
+  inv[0] = (h[4] * h[8] - h[5] * h[7]) / det;
+  inv[1] = (h[2] * h[7] - h[1] * h[8]) / det;
+  inv[2] = (h[1] * h[5] - h[2] * h[4]) / det;
+  inv[3] = (h[5] * h[6] - h[3] * h[8]) / det;
+  inv[4] = (h[0] * h[8] - h[2] * h[6]) / det;
+  inv[5] = (h[2] * h[3] - h[0] * h[5]) / det;
+  inv[6] = (h[3] * h[7] - h[4] * h[6]) / det;
+  inv[7] = (h[1] * h[6] - h[0] * h[7]) / det;
+  inv[8] = (h[0] * h[4] - h[1] * h[3]) / det;
+  std::copy(h, h + 9, wp.h);
+  int dims[3], images[3];
+  bool grid_ok = true;
+  for (int k = 0; k < 3; ++k) {
+    double height = 1 / std::sqrt(inv[k] * inv[k] + inv[3 + k] * inv[3 + k] + inv[6 + k] * inv[6 + k]);
+    double ratio = height / cutoff;
+    grid_ok &= ratio >= 1;
+    dims[k] = int(std::max(1.0, std::min(double(INT_MAX / 4), std::floor(ratio))));
+    double im = std::ceil(cutoff / height);
+    if (im > 1000000)
+      throw Error("Excessive periodic image range");
+    images[k] = std::max(1, int(im));
+  }
+  if (double(2 * images[0] + 1) * (2 * images[1] + 1) * (2 * images[2] + 1) > INT_MAX)
+    throw Error("Periodic image tuples exceed v1 int32 capacity");
+  if (opts.backend == NeighborBackend::CellList && !grid_ok)
+    throw Error("CellList requires all reciprocal plane heights >= cutoff");
+  size_t cap = std::max(size_t(1), std::min({opts.grid_byte_budget / 16,
+                                             size_t(std::max(s.size, 1)) * size_t(opts.grid_to_atom_budget),
+                                             size_t(INT_MAX / 4)}));
+  bool coarsened = false;
+  while (double(dims[0]) * dims[1] * dims[2] > double(cap)) {
+    int axis = int(std::max_element(dims, dims + 3) - dims);
+    dims[axis] = (dims[axis] + 1) / 2;
+    coarsened = true;
+  }
+  std::copy(dims, dims + 3, wp.dims);
+  int nb = dims[0] * dims[1] * dims[2], n = s.size;
+  original_elements.clear();
+  if (n && !on_device) {
+    original_elements.assign(s.elements, s.elements + n);
+    for (int z : original_elements)
+      if (z < 1 || z > 118)
+        throw Error("Invalid atomic number");
+    for (size_t k = 0; k < size_t(n) * 3; ++k)
+      if (!std::isfinite(s.positions[k]))
+        throw Error("Nonfinite coordinate");
+  }
+  grow_pinned(pinned_, pinned_capacity_, size_t(n) * 16 + 256);
+  check(cudaEventRecord(start, stream));
+  const float *in_xyz = device_positions;
+  const int *in_z = device_elements;
+  if (!on_device) {
+    // Pinned staging (xyz then Z, 16 bytes per atom): one asynchronous upload that leaves
+    // the caller's arrays untouched.
+    auto *px = static_cast<float *>(pinned_);
+    if (n) {
+      std::memcpy(px, s.positions, size_t(n) * 12);
+      std::memcpy(px + size_t(n) * 3, s.elements, size_t(n) * 4);
+    }
+    float *dx = array<float>("input.xyzz", size_t(n) * 4);
+    if (n)
+      check(cudaMemcpyAsync(dx, px, size_t(n) * 16, cudaMemcpyHostToDevice, stream));
+    in_xyz = dx;
+    in_z = reinterpret_cast<const int *>(dx + size_t(n) * 3);
+  }
+  input_elements_ = in_z;
+  float *wxyz = array<float>("prep.xyz", size_t(n) * 3);
+  int *wind = array<int>("prep.winding", size_t(n) * 3);
+  int *bin = array<int>("prep.bin", n);
+  float *sorted = array<float>("geometry.xyz", size_t(n) * 3);
+  int *sz = array<int>("geometry.z", n);
+  int *sb = array<int>("geometry.bin", n);
+  int *sw = array<int>("geometry.winding", size_t(n) * 3);
+  internal_to_original = array<int>("geometry.i2o", n);
+  original_to_internal = array<int>("geometry.o2i", n);
+  int *counts = array<int>("grid.count", size_t(nb) + 1);
+  int *offsets = array<int>("grid.offset", size_t(nb) + 1);
+  int *cursor = array<int>("grid.cursor", nb);
+  int *status = array<int>("status", 4);
+  auto *stats = array<ConnStats>("stats", 1);
+  int *row_counts = array<int>("edges.count", size_t(n) + 1);
+  int *row = array<int>("edges.offset", size_t(n) + 1);
+  clear(counts, size_t(nb + 1) * 4);
+  clear(cursor, size_t(nb) * 4);
+  clear(status, 16);
+  clear(stats, sizeof(ConnStats));
+  clear(row_counts, size_t(n + 1) * 4);
+  double brute = double(n) * n;
+  for (int k = 0; k < 3; ++k)
+    brute *= 2 * images[k] + 1;
+  int blocks = (n + 255) / 256;
+  if (n)
+    wrap_atoms<<<blocks, 256, 0, stream>>>(n, in_xyz, in_z, wp, wxyz, wind, bin, counts, status);
+  scan_exclusive<<<1, 1024, 0, stream>>>(counts, offsets, nb, nullptr);
+  if (n) {
+    place_atoms<<<blocks, 256, 0, stream>>>(n, bin, offsets, cursor, internal_to_original);
+    order_bins<<<(nb + 255) / 256, 256, 0, stream>>>(nb, offsets, internal_to_original);
+    gather_atoms<<<blocks, 256, 0, stream>>>(n, internal_to_original, wxyz, in_z, bin, wind, sorted, sz, sb, sw,
+                                             original_to_internal);
+    bin_stats<<<(nb + 255) / 256, 256, 0, stream>>>(nb, dims[0], dims[1], dims[2], offsets, stats);
+  }
+  decide_backend<<<1, 1, 0, stream>>>(stats, int(opts.backend), grid_ok, brute);
+  Traverse tv;
+  tv.n = n;
+  std::copy(dims, dims + 3, tv.grid);
+  std::copy(images, images + 3, tv.images);
+  std::copy(s.cell.begin(), s.cell.end(), tv.h);
+  tv.cutoff2 = cutoff * cutoff;
+  tv.xyz = sorted;
+  tv.bins = sb;
+  tv.offsets = offsets;
+  tv.winding = sw;
+  tv.stats = stats;
+  if (n) {
+    neighbour_pass<<<(n * 32 + 255) / 256, 256, 0, stream>>>(tv, row_counts, nullptr, nullptr, nullptr, nullptr);
+    scan_exclusive<<<1, 1024, 0, stream>>>(row_counts, row, n, &stats->total_edges);
+  }
+  check(cudaGetLastError());
+  // The single host synchronisation of prepare(): edge total, backend, diagnostics, status.
+  auto *hs = reinterpret_cast<ConnStats *>(static_cast<char *>(pinned_) + size_t(n) * 16 + 64);
+  check(cudaMemcpyAsync(hs, stats, sizeof(ConnStats), cudaMemcpyDeviceToHost, stream));
+  check(cudaMemcpyAsync(&hs->status, status, 4, cudaMemcpyDeviceToHost, stream));
+  check(cudaStreamSynchronize(stream));
+  if (hs->status == kStatusBadElement)
+    throw Error("Invalid atomic number");
+  if (hs->status == kStatusNonfinite)
+    throw Error("Nonfinite coordinate");
+  if (hs->status == kStatusWinding)
+    throw Error("Coordinate winding exceeds int32 range");
+  auto selected = hs->cell ? NeighborBackend::CellList : NeighborBackend::BruteForce;
+  std::string reason = "explicit backend";
+  if (opts.backend == NeighborBackend::Auto)
+    reason = !grid_ok ? "reciprocal plane height below cutoff"
+             : selected == NeighborBackend::CellList
+                 ? (coarsened ? "coarsened grid has lower occupancy-estimated work"
+                              : "grid has lower occupancy-estimated work")
+                 : "brute force has comparable or lower estimated work";
+  diagnostics.selected = selected;
+  diagnostics.reason = reason;
+  diagnostics.grid = {dims[0], dims[1], dims[2]};
+  diagnostics.max_occupancy = hs->max_occupancy;
+  diagnostics.occupied_bins = hs->occupied;
+  diagnostics.mean_occupancy = double(n) / nb;
+  diagnostics.grid_candidates = double(hs->work);
+  diagnostics.brute_candidates = brute;
+  long long total = n ? hs->total_edges : 0;
+  if (total > INT_MAX)
+    throw Error("Directed edge count exceeds int32 capacity");
+  diagnostics.edges = total;
+  int *sender = array<int>("edges.sender", size_t(total));
+  int *shift = array<int>("edges.shift", size_t(total) * 3);
+  float4 *vec = array<float4>("edges.vector", size_t(total));
+  int *rev = array<int>("edges.reverse", size_t(total));
+  if (n && total) {
+    neighbour_pass<<<(n * 32 + 255) / 256, 256, 0, stream>>>(tv, nullptr, row, sender, shift, vec);
+    reverse_edges<<<n, 128, 0, stream>>>(row, sender, shift, rev, status);
+  }
+  check(cudaGetLastError());
+  geometry = {};
+  geometry.n = n;
+  geometry.xyz = sorted;
+  geometry.elements = sz;
+  geometry.bins = sb;
+  geometry.offsets = offsets;
+  geometry.winding = sw;
+  geometry.status = status;
+  geometry.cutoff2 = cutoff * cutoff;
+  geometry.backend = selected;
+  std::copy(s.cell.begin(), s.cell.end(), geometry.h);
+  std::copy(dims, dims + 3, geometry.grid);
+  std::copy(images, images + 3, geometry.images);
+  geometry.edge_offsets = row;
+  geometry.edge_sender = sender;
+  geometry.edge_shift = shift;
+  geometry.edge_vector = vec;
+  geometry.edge_reverse = rev;
+  geometry.edge_capacity = total;
+}
+
+int Context::status_code() {
+  int status = 0;
+  check(cudaMemcpyAsync(&status, geometry.status, 4, cudaMemcpyDeviceToHost, stream));
+  check(cudaStreamSynchronize(stream));
+  return status;
+}
+
+void Context::synchronize() {
+  check(cudaGetLastError());
+  check(cudaStreamSynchronize(stream));
+  int status = status_code();
+  if (status)
+    throw Error("Model detected invalid device state (code " + std::to_string(status) + ")");
+}
+
+Result Context::finish(float *e, float *f, float *v, const float *e0_by_z) {
+  int n = geometry.n;
+  size_t out_floats = size_t(n) * 4;
+  float *ordered = array<float>("output.ordered", out_floats);
+  double *partial = array<double>("output.partial", kReduceBlocks * 10 + 16);
+  double *sums = partial + kReduceBlocks * 10;
+  if (n)
+    restore_outputs<<<kReduceBlocks, 256, 0, stream>>>(n, original_to_internal, e, f, v, e0_by_z,
+                                                       input_elements_, ordered, partial);
+  else
+    clear(partial, kReduceBlocks * 10 * sizeof(double));
+  sum_partials<<<1, 32, 0, stream>>>(partial, sums);
+  grow_pinned(pinned_, pinned_capacity_, out_floats * 4 + 256);
+  auto *host = static_cast<char *>(pinned_);
+  auto *hsums = reinterpret_cast<double *>(host);
+  auto *hstatus = reinterpret_cast<int *>(host + 80);
+  auto *hout = reinterpret_cast<float *>(host + 128);
+  check(cudaMemcpyAsync(hsums, sums, 80, cudaMemcpyDeviceToHost, stream));
+  check(cudaMemcpyAsync(hstatus, geometry.status, 4, cudaMemcpyDeviceToHost, stream));
+  if (out_floats)
+    check(cudaMemcpyAsync(hout, ordered, out_floats * 4, cudaMemcpyDeviceToHost, stream));
+  check(cudaEventRecord(stop, stream));
+  check(cudaGetLastError());
+  check(cudaStreamSynchronize(stream));
+  if (*hstatus)
+    throw Error("Model detected invalid device state (code " + std::to_string(*hstatus) + ")");
+  check(cudaEventElapsedTime(&diagnostics.device_ms, start, stop));
+  Result r;
+  r.energies.assign(hout, hout + n);
+  r.forces.assign(hout + n, hout + 4 * size_t(n));
+  for (int i = 0; i < n; ++i) {
+    if (!std::isfinite(hout[i]))
+      throw Error("Nonfinite model output");
+    for (int k = 0; k < 3; ++k)
+      if (!std::isfinite(hout[n + 3 * i + k]))
+        throw Error("Nonfinite force");
+  }
+  r.energy = hsums[0];
+  for (int k = 0; k < 9; ++k) {
+    if (!std::isfinite(hsums[1 + k]))
+      throw Error("Nonfinite virial");
+    r.virial[k] = float(hsums[1 + k]);
+  }
+  return r;
+}
+
+Result Calculator::calculate(const Structure &s) {
+  if (busy_.test_and_set(std::memory_order_acquire))
+    throw Error("Calculator is single-flight: concurrent call rejected");
+  struct Guard {
+    std::atomic_flag &b;
+    ~Guard() { b.clear(std::memory_order_release); }
+  } guard{busy_};
+  try {
+    context_.prepare(s, cutoff_, options_);
+    return evaluate();
+  } catch (...) {
+    cudaStreamSynchronize(context_.stream);
+    throw;
+  }
+}
+} // namespace lapis
