@@ -1,0 +1,172 @@
+// mace::MH1 for B200: model construction and the forward + analytical backward evaluation.
+//
+// Stage order and scaling follow the reference's MH1::evaluate (mace/src/mh1.cu:754-898):
+// embedding and ZBL, two interaction layers (up/res/skip linears, messages + density,
+// linear_1, density normalisation, gate, linear_2, symmetric contraction, product linear +
+// skip, layer-0 readout), the SiLU readout of layer 1, then the reverse pass (readout VJPs,
+// product / gate / normalisation VJPs, linear transposes, edge backward for layers 1 and 0).
+// Energies are scale (constants[6]) x readouts + shift (constants[7]) + ZBL; the per-element
+// baseline e0 is added in float64 for the total (mace/src/mh1.cu:890-896).
+#include "mace/mh1.hpp"
+#include "model.hpp"
+#include <climits>
+#include <cstdlib>
+#include <cstdio>
+
+namespace mace {
+using namespace lapis;
+
+struct MH1::Model {
+  ModelData data;
+};
+
+MH1::MH1(const std::string &archive, Options o, const std::string &head)
+    : Calculator(6, o), model_(std::make_unique<Model>()) {
+  if (!head.empty())
+    throw Error("unsupported MH1 checkpoint: head selection requires an original checkpoint; an archive already "
+                "contains one head");
+  model_->data.load(archive);
+}
+MH1::MH1(const std::string &archive, Options o) : MH1(archive, o, {}) {}
+MH1::~MH1() = default;
+size_t MH1::parameter_bytes() const { return model_->data.bytes; }
+
+namespace {
+// Opt-in per-stage timing (MACE_PROFILE_MH1=1), like the reference's StageTimer
+// (mace/src/mh1.cu:53-82): CUDA events on the model stream, printed to stderr.
+struct StageTimer {
+  cudaStream_t stream;
+  bool enabled = std::getenv("MACE_PROFILE_MH1") != nullptr;
+  std::vector<std::pair<std::string, cudaEvent_t>> events;
+  explicit StageTimer(cudaStream_t s) : stream(s) { mark("start"); }
+  void mark(const std::string &name) {
+    if (!enabled)
+      return;
+    cudaEvent_t e;
+    check(cudaEventCreate(&e));
+    events.emplace_back(name, e);
+    check(cudaEventRecord(e, stream));
+  }
+  void report() {
+    if (!enabled || events.empty())
+      return;
+    check(cudaEventSynchronize(events.back().second));
+    for (size_t k = 1; k < events.size(); ++k) {
+      float ms = 0;
+      check(cudaEventElapsedTime(&ms, events[k - 1].second, events[k].second));
+      std::fprintf(stderr, "MH1 %s: %.4f ms\n", events[k].first.c_str(), ms);
+    }
+  }
+  ~StageTimer() {
+    for (auto &e : events)
+      cudaEventDestroy(e.second);
+  }
+};
+} // namespace
+
+Result MH1::evaluate() {
+  auto &c = context_;
+  auto &m = model_->data;
+  cudaStream_t s = c.stream;
+  int n = c.geometry.n;
+  size_t E = size_t(c.geometry.edge_capacity);
+  if (n > INT_MAX / 9728)
+    throw Error("MH1 node dimensions exceed v1 int32 capacity");
+  StageTimer timer(s);
+  auto node = [&](const std::string &name, size_t width) { return c.array<float>(name, size_t(n) * width); };
+  const float *cst = m.constants;
+  int *species = c.array<int>("mh.species", n);
+  float *energy = node("mh.e", 1), *force = node("mh.f", 3), *virial = node("mh.v", 9);
+  float *x0 = node("mh.embedding", 512);
+  launch_species(s, c.geometry, m.lookup, species);
+  launch_embed(s, n, species, m.embedding, x0);
+  launch_zbl(s, c.geometry, m.constants_dev, m.zbl_radii, m.zbl_c, cst[7], energy, force, virial);
+  EdgeArrays ea{c.array<float>("mh.edge.basis", E * 10), c.array<float>("mh.edge.dbasis", E * 10),
+                c.array<float2>("mh.edge.cut", E), c.array<float>("mh.edge.Y", E * 16)};
+  int *pair = c.array<int>("mh.edge.pair", E);
+  launch_edge_geometry(s, c.geometry, species, m.constants_dev, m.radii, m.bessel, ea, pair);
+  timer.mark("embedding/ZBL/geometry");
+  RadialOut ro[2];
+  float *up[2], *rho[2], *raw[2], *pre[2], *pin[2], *hidden[2];
+  float *res = node("mh.t.res", 9728), *skip = node("mh.t.skip", 2048), *msg = node("mh.t.msg", 5120),
+        *gate = node("mh.t.gate", 8192), *poly = node("mh.t.poly", 2048), *node_e = node("mh.t.energy", 1);
+  const float *input = x0;
+  for (int k = 0; k < 2; ++k) {
+    const Layer &l = m.layers[k];
+    std::string p = "mh.l" + std::to_string(k);
+    up[k] = node(p + ".up", l.in_comp * 128);
+    rho[k] = node(p + ".rho", 1);
+    raw[k] = node(p + ".raw", 9728);
+    pre[k] = node(p + ".pre", 9728);
+    pin[k] = node(p + ".pin", 8192);
+    hidden[k] = node(p + ".hidden", k ? 512 : 2048);
+    ro[k] = RadialOut{c.array<float>(p + ".h", E * 64), c.array<float>(p + ".dh", E * 64),
+                      c.array<float2>(p + ".den", E)};
+    linear(s, n, l.up, input, up[k]);
+    linear(s, n, l.res, up[k], res);
+    linear(s, n, l.skip, input, skip);
+    launch_radial(s, c.geometry, l, pair, ea, ro[k]);
+    timer.mark("forward" + std::to_string(k) + ".linears/radial");
+    launch_message_forward(s, k, c.geometry, l, ea, ro[k], up[k], msg, rho[k]);
+    timer.mark("forward" + std::to_string(k) + ".messages");
+    linear(s, n, l.one, msg, raw[k]);
+    launch_normalize_gate(s, n, raw[k], res, rho[k], l.alpha, l.beta, cst[11], cst[12], pre[k], gate);
+    linear(s, n, l.two, gate, pin[k]);
+    launch_product(s, n, l, pin[k], poly);
+    linear(s, n, l.plin, poly, hidden[k]);
+    launch_add(s, size_t(n) * (k ? 512 : 2048), skip, hidden[k], 1.f);
+    if (k == 0) {
+      linear(s, n, m.read0, hidden[0], node_e);
+      launch_add(s, n, node_e, energy, cst[6]);
+    }
+    input = hidden[k];
+    timer.mark("forward" + std::to_string(k) + ".node");
+  }
+  float *rpre = node("mh.r.pre", 16), *rhid = node("mh.r.hidden", 16), *rgrad = node("mh.r.grad", 16),
+        *rdpre = node("mh.r.dpre", 16);
+  linear(s, n, m.read1up, hidden[1], rpre);
+  launch_readout_act(s, n * 16, rpre, nullptr, rhid, cst[13], false);
+  linear(s, n, m.read1down, rhid, node_e);
+  launch_add(s, n, node_e, energy, cst[6]);
+  // ---- analytical backward ----
+  float *one = node_e;
+  float *hgrad1 = node("mh.b.hgrad1", 512), *hgrad0 = node("mh.b.hgrad0", 2048);
+  float *pgrad = node("mh.b.poly", 2048), *pingrad = node("mh.b.pin", 8192), *gategrad = gate;
+  float *pregrad = res, *rawgrad = node("mh.b.raw", 9728), *rhograd = node("mh.b.rho", 1);
+  float *msggrad = msg, *upgrad = node("mh.b.up", 512);
+  float4 *edge_force = c.array<float4>("mh.edge.force", E);
+  launch_fill(s, n, one, cst[6]);
+  linear(s, n, m.read1down, one, rgrad, true);
+  launch_readout_act(s, n * 16, rpre, rgrad, rdpre, cst[13], true);
+  linear(s, n, m.read1up, rdpre, hgrad1, true);
+  timer.mark("readouts");
+  float *hgrad = hgrad1;
+  for (int k = 1; k >= 0; --k) {
+    const Layer &l = m.layers[k];
+    if (k == 0)
+      linear(s, n, m.read0, one, hgrad, true, true);
+    linear(s, n, l.plin, hgrad, pgrad, true);
+    launch_product_backward(s, n, l, pin[k], pgrad, pingrad);
+    linear(s, n, l.two, pingrad, gategrad, true);
+    launch_gate_norm_backward(s, n, pre[k], raw[k], rho[k], gategrad, l.alpha, l.beta, cst[11], cst[12], pregrad,
+                              rawgrad, rhograd);
+    linear(s, n, l.one, rawgrad, msggrad, true);
+    if (k == 1)
+      linear(s, n, l.res, pregrad, upgrad, true);
+    timer.mark("backward" + std::to_string(k) + ".node");
+    launch_message_backward(s, k, c.geometry, l, ea, ro[k], up[k], msggrad, rhograd, upgrad, edge_force, k == 0);
+    timer.mark("backward" + std::to_string(k) + ".edges");
+    if (k == 1) {
+      linear(s, n, l.skip, hgrad, hgrad0, true);
+      linear(s, n, l.up, upgrad, hgrad0, true, true);
+      hgrad = hgrad0;
+    }
+  }
+  launch_force_gather(s, c.geometry, edge_force, force, virial);
+  check(cudaGetLastError());
+  timer.mark("forces");
+  auto result = c.finish(energy, force, virial, m.e0_z);
+  timer.report();
+  return result;
+}
+} // namespace mace

@@ -1,0 +1,111 @@
+// MH1 parameter layout on the device and the kernel entry points of the B200 build.
+//
+// Node tensors use the reference's [irrep block][component][node][channel] layout
+// (mace/src/mh1.cu:83-84): every equivariant linear is then, per path and component, a
+// row-major GEMM with nodes as rows.  Edge tensors are indexed by the CSR edge id of the
+// Lapis runtime (receiver-major).
+#pragma once
+#include "lapis/runtime.hpp"
+#include "tp_table.h"
+#include <string>
+#include <vector>
+
+namespace mace {
+
+struct LinearPath {
+  int in_offset, out_offset, in_mul, out_mul, dim, weight_offset;
+};
+struct Linear {
+  int input = 0, output = 0;
+  std::vector<LinearPath> paths;
+  const float *weight = nullptr; // device, [in_mul][out_mul] per path
+};
+// Radial MLP weights, transposed at load for coalesced per-unit access.
+struct Radial {
+  const float *source, *target; // [species][64]
+  const float *input_t;         // [10][64]
+  const float *bias0;           // [64]
+  const float *weight_t[3];     // [64 in][64 out]; entry 0 unused
+  const float *bias[3], *gamma[3], *beta[3];
+  const float *out_t;           // [64][outputs]
+  const float *out_b;           // [outputs]
+  int depth, outputs;
+};
+struct PolyTerm {
+  int output, degree, a, b, c;
+};
+struct TPValues {
+  float v[128]; // coupling values in the compiled term order (tp_table.h)
+};
+struct Layer {
+  Linear up, res, one, two, skip, plin;
+  Radial radial, density;
+  float alpha, beta;
+  TPValues tp;
+  const PolyTerm *poly; // device [npoly]
+  const float *pcoef;   // device [npoly][512]
+  int npoly, pouts, paths, in_comp, out_comp;
+};
+
+struct Device {
+  std::vector<void *> allocations;
+  ~Device();
+  float *upload(const void *data, size_t bytes);
+};
+
+struct ModelData {
+  Device device;
+  Layer layers[2];
+  Linear read0, read1up, read1down;
+  float constants[14];
+  const float *constants_dev, *embedding, *bessel, *radii, *zbl_radii, *zbl_c;
+  const int *lookup;  // [119] atomic number -> species index or -1
+  const float *e0_z;  // [119] baseline energy by atomic number
+  size_t bytes = 0;
+  int species = 0;
+  void load(const std::string &path);
+};
+
+// ---- kernels (edge_kernels.cu / node_kernels.cu) ----
+struct EdgeArrays {
+  float *basis, *dbasis; // [E][10]
+  float2 *cut;           // [E] (cut, dcut)
+  float *Y;              // [E][16]
+};
+struct RadialOut {
+  float *h, *dh;        // [E][64]
+  float2 *density;      // [E] (value, d/dr)
+};
+
+void launch_species(cudaStream_t, const lapis::DeviceGeometry &, const int *lookup, int *species);
+void launch_embed(cudaStream_t, int n, const int *species, const float *embedding, float *x);
+void launch_zbl(cudaStream_t, const lapis::DeviceGeometry &, const float *constants, const float *radii,
+                const float *coeff, float shift, float *energy, float *force, float *virial);
+// pair[e] = sender species | receiver species << 16 (written by launch_edge_geometry).
+void launch_edge_geometry(cudaStream_t, const lapis::DeviceGeometry &, const int *species, const float *constants,
+                          const float *radii, const float *bessel, EdgeArrays, int *pair);
+void launch_radial(cudaStream_t, const lapis::DeviceGeometry &, const Layer &, const int *pair, EdgeArrays,
+                   RadialOut);
+void launch_message_forward(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &, EdgeArrays,
+                            RadialOut, const float *up, float *message, float *density);
+void launch_message_backward(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &,
+                             EdgeArrays, RadialOut, const float *up, const float *message_grad,
+                             const float *density_grad, float *up_grad, float4 *edge_force, bool accumulate);
+void launch_force_gather(cudaStream_t, const lapis::DeviceGeometry &, const float4 *edge_force, float *force,
+                         float *virial);
+
+void linear(cudaStream_t, int n, const Linear &, const float *x, float *y, bool backward = false,
+            bool add = false);
+void launch_normalize_gate(cudaStream_t, int n, const float *raw, const float *res, const float *density,
+                           float alpha, float beta, float scalar_scale, float gate_scale, float *pre,
+                           float *gate);
+void launch_gate_norm_backward(cudaStream_t, int n, const float *pre, const float *raw, const float *density,
+                               const float *gate_grad, float alpha, float beta, float scalar_scale,
+                               float gate_scale, float *pre_grad, float *raw_grad, float *density_grad);
+void launch_product(cudaStream_t, int n, const Layer &, const float *x, float *y);
+void launch_product_backward(cudaStream_t, int n, const Layer &, const float *x, const float *grad, float *xg);
+void launch_add(cudaStream_t, size_t count, const float *a, float *b, float scale);
+void launch_fill(cudaStream_t, size_t count, float *a, float value);
+void launch_readout_act(cudaStream_t, int count, const float *x, const float *grad, float *y, float scale,
+                        bool backward);
+} // namespace mace

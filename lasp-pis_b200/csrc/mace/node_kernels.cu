@@ -1,0 +1,318 @@
+// MH1 node kernels for B200: equivariant linears, normalisation + gate, the symmetric
+// contraction (cubic product basis) and small elementwise ops.
+//
+// Reference semantics (LipidL/LASP-PIS mace/src/mh1.cu):
+//   linear()                  85-106   per path and component Y (+)= X W, or X_grad += Y_grad W^T
+//   embed_kernel              107-120  species embedding (unknown element -> status 2)
+//   normalize_kernel          121-128  pre = raw / (alpha + beta * density) + res
+//   gate_kernel<false/true>   129-159  SiLU scalars, sigmoid-gated l = 1..3 blocks, and the VJP
+//   norm_backward             160-176  VJP of the density normalisation
+//   product_kernel            177-214  sparse cubic polynomial per channel and its VJP
+//   read_act                  225-235  readout SiLU and its VJP
+// Normalisation and gating are fused into one pass (forward) and one pass with the
+// normalisation VJP (backward); the reference launches them separately.
+#include "model.hpp"
+
+namespace mace {
+namespace {
+__device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + expf(-x)); }
+
+// ---------------- FP32 GEMM: C[z] += A[z] * B  (B optionally read transposed) ----------------
+constexpr int BM = 64, BN = 64, BK = 16;
+template <bool TransB>
+__global__ void __launch_bounds__(256) gemm_kernel(int M, int N, int K, const float *__restrict__ A, int lda,
+                                                   long long sA, const float *__restrict__ B, int ldb,
+                                                   float *__restrict__ C, int ldc, long long sC) {
+  __shared__ __align__(16) float As[BK][BM + 4];
+  __shared__ __align__(16) float Bs[BK][BN + 4];
+  A += blockIdx.z * sA;
+  C += blockIdx.z * sC;
+  int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += BK) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      int idx = tid + 256 * q, r = idx >> 4, kk = idx & 15, gm = m0 + r, gk = k0 + kk;
+      As[kk][r] = (gm < M && gk < K) ? A[size_t(gm) * lda + gk] : 0.f;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      int idx = tid + 256 * q;
+      if (!TransB) {
+        int kk = idx >> 6, nn = idx & 63, gk = k0 + kk, gn = n0 + nn;
+        Bs[kk][nn] = (gk < K && gn < N) ? B[size_t(gk) * ldb + gn] : 0.f;
+      } else {
+        int nn = idx >> 4, kk = idx & 15, gk = k0 + kk, gn = n0 + nn;
+        Bs[kk][nn] = (gk < K && gn < N) ? B[size_t(gn) * ldb + gk] : 0.f;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float4 a = *reinterpret_cast<const float4 *>(&As[kk][ty * 4]);
+      float4 b = *reinterpret_cast<const float4 *>(&Bs[kk][tx * 4]);
+      float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          acc[r][c] = fmaf(av[r], bv[c], acc[r][c]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    int gm = m0 + ty * 4 + r;
+    if (gm >= M)
+      continue;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      int gn = n0 + tx * 4 + c;
+      if (gn < N)
+        C[size_t(gm) * ldc + gn] += acc[r][c];
+    }
+  }
+}
+
+__global__ void species_kernel(lapis::DeviceGeometry g, const int *lookup, int *species) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= g.n)
+    return;
+  int s = lookup[g.elements[i]];
+  if (s < 0) {
+    atomicCAS(g.status, 0, 2);
+    s = 0;
+  }
+  species[i] = s;
+}
+
+__global__ void embed_kernel(int n, const int *species, const float *embedding, float *x) {
+  size_t q = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (q >= size_t(n) * 512)
+    return;
+  int i = int(q / 512), c = int(q % 512);
+  x[q] = embedding[species[i] * 512 + c];
+}
+
+// One thread per (node, channel < 512): the 4 scalar groups and the 15 gated components.
+__global__ void normalize_gate_kernel(int n, const float *raw, const float *res, const float *rho, float alpha,
+                                      float beta, float cs, float cg, float *pre, float *gate) {
+  int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= n * 512)
+    return;
+  int i = q / 512, c = q % 512;
+  float den = alpha + beta * rho[i];
+  float u[4];
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    size_t k = size_t(i) * 2048 + g * 512 + c;
+    u[g] = raw[k] / den + res[k];
+    pre[k] = u[g];
+  }
+  gate[q] = cs * u[0] * sigm(u[0]);
+#pragma unroll
+  for (int l = 1; l <= 3; ++l) {
+    float gl = sigm(u[l]);
+    for (int m = l * l; m < (l + 1) * (l + 1); ++m) {
+      size_t k = size_t(n) * 2048 + (size_t(m - 1) * n + i) * 512 + c;
+      float p = raw[k] / den + res[k];
+      pre[k] = p;
+      gate[(size_t(m) * n + i) * 512 + c] = p * cg * gl;
+    }
+  }
+}
+
+// CTA per node: gate VJP into pre_grad, normalisation VJP into raw_grad and density_grad.
+__global__ void __launch_bounds__(128) gate_norm_backward_kernel(int n, const float *pre, const float *raw,
+                                                                 const float *rho, const float *gg, float alpha,
+                                                                 float beta, float cs, float cgt, float *pg,
+                                                                 float *rg, float *rho_grad) {
+  __shared__ float red[4];
+  int i = blockIdx.x, t = threadIdx.x;
+  float den = alpha + beta * rho[i], s = 0.f;
+  for (int c = t; c < 512; c += 128) {
+    size_t k0 = size_t(i) * 2048 + c;
+    float u = pre[k0], sg = sigm(u);
+    float g0 = gg[size_t(i) * 512 + c] * cs * sg * (1.f + u * (1.f - sg));
+    pg[k0] = g0;
+    rg[k0] = g0 / den;
+    s -= g0 * raw[k0] * beta / (den * den);
+#pragma unroll
+    for (int l = 1; l <= 3; ++l) {
+      size_t gi = size_t(i) * 2048 + l * 512 + c;
+      float gl = sigm(pre[gi]), dg = 0.f;
+      for (int m = l * l; m < (l + 1) * (l + 1); ++m) {
+        size_t src = size_t(n) * 2048 + (size_t(m - 1) * n + i) * 512 + c;
+        float go = gg[(size_t(m) * n + i) * 512 + c];
+        float v = go * cgt * gl;
+        pg[src] = v;
+        rg[src] = v / den;
+        s -= v * raw[src] * beta / (den * den);
+        dg += go * pre[src] * cgt * gl * (1.f - gl);
+      }
+      pg[gi] = dg;
+      rg[gi] = dg / den;
+      s -= dg * raw[gi] * beta / (den * den);
+    }
+  }
+#pragma unroll
+  for (int step = 16; step; step >>= 1)
+    s += __shfl_xor_sync(0xffffffffu, s, step);
+  if ((t & 31) == 0)
+    red[t >> 5] = s;
+  __syncthreads();
+  if (t == 0)
+    rho_grad[i] = red[0] + red[1] + red[2] + red[3];
+}
+
+// Symmetric contraction: y[out][c] = sum_t coef[t][c] x[a][c] x[b][c] x[c'][c] (degree <= 3).
+__global__ void __launch_bounds__(128) product_kernel(int n, const PolyTerm *terms, const float *coef, int count,
+                                                      int outputs, const float *x, float *y) {
+  __shared__ float v[16][128];
+  int t = threadIdx.x;
+  size_t q = size_t(blockIdx.x) * 128 + t;
+  int i = int(q / 512), c = int(q % 512);
+#pragma unroll
+  for (int m = 0; m < 16; ++m)
+    v[m][t] = x[(size_t(m) * n + i) * 512 + c];
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k = 0; k < count; ++k) {
+    PolyTerm tm = terms[k];
+    float w = coef[size_t(k) * 512 + c];
+    float val = w * v[tm.a][t];
+    if (tm.degree >= 2)
+      val *= v[tm.b][t];
+    if (tm.degree >= 3)
+      val *= v[tm.c][t];
+    if (tm.output == 0)
+      acc[0] += val;
+    else if (tm.output == 1)
+      acc[1] += val;
+    else if (tm.output == 2)
+      acc[2] += val;
+    else
+      acc[3] += val;
+  }
+  for (int o = 0; o < outputs; ++o)
+    y[(size_t(o) * n + i) * 512 + c] = acc[o];
+}
+
+__global__ void __launch_bounds__(128) product_backward_kernel(int n, const PolyTerm *terms, const float *coef,
+                                                               int count, int outputs, const float *x,
+                                                               const float *grad, float *xg) {
+  __shared__ float v[16][128], g[16][128];
+  int t = threadIdx.x;
+  size_t q = size_t(blockIdx.x) * 128 + t;
+  int i = int(q / 512), c = int(q % 512);
+#pragma unroll
+  for (int m = 0; m < 16; ++m) {
+    v[m][t] = x[(size_t(m) * n + i) * 512 + c];
+    g[m][t] = 0.f;
+  }
+  float G[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int o = 0; o < outputs; ++o)
+    G[o] = grad[(size_t(o) * n + i) * 512 + c];
+  for (int k = 0; k < count; ++k) {
+    PolyTerm tm = terms[k];
+    float gw = coef[size_t(k) * 512 + c] *
+               (tm.output == 0 ? G[0] : tm.output == 1 ? G[1] : tm.output == 2 ? G[2] : G[3]);
+    float a = v[tm.a][t], b = tm.degree >= 2 ? v[tm.b][t] : 1.f, d = tm.degree >= 3 ? v[tm.c][t] : 1.f;
+    g[tm.a][t] += gw * b * d;
+    if (tm.degree >= 2)
+      g[tm.b][t] += gw * a * d;
+    if (tm.degree >= 3)
+      g[tm.c][t] += gw * a * b;
+  }
+#pragma unroll
+  for (int m = 0; m < 16; ++m)
+    xg[(size_t(m) * n + i) * 512 + c] = g[m][t];
+}
+
+__global__ void add_kernel(size_t count, const float *a, float *b, float scale) {
+  size_t k = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (k < count)
+    b[k] += scale * a[k];
+}
+__global__ void fill_kernel(size_t count, float *a, float value) {
+  size_t k = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (k < count)
+    a[k] = value;
+}
+__global__ void readout_act_kernel(int count, const float *x, const float *grad, float *y, float scale,
+                                   bool backward) {
+  int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= count)
+    return;
+  float s = sigm(x[k]);
+  y[k] = backward ? grad[k] * scale * s * (1.f + x[k] * (1.f - s)) : scale * x[k] * s;
+}
+
+unsigned blocks_for(size_t count, int threads) { return unsigned((count + threads - 1) / threads); }
+} // namespace
+
+void launch_species(cudaStream_t s, const lapis::DeviceGeometry &g, const int *lookup, int *species) {
+  if (g.n)
+    species_kernel<<<blocks_for(g.n, 256), 256, 0, s>>>(g, lookup, species);
+}
+void launch_embed(cudaStream_t s, int n, const int *species, const float *embedding, float *x) {
+  if (n)
+    embed_kernel<<<blocks_for(size_t(n) * 512, 256), 256, 0, s>>>(n, species, embedding, x);
+}
+
+void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bool backward, bool add) {
+  if (!n)
+    return;
+  if (!add)
+    lapis::check(cudaMemsetAsync(y, 0, size_t(n) * (backward ? l.input : l.output) * 4, s));
+  for (const auto &p : l.paths) {
+    const float *w = l.weight + p.weight_offset;
+    if (!backward) {
+      dim3 grid((p.out_mul + BN - 1) / BN, (n + BM - 1) / BM, p.dim);
+      gemm_kernel<false><<<grid, 256, 0, s>>>(n, p.out_mul, p.in_mul, x + size_t(p.in_offset) * n, p.in_mul,
+                                              (long long)n * p.in_mul, w, p.out_mul, y + size_t(p.out_offset) * n,
+                                              p.out_mul, (long long)n * p.out_mul);
+    } else {
+      dim3 grid((p.in_mul + BN - 1) / BN, (n + BM - 1) / BM, p.dim);
+      gemm_kernel<true><<<grid, 256, 0, s>>>(n, p.in_mul, p.out_mul, x + size_t(p.out_offset) * n, p.out_mul,
+                                             (long long)n * p.out_mul, w, p.out_mul, y + size_t(p.in_offset) * n,
+                                             p.in_mul, (long long)n * p.in_mul);
+    }
+  }
+}
+
+void launch_normalize_gate(cudaStream_t s, int n, const float *raw, const float *res, const float *density,
+                           float alpha, float beta, float scalar_scale, float gate_scale, float *pre, float *gate) {
+  if (n)
+    normalize_gate_kernel<<<blocks_for(size_t(n) * 512, 256), 256, 0, s>>>(n, raw, res, density, alpha, beta,
+                                                                           scalar_scale, gate_scale, pre, gate);
+}
+void launch_gate_norm_backward(cudaStream_t s, int n, const float *pre, const float *raw, const float *density,
+                               const float *gate_grad, float alpha, float beta, float scalar_scale, float gate_scale,
+                               float *pre_grad, float *raw_grad, float *density_grad) {
+  if (n)
+    gate_norm_backward_kernel<<<n, 128, 0, s>>>(n, pre, raw, density, gate_grad, alpha, beta, scalar_scale,
+                                                gate_scale, pre_grad, raw_grad, density_grad);
+}
+void launch_product(cudaStream_t s, int n, const Layer &l, const float *x, float *y) {
+  if (n)
+    product_kernel<<<n * 4, 128, 0, s>>>(n, l.poly, l.pcoef, l.npoly, l.pouts, x, y);
+}
+void launch_product_backward(cudaStream_t s, int n, const Layer &l, const float *x, const float *grad, float *xg) {
+  if (n)
+    product_backward_kernel<<<n * 4, 128, 0, s>>>(n, l.poly, l.pcoef, l.npoly, l.pouts, x, grad, xg);
+}
+void launch_add(cudaStream_t s, size_t count, const float *a, float *b, float scale) {
+  if (count)
+    add_kernel<<<blocks_for(count, 256), 256, 0, s>>>(count, a, b, scale);
+}
+void launch_fill(cudaStream_t s, size_t count, float *a, float value) {
+  if (count)
+    fill_kernel<<<blocks_for(count, 256), 256, 0, s>>>(count, a, value);
+}
+void launch_readout_act(cudaStream_t s, int count, const float *x, const float *grad, float *y, float scale,
+                        bool backward) {
+  if (count)
+    readout_act_kernel<<<blocks_for(count, 256), 256, 0, s>>>(count, x, grad, y, scale, backward);
+}
+} // namespace mace

@@ -1,0 +1,35 @@
+"""ASE calculator over the C ABI (same surface as the reference's MH1Calculator,
+mace/python/mace_inference/calculator.py:10-94): energy, energies, forces and
+stress = -virial / volume in Voigt order; ``evaluate`` bypasses the ASE cache."""
+import numpy as np
+from ase.calculators.calculator import Calculator, all_changes
+from ase.stress import full_3x3_to_voigt_6_stress
+
+from .native import NativeMH1
+
+
+class MH1Calculator(Calculator):
+    implemented_properties = ["energy", "energies", "forces", "stress"]
+
+    def __init__(self, model, *, backend="auto", library=None, head=None, **kwargs):
+        super().__init__(**kwargs)
+        self.native = NativeMH1(model, backend=backend, library=library, head=head)
+
+    def close(self):
+        if getattr(self, "native", None):
+            self.native.close()
+
+    def evaluate(self, atoms):
+        if not np.all(atoms.pbc):
+            raise ValueError("v1 requires three periodic axes")
+        r = self.native.calculate(atoms.positions, atoms.numbers, atoms.cell.array)
+        r["stress"] = full_3x3_to_voigt_6_stress(-r["virial"] / atoms.get_volume())
+        return r
+
+    def calculate(self, atoms=None, properties=("energy",), system_changes=all_changes):
+        super().calculate(atoms, properties, system_changes)
+        self.results = self.evaluate(self.atoms)
+
+    @property
+    def diagnostics(self):
+        return self.native.diagnostics

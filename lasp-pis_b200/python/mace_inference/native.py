@@ -1,0 +1,124 @@
+"""ctypes binding of the C ABI (include/mace/c_api.h); raises RuntimeError on failure."""
+from __future__ import annotations
+
+import ctypes as ct
+import json
+
+import numpy as np
+
+from .library import library_path
+
+_libs: dict[str, ct.CDLL] = {}
+
+
+def load(path=None) -> ct.CDLL:
+    path = str(path or library_path())
+    if path in _libs:
+        return _libs[path]
+    lib = ct.CDLL(path)
+    lib.mace_create_mh1.argtypes = [ct.c_char_p, ct.c_int]
+    lib.mace_create_mh1.restype = ct.c_void_p
+    lib.mace_create_mh1_head.argtypes = [ct.c_char_p, ct.c_int, ct.c_char_p]
+    lib.mace_create_mh1_head.restype = ct.c_void_p
+    lib.mace_create_mh1_device.argtypes = [ct.c_char_p, ct.c_int, ct.c_int]
+    lib.mace_create_mh1_device.restype = ct.c_void_p
+    lib.mace_destroy.argtypes = [ct.c_void_p]
+    lib.mace_destroy.restype = None
+    lib.mace_last_error.restype = ct.c_char_p
+    lib.mace_calculate.argtypes = [ct.c_void_p, ct.c_int] + [ct.c_void_p] * 7
+    lib.mace_calculate.restype = ct.c_int
+    lib.mace_calculate_device.argtypes = [ct.c_void_p, ct.c_int] + [ct.c_void_p] * 7
+    lib.mace_calculate_device.restype = ct.c_int
+    lib.mace_diagnostics.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_size_t]
+    lib.mace_diagnostics.restype = ct.c_int
+    lib.mace_last_edges.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_longlong]
+    lib.mace_last_edges.restype = ct.c_longlong
+    lib.lapis_neighbor_edges.argtypes = [ct.c_int, ct.c_void_p, ct.c_void_p, ct.c_float, ct.c_int, ct.c_longlong,
+                                         ct.c_void_p, ct.c_longlong]
+    lib.lapis_neighbor_edges.restype = ct.c_longlong
+    _libs[path] = lib
+    return lib
+
+
+def _error(lib) -> str:
+    return lib.mace_last_error().decode()
+
+
+def neighbor_edges(xyz, cell, cutoff=6.0, backend=0, grid_bytes=0, library=None):
+    """Canonical directed edges int32 [E, 5] (receiver, sender, sx, sy, sz) of the Lapis list."""
+    lib = load(library)
+    xyz = np.ascontiguousarray(xyz, np.float32).reshape(-1, 3)
+    cell = np.ascontiguousarray(cell, np.float32).reshape(3, 3)
+    count = lib.lapis_neighbor_edges(len(xyz), xyz.ctypes.data, cell.ctypes.data, cutoff, backend, grid_bytes,
+                                     None, 0)
+    if count < 0:
+        raise RuntimeError(_error(lib))
+    out = np.zeros((max(count, 1), 5), np.int32)
+    lib.lapis_neighbor_edges(len(xyz), xyz.ctypes.data, cell.ctypes.data, cutoff, backend, grid_bytes,
+                             out.ctypes.data, count)
+    return out[:count]
+
+
+class NativeMH1:
+    """One MH1 handle: ``calculate(xyz, z, cell)`` -> energy, energies, forces, virial."""
+
+    def __init__(self, archive, backend=0, library=None, device=None, head=None):
+        self.lib = load(library)
+        b = {"auto": 0, "brute": 1, "cell": 2}.get(backend, backend)
+        if device is not None:
+            self.handle = self.lib.mace_create_mh1_device(str(archive).encode(), b, device)
+        elif head is not None:
+            self.handle = self.lib.mace_create_mh1_head(str(archive).encode(), b, head.encode())
+        else:
+            self.handle = self.lib.mace_create_mh1(str(archive).encode(), b)
+        if not self.handle:
+            raise RuntimeError(_error(self.lib))
+
+    def _call(self, fn, n, xyz_ptr, z_ptr, cell):
+        cell = np.ascontiguousarray(cell, np.float32).reshape(3, 3)
+        energy = np.zeros(1, np.float64)
+        atomic = np.zeros(n, np.float32)
+        forces = np.zeros((n, 3), np.float32)
+        virial = np.zeros((3, 3), np.float32)
+        if fn(self.handle, n, xyz_ptr, z_ptr, cell.ctypes.data, energy.ctypes.data, atomic.ctypes.data,
+              forces.ctypes.data, virial.ctypes.data):
+            raise RuntimeError(_error(self.lib))
+        return dict(energy=float(energy[0]), energies=atomic, forces=forces, virial=virial)
+
+    def calculate(self, xyz, z, cell):
+        xyz = np.ascontiguousarray(xyz, np.float32).reshape(-1, 3)
+        z = np.ascontiguousarray(z, np.int32)
+        return self._call(self.lib.mace_calculate, len(z), xyz.ctypes.data, z.ctypes.data, cell)
+
+    def calculate_device(self, n, xyz_ptr, z_ptr, cell):
+        """Device-resident inputs (raw device pointers on the handle's GPU)."""
+        return self._call(self.lib.mace_calculate_device, n, xyz_ptr, z_ptr, cell)
+
+    def last_edges(self):
+        count = self.lib.mace_last_edges(self.handle, None, 0)
+        if count < 0:
+            raise RuntimeError(_error(self.lib))
+        out = np.zeros((max(count, 1), 5), np.int32)
+        self.lib.mace_last_edges(self.handle, out.ctypes.data, count)
+        return out[:count]
+
+    @property
+    def diagnostics(self):
+        buf = ct.create_string_buffer(1 << 16)
+        if self.lib.mace_diagnostics(self.handle, buf, len(buf)):
+            raise RuntimeError(_error(self.lib))
+        return json.loads(buf.value)
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.mace_destroy(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *args):
+        self.close()
+
+    def __del__(self):
+        self.close()

@@ -29,3 +29,15 @@ def oracle_model(archive_path):
     import oracle
     oracle.build()
     return oracle.Oracle(archive_path)
+
+
+LIB = ROOT / "lasp-pis_b200" / "lib" / "libmace.so"
+
+
+@pytest.fixture(scope="session")
+def library():
+    """Build (if needed) and return the path of the B200 libmace.so."""
+    import subprocess
+    if not LIB.exists():
+        subprocess.run(["make", "-s", "-C", str(ROOT / "lasp-pis_b200"), "-j8"], check=True)
+    return LIB

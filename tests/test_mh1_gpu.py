@@ -1,0 +1,157 @@
+"""GPU parity of the B200 engine, through the C ABI.
+
+Edges: the canonical (receiver, sender, shift) multiset must equal the reference's own
+Lapis traversal bit for bit (sha256 of the sorted int32 list recorded on a B200 by
+tests/golden/make_ref_golden.py) and the float64 oracle's.
+
+Model outputs are compared with the float64 oracle (oracle/) and with the reference CUDA
+build's outputs on identical inputs and weights (tests/golden/ref_*.npz).  Tolerances:
+energy 1e-6 relative; forces 1e-5 eV/A relative to max(1, max|F|); per-atom energies 5e-5 eV;
+virial 1e-6 relative to max|W| (the virial at 1e-5 eV absolute is below the reference's own
+run-to-run spread for these sizes).  Against the reference the force bound is the
+reference's own distance to the oracle plus ours.
+"""
+import hashlib
+import json
+import subprocess
+
+import numpy as np
+import pytest
+
+import oracle as O
+import scenarios
+from conftest import DATA, GOLDEN, ROOT
+from lasp_b200 import structures
+
+pytestmark = pytest.mark.gpu
+SUMMARY = json.loads((GOLDEN / "ref_summary.json").read_text())
+
+
+def digest(edges):
+    return hashlib.sha256(np.ascontiguousarray(edges, np.int32).tobytes()).hexdigest()
+
+
+@pytest.fixture(scope="module")
+def engine(library, archive_path):
+    from mace_inference import NativeMH1
+    models = {b: NativeMH1(archive_path, backend=b, library=library) for b in (0, 1, 2)}
+    yield models
+    for m in models.values():
+        m.close()
+
+
+@pytest.mark.parametrize("case", list(scenarios.framework_scenarios()), ids=lambda c: c[0])
+def test_neighbor_edges_match_reference(library, case):
+    from mace_inference import neighbor_edges
+    name, xyz, cell, cutoff, grid, backends = case
+    for b in backends:
+        e = neighbor_edges(xyz, cell, cutoff, b, grid, library=library)
+        ref = SUMMARY["edges"][name][str(b)]
+        assert len(e) == ref["count"], (name, b)
+        assert digest(e) == ref["sha256"], (name, b)
+
+
+def test_neighbor_errors(library):
+    from mace_inference import neighbor_edges
+    with pytest.raises(RuntimeError, match="Singular"):
+        neighbor_edges(np.zeros((2, 3)), np.zeros((3, 3)), 2.5, library=library)
+    with pytest.raises(RuntimeError, match="CellList"):
+        neighbor_edges(np.zeros((2, 3)), np.eye(3), 2.5, 2, library=library)
+
+
+def check_close(r, ref, fscale=1.0):
+    assert abs(r["energy"] - ref["energy"]) <= 1e-6 * abs(ref["energy"]), (r["energy"], ref["energy"])
+    fmax = max(1.0, float(np.abs(ref["forces"]).max()))
+    ferr = float(np.abs(r["forces"] - ref["forces"]).max())
+    assert ferr <= 1e-5 * fmax * fscale, ferr
+    assert float(np.abs(r["energies"] - ref["energies"]).max()) <= 5e-5
+    wmax = float(np.abs(ref["virial"]).max())
+    assert float(np.abs(r["virial"] - ref["virial"]).max()) <= 1e-6 * wmax * fscale
+
+
+@pytest.mark.parametrize("name", ["C1", "C2", "C3"])
+def test_model_edges_match_reference(engine, name):
+    s = structures.load(name, DATA)
+    engine[0].calculate(s.positions, s.numbers, s.cell)
+    e = engine[0].last_edges()
+    ref = SUMMARY["configs"][name]["edges_1"]
+    assert len(e) == ref["count"] and digest(e) == ref["sha256"]
+
+
+@pytest.mark.parametrize("name", ["C1", "C2"])
+def test_matches_oracle(engine, oracle_model, name):
+    s = structures.load(name, DATA)
+    ref = oracle_model.calculate(s.positions, s.numbers, s.cell)
+    for b in (0, 1, 2):
+        check_close(engine[b].calculate(s.positions, s.numbers, s.cell), ref)
+
+
+@pytest.mark.parametrize("name", ["C1", "C2", "C3"])
+def test_matches_reference_cuda(engine, name):
+    s = structures.load(name, DATA)
+    g = dict(np.load(GOLDEN / f"ref_{name}.npz"))
+    r = engine[0].calculate(s.positions, s.numbers, s.cell)
+    check_close(r, g, fscale=3.0)
+
+
+def test_native_behaviour(engine):
+    """Backends agree, permutation, empty structure, error recovery (mace/tests/native.py:41-72)."""
+    xyz, z, cell = scenarios.native_case()
+    base = engine[1].calculate(xyz, z, cell)
+    g = np.load(GOLDEN / "ref_native.npz")
+    assert abs(base["energy"] - float(g["energy"])) <= 1e-6 * abs(float(g["energy"]))
+    assert np.abs(base["forces"] - g["forces"]).max() <= 1e-5
+    for b in (0, 2):
+        r = engine[b].calculate(xyz, z, cell)
+        for k in r:
+            np.testing.assert_allclose(r[k], base[k], atol=2e-4, rtol=2e-5)
+    order = np.array([2, 0, 3, 1])
+    p = engine[0].calculate(xyz[order], z[order], cell)
+    np.testing.assert_allclose(p["forces"], base["forces"][order], atol=2e-4, rtol=2e-5)
+    assert engine[0].calculate(np.zeros((0, 3)), np.zeros(0, np.int32), cell)["energy"] == 0
+    with pytest.raises(RuntimeError, match="Singular"):
+        engine[0].calculate(xyz, z, np.zeros((3, 3)))
+    with pytest.raises(RuntimeError, match="code 2"):
+        engine[0].calculate(xyz, np.array([14, 6, 8, 99], np.int32), cell)
+    with pytest.raises(RuntimeError, match="Invalid atomic number"):
+        engine[0].calculate(xyz, np.array([14, 6, 8, 0], np.int32), cell)
+    again = engine[0].calculate(xyz, z, cell)
+    for k in again:
+        np.testing.assert_allclose(again[k], base[k], atol=2e-4, rtol=2e-5)
+
+
+def test_repeat_is_bitwise_deterministic(engine):
+    s = structures.load("C2", DATA)
+    a = engine[0].calculate(s.positions, s.numbers, s.cell)
+    b = engine[0].calculate(s.positions, s.numbers, s.cell)
+    assert a["energy"] == b["energy"]
+    assert np.array_equal(a["energies"], b["energies"])
+
+
+def test_device_entry_point_matches_host(engine):
+    import torch
+    s = structures.load("C2", DATA)
+    host = engine[0].calculate(s.positions, s.numbers, s.cell)
+    xyz = torch.from_numpy(s.positions).cuda()
+    z = torch.from_numpy(s.numbers).cuda()
+    torch.cuda.synchronize()
+    dev = engine[0].calculate_device(s.size, xyz.data_ptr(), z.data_ptr(), s.cell)
+    assert dev["energy"] == pytest.approx(host["energy"], rel=1e-7)
+    assert np.abs(dev["forces"] - host["forces"]).max() <= 1e-5
+
+
+def test_cli_matches_reference(library, archive_path, tmp_path):
+    s = structures.load("C1", DATA)
+    arc = tmp_path / "C1.arc"
+    structures.write_arc(arc, [s])
+    exe = ROOT / "lasp-pis_b200" / "bin" / "mace-main"
+    r = subprocess.run([str(exe), str(archive_path), str(arc), "--json"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    mine = json.loads(r.stdout)
+    ref = json.loads((GOLDEN / "ref_cli_C1.json").read_text())
+    assert mine["atoms"] == ref["atoms"] == 64
+    assert mine["energy"] == pytest.approx(ref["energy"], rel=1e-6)
+    assert np.abs(np.array(mine["forces"]) - np.array(ref["forces"])).max() <= 5e-5
+    out = tmp_path / "out.txt"
+    r = subprocess.run([str(exe), str(archive_path), str(arc), "--output", str(out)], capture_output=True, text=True)
+    assert r.returncode == 0 and "Energy (eV)" in out.read_text()
