@@ -1,0 +1,292 @@
+#!/usr/bin/env python3
+"""MH1 inference throughput on B200: atoms*evals/s of energy + forces + virial.
+
+Workload (N = 1): config C3 -- 10,000-atom perturbed-FCC cube, 46.4 A, ~85 neighbours per
+atom within 6 A -- with the seeded synthetic MH1-shaped archive.  One step = one full
+evaluation (neighbour list, both interaction layers, readouts, analytical backward, forces
+and virial).  N > 1 GPUs: one process per GPU, each evaluates its own C3-sized structure
+(independent structures, no data-path collective: weak scaling); the job time is the max
+over ranks.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+value  inputs already resident in HBM (mace_calculate_device), per-step CUDA events,
+       L2 flushed (256 MiB write) between steps outside the timed windows.
+e2e    the reference-facing C ABI (mace_calculate) with host buffers: the host-to-device
+       copy of the inputs and the device-to-host copy of energies/forces are inside.
+--impl reference   the reference's own implementation of this path -- its CUDA build
+       compiled from its sources (oracle/_ref/libmace_ref.so) -- through its C ABI on the
+       same config, on rank 0; falls back to the float64 CPU oracle if that build is absent.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT / "lasp-pis_b200" / "python")]
+DATA = ROOT / "lasp-pis_b200" / "data"
+METRIC = "atoms*evals/s (E+F+virial), MH1-shape, C3 10k-atom cell"
+UNIT = "atoms*evals/s"
+PEAKS = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def algorithmic_flops_backward1(edges: int) -> float:
+    """Algorithmic FP32 work of the layer-1 edge backward kernel per launch.
+
+    Per directed edge: the r-tangent of the 64 -> 10 x 128 radial projection (2 x 64 x 1280)
+    and the tensor-product adjoints, 15 FLOP per (term, channel) x 86 terms x 128 channels.
+    """
+    return edges * (2.0 * 64 * 1280 + 15.0 * 86 * 128)
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *args):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, flag in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), f[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def peaks():
+    if PEAKS.exists():
+        p = json.loads(PEAKS.read_text())
+        return p, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def cpu_baseline(archive):
+    """Float64 CPU oracle (a restatement of the reference path) on a bounded sample."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    from lasp_b200 import structures
+    cores = oracle.threads(os.cpu_count() or 1)
+    s = structures.density_sample(256)
+    model = oracle.Oracle(archive)
+    t = time.perf_counter()
+    model.calculate(s.positions, s.numbers, s.cell)
+    dt = time.perf_counter() - t
+    return {"value": s.size / dt, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"one E+F+virial evaluation of a {s.size}-atom cube at C3 density (same generator, "
+                      f"{dt:.1f} s) by the float64 oracle"}
+
+
+def reference_arm(args, archive, structure):
+    import ctypes as ct
+    lib_path = ROOT / "oracle" / "_ref" / "libmace_ref.so"
+    if not lib_path.exists():
+        base = cpu_baseline(archive)
+        line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": args.gpus,
+                "steps": 1, "warmup": 0, "higher_is_better": True, "data": "synthetic",
+                "config": {"workload": "C3 density sample (reference CUDA build absent)"},
+                "cpu_baseline": base, "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                                              "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+    lib = ct.CDLL(str(lib_path))
+    lib.mace_create_mh1.argtypes = [ct.c_char_p, ct.c_int]
+    lib.mace_create_mh1.restype = ct.c_void_p
+    lib.mace_last_error.restype = ct.c_char_p
+    lib.mace_calculate.argtypes = [ct.c_void_p, ct.c_int] + [ct.c_void_p] * 7
+    lib.mace_destroy.argtypes = [ct.c_void_p]
+    h = lib.mace_create_mh1(str(archive).encode(), 0)
+    if not h:
+        print(json.dumps({"impl": "reference", "unavailable": lib.mace_last_error().decode()}))
+        return
+    s = structure
+    n = s.size
+    e = np.zeros(1)
+    a = np.zeros(n, np.float32)
+    f = np.zeros((n, 3), np.float32)
+    v = np.zeros((3, 3), np.float32)
+    ptrs = [x.ctypes.data for x in (s.positions, s.numbers, s.cell, e, a, f, v)]
+    for _ in range(args.warmup):
+        assert lib.mace_calculate(h, n, *ptrs) == 0, lib.mace_last_error()
+    times = []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        assert lib.mace_calculate(h, n, *ptrs) == 0
+        times.append(time.perf_counter() - t)
+    lib.mace_destroy(h)
+    total = float(np.sum(times))
+    value = n * args.steps / total
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "C3: 10,000-atom perturbed FCC cube, 46.4 A, cutoff 6 A", "atoms": n,
+                       "implementation": "reference CUDA build (LipidL/LASP-PIS libmace) compiled for sm_100a from "
+                                         "its sources, called through its C ABI with host buffers"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": 1, "kind": "reference",
+                             "sample": "full C3 workload per step; the reference has no CPU inference path, its "
+                                       "host code (prepare/finish) is single-threaded and the model runs on one B200"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="C3")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", 0))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    from lasp_b200 import structures, synth
+    archive = DATA / "mh1_synth.pwm"
+    synth.write_archive(archive)
+    structure = structures.load(args.config, DATA)
+    if args.impl == "reference":
+        if rank == 0:
+            reference_arm(args, archive, structure)
+        return
+    import torch
+    torch.cuda.set_device(local)
+    lib_path = ROOT / "lasp-pis_b200" / "lib" / "libmace.so"
+    if not lib_path.exists():
+        raise SystemExit("libmace.so is not built: run __graft_entry__.build() (make -C lasp-pis_b200)")
+    from mace_inference import NativeMH1
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    model = NativeMH1(archive, backend=0, library=lib_path, device=local)
+    s = structure
+    n = s.size
+    xyz_d = torch.from_numpy(s.positions).cuda()
+    z_d = torch.from_numpy(s.numbers).cuda()
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MiB > L2
+    xyz_h = torch.from_numpy(s.positions).pin_memory()
+    z_h = torch.from_numpy(s.numbers).pin_memory()
+    xyz_h_np, z_h_np = xyz_h.numpy(), z_h.numpy()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        model.calculate_device(n, xyz_d.data_ptr(), z_d.data_ptr(), s.cell)
+        model.calculate(xyz_h_np, z_h_np, s.cell)
+    model.profile(True)
+
+    def timed(fn):
+        times, stages = [], {}
+        for _ in range(args.steps):
+            flush.fill_(1.0)
+            torch.cuda.synchronize()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            fn()
+            end.record()
+            end.synchronize()
+            times.append(start.elapsed_time(end))
+            for name, ms in model.diagnostics["stages"]:
+                stages.setdefault(name, []).append(ms)
+        return times, stages
+
+    with ClockSampler(local) as clocks:
+        barrier()
+        dev_times, stages = timed(lambda: model.calculate_device(n, xyz_d.data_ptr(), z_d.data_ptr(), s.cell))
+        barrier()
+        e2e_times, _ = timed(lambda: model.calculate(xyz_h_np, z_h_np, s.cell))
+        barrier()
+    diag = model.diagnostics
+    dev_ms = float(np.sum(dev_times))
+    e2e_ms = float(np.sum(e2e_times))
+    if world > 1:
+        t = torch.tensor([dev_ms, e2e_ms], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        dev_ms, e2e_ms = float(t[0]), float(t[1])
+    if rank == 0:
+        pk, kind = peaks()
+        edges = int(diag["edges"])
+        k_ms = float(np.mean(stages.get("backward1.edges", [float("nan")])))
+        achieved = algorithmic_flops_backward1(edges) / (k_ms * 1e-3) / 1e12
+        peak = float(pk["bf16_tflops"])
+        line = {
+            "metric": METRIC, "value": world * n * args.steps / (dev_ms * 1e-3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "C3: 10,000-atom perturbed FCC cube, 46.4 A, cutoff 6 A, seeded synthetic "
+                                   "MH1-shaped archive (seed 20261201)", "atoms_per_gpu": n, "edges_per_gpu": edges,
+                       "parallelism": f"dp{world} (independent structures)",
+                       "l2": "256 MiB buffer written between timed steps (outside the per-step event windows)"},
+            "e2e": {"value": world * n * args.steps / (e2e_ms * 1e-3), "unit": UNIT,
+                    "h2d_bytes_per_step": n * 16, "d2h_bytes_per_step": n * 16 + 84},
+            "roofline": {"kernel": "message_backward_kernel<1> (layer-1 edge backward, FP32 SIMT)",
+                         "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "peak_source": f"bf16_tflops ({kind}); the kernel runs on the "
+                                                                f"FP32 SIMT pipe", "traffic": None,
+                         "algorithmic_flops_per_launch": algorithmic_flops_backward1(edges),
+                         "kernel_ms": k_ms},
+            "stages_ms": {k: float(np.mean(v)) for k, v in stages.items()},
+            "gpu_launches": int(diag["launches"]) * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(archive)
+        print(json.dumps(line))
+    model.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -50,7 +50,11 @@ struct Diagnostics {
   float device_ms = 0;
   std::string reason;
   long long edges = 0; // directed edges of the last call (B200 build addition)
+  int launches = 0;     // kernels launched by the last call (B200 build addition)
+  std::vector<std::pair<std::string, float>> stages; // per-stage device ms when profiling
 };
+// Kernel launch counter of the calling thread (reset by Context::prepare).
+int &launch_counter();
 struct KernelResources {
   std::string name;
   int registers = 0, block_threads = 0, active_blocks_per_sm = 0;

@@ -44,6 +44,9 @@ MACE_EXPORT int mace_calculate_device(void *handle, int n, const float *xyz_devi
  * (receiver, sender, sx, sy, sz) for k < min(count, capacity), canonically sorted.
  * Returns the edge count (which may exceed capacity) or -1. */
 MACE_EXPORT long long mace_last_edges(void *handle, int *out, long long capacity);
+/* Turn per-stage device timing on/off for later calls; mace_diagnostics then reports
+ * "stages" (name, device ms) and "launches" of the last call.  Returns 0 or -1. */
+MACE_EXPORT int mace_profile(void *handle, int enable);
 /* Lapis neighbour list alone (no model): directed edges of a structure at `cutoff` with
  * backend 0/1/2 and an optional grid byte budget (0 = default), in input atom indices,
  * canonically sorted, 5 ints each as in mace_last_edges.  Runs on the current device.

@@ -15,6 +15,9 @@ public:
   MH1(const std::string &model, lapis::Options options, const std::string &head);
   ~MH1() override;
   size_t parameter_bytes() const;
+  // Per-stage CUDA-event timing of each call into diagnostics().stages (also enabled by the
+  // MACE_PROFILE_MH1 environment variable, which additionally prints them to stderr).
+  void set_profiling(bool enabled);
   lapis::Result calculate_file(const std::string &path, size_t frame = 0);
 };
 } // namespace mace

@@ -14,6 +14,7 @@
 // backend rule is evaluated on the device from exact integer occupancy sums, so prepare()
 // needs one host synchronisation (to size the edge arrays) instead of two.
 #include "lapis/runtime.hpp"
+#include "launch.cuh"
 #include <algorithm>
 #include <climits>
 #include <cmath>
@@ -313,6 +314,11 @@ __global__ void sum_partials(const double *partial, double *out) {
 }
 } // namespace
 
+int &launch_counter() {
+  thread_local int count = 0;
+  return count;
+}
+
 bool Buffer::reserve(size_t bytes) {
   if (bytes <= capacity)
     return false;
@@ -363,6 +369,7 @@ static void grow_pinned(void *&pinned, size_t &capacity, size_t bytes) {
 
 void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
   resources.clear();
+  launch_counter() = 0;
   if (s.size < 0 || s.size > INT_MAX / 16 || !std::isfinite(cutoff) || cutoff <= 0 ||
       !std::isfinite(cutoff * cutoff))
     throw Error("Invalid atom count or cutoff");
@@ -480,16 +487,16 @@ void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
     brute *= 2 * images[k] + 1;
   int blocks = (n + 255) / 256;
   if (n)
-    wrap_atoms<<<blocks, 256, 0, stream>>>(n, in_xyz, in_z, wp, wxyz, wind, bin, counts, status);
-  scan_exclusive<<<1, 1024, 0, stream>>>(counts, offsets, nb, nullptr);
+    lapis::launch(wrap_atoms, blocks, 256, 0, stream, n, in_xyz, in_z, wp, wxyz, wind, bin, counts, status);
+  lapis::launch(scan_exclusive, 1, 1024, 0, stream, counts, offsets, nb, nullptr);
   if (n) {
-    place_atoms<<<blocks, 256, 0, stream>>>(n, bin, offsets, cursor, internal_to_original);
-    order_bins<<<(nb + 255) / 256, 256, 0, stream>>>(nb, offsets, internal_to_original);
-    gather_atoms<<<blocks, 256, 0, stream>>>(n, internal_to_original, wxyz, in_z, bin, wind, sorted, sz, sb, sw,
+    lapis::launch(place_atoms, blocks, 256, 0, stream, n, bin, offsets, cursor, internal_to_original);
+    lapis::launch(order_bins, (nb + 255) / 256, 256, 0, stream, nb, offsets, internal_to_original);
+    lapis::launch(gather_atoms, blocks, 256, 0, stream, n, internal_to_original, wxyz, in_z, bin, wind, sorted, sz, sb, sw,
                                              original_to_internal);
-    bin_stats<<<(nb + 255) / 256, 256, 0, stream>>>(nb, dims[0], dims[1], dims[2], offsets, stats);
+    lapis::launch(bin_stats, (nb + 255) / 256, 256, 0, stream, nb, dims[0], dims[1], dims[2], offsets, stats);
   }
-  decide_backend<<<1, 1, 0, stream>>>(stats, int(opts.backend), grid_ok, brute);
+  lapis::launch(decide_backend, 1, 1, 0, stream, stats, int(opts.backend), grid_ok, brute);
   Traverse tv;
   tv.n = n;
   std::copy(dims, dims + 3, tv.grid);
@@ -502,8 +509,8 @@ void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
   tv.winding = sw;
   tv.stats = stats;
   if (n) {
-    neighbour_pass<<<(n * 32 + 255) / 256, 256, 0, stream>>>(tv, row_counts, nullptr, nullptr, nullptr, nullptr);
-    scan_exclusive<<<1, 1024, 0, stream>>>(row_counts, row, n, &stats->total_edges);
+    lapis::launch(neighbour_pass, (n * 32 + 255) / 256, 256, 0, stream, tv, row_counts, nullptr, nullptr, nullptr, nullptr);
+    lapis::launch(scan_exclusive, 1, 1024, 0, stream, row_counts, row, n, &stats->total_edges);
   }
   check(cudaGetLastError());
   // The single host synchronisation of prepare(): edge total, backend, diagnostics, status.
@@ -542,8 +549,8 @@ void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
   float4 *vec = array<float4>("edges.vector", size_t(total));
   int *rev = array<int>("edges.reverse", size_t(total));
   if (n && total) {
-    neighbour_pass<<<(n * 32 + 255) / 256, 256, 0, stream>>>(tv, nullptr, row, sender, shift, vec);
-    reverse_edges<<<n, 128, 0, stream>>>(row, sender, shift, rev, status);
+    lapis::launch(neighbour_pass, (n * 32 + 255) / 256, 256, 0, stream, tv, nullptr, row, sender, shift, vec);
+    lapis::launch(reverse_edges, n, 128, 0, stream, row, sender, shift, rev, status);
   }
   check(cudaGetLastError());
   geometry = {};
@@ -589,11 +596,11 @@ Result Context::finish(float *e, float *f, float *v, const float *e0_by_z) {
   double *partial = array<double>("output.partial", kReduceBlocks * 10 + 16);
   double *sums = partial + kReduceBlocks * 10;
   if (n)
-    restore_outputs<<<kReduceBlocks, 256, 0, stream>>>(n, original_to_internal, e, f, v, e0_by_z,
+    lapis::launch(restore_outputs, kReduceBlocks, 256, 0, stream, n, original_to_internal, e, f, v, e0_by_z,
                                                        input_elements_, ordered, partial);
   else
     clear(partial, kReduceBlocks * 10 * sizeof(double));
-  sum_partials<<<1, 32, 0, stream>>>(partial, sums);
+  lapis::launch(sum_partials, 1, 32, 0, stream, partial, sums);
   grow_pinned(pinned_, pinned_capacity_, out_floats * 4 + 256);
   auto *host = static_cast<char *>(pinned_);
   auto *hsums = reinterpret_cast<double *>(host);

@@ -208,6 +208,19 @@ long long lapis_neighbor_edges(int n, const float *xyz, const float *cell, float
   }
 }
 
+int mace_profile(void *handle, int enable) {
+  try {
+    error.clear();
+    if (!handle)
+      throw Error("Null calculator or result pointer");
+    static_cast<Handle *>(handle)->model->set_profiling(enable != 0);
+    return 0;
+  } catch (const std::exception &e) {
+    error = e.what();
+    return -1;
+  }
+}
+
 int mace_diagnostics(void *handle, char *buffer, size_t capacity) {
   try {
     if (!handle || !buffer)
@@ -222,7 +235,10 @@ int mace_diagnostics(void *handle, char *buffer, size_t capacity) {
       << ",\"brute_candidates\":" << d.brute_candidates << ",\"context_bytes\":" << d.allocated_bytes
       << ",\"context_peak_bytes\":" << d.peak_bytes << ",\"parameter_bytes\":" << h->model->parameter_bytes()
       << ",\"device_ms\":" << d.device_ms << ",\"edges\":" << d.edges << ",\"device\":" << h->device
-      << ",\"kernels\":[";
+      << ",\"launches\":" << d.launches << ",\"stages\":[";
+    for (size_t k = 0; k < d.stages.size(); ++k)
+      s << (k ? "," : "") << "[\"" << d.stages[k].first << "\"," << d.stages[k].second << "]";
+    s << "],\"kernels\":[";
     bool first = true;
     for (auto &r : h->model->resources()) {
       if (!first)

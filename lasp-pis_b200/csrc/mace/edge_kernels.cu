@@ -14,6 +14,7 @@
 // forces are written per edge and gathered per atom through the reverse-edge index
 // (deterministic, no force atomics), and per-atom sums are warp reductions.
 #include "model.hpp"
+#include "../lapis/launch.cuh"
 #include <type_traits>
 #include <utility>
 
@@ -677,13 +678,13 @@ __global__ void force_gather_kernel(DeviceGeometry g, const float4 *ef, float *f
 void launch_zbl(cudaStream_t s, const DeviceGeometry &g, const float *constants, const float *radii,
                 const float *coeff, float shift, float *energy, float *force, float *virial) {
   if (g.n)
-    zbl_kernel<<<(g.n * 32 + 255) / 256, 256, 0, s>>>(g, constants, radii, coeff, shift, energy, force, virial);
+    lapis::launch(zbl_kernel, (g.n * 32 + 255) / 256, 256, 0, s, g, constants, radii, coeff, shift, energy, force, virial);
 }
 
 void launch_edge_geometry(cudaStream_t s, const DeviceGeometry &g, const int *species, const float *constants,
                           const float *radii, const float *bessel, EdgeArrays ea, int *pair) {
   if (g.n)
-    geometry_kernel<<<(g.n * 32 + 255) / 256, 256, 0, s>>>(g, species, constants, radii, bessel, ea, pair);
+    lapis::launch(geometry_kernel, (g.n * 32 + 255) / 256, 256, 0, s, g, species, constants, radii, bessel, ea, pair);
 }
 
 void launch_radial(cudaStream_t s, const DeviceGeometry &g, const Layer &l, const int *pair, EdgeArrays ea,
@@ -695,7 +696,7 @@ void launch_radial(cudaStream_t s, const DeviceGeometry &g, const Layer &l, cons
   lapis::check(cudaFuncSetAttribute(radial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   long long groups = (E + 3) / 4;
   int blocks = int(std::min<long long>((groups + 3) / 4, 148 * 8));
-  radial_kernel<<<blocks, 128, smem, s>>>(E, RadialParams{l.radial, l.density}, pair, ea, ro);
+  lapis::launch(radial_kernel, blocks, 128, smem, s, E, RadialParams{l.radial, l.density}, pair, ea, ro);
 }
 
 void launch_message_forward(cudaStream_t s, int layer, const DeviceGeometry &g, const Layer &l, EdgeArrays ea,
@@ -703,10 +704,10 @@ void launch_message_forward(cudaStream_t s, int layer, const DeviceGeometry &g, 
   if (!g.n)
     return;
   if (layer == 0)
-    message_forward_kernel<0><<<g.n, 128, 0, s>>>(g.n, g.edge_offsets, g.edge_sender, ro.h, ea.Y, ea.cut, ro.density,
+    lapis::launch(message_forward_kernel<0>, g.n, 128, 0, s, g.n, g.edge_offsets, g.edge_sender, ro.h, ea.Y, ea.cut, ro.density,
                                                   up, l.radial.out_t, l.radial.out_b, l.tp, message, density);
   else
-    message_forward_kernel<1><<<g.n, 128, 0, s>>>(g.n, g.edge_offsets, g.edge_sender, ro.h, ea.Y, ea.cut, ro.density,
+    lapis::launch(message_forward_kernel<1>, g.n, 128, 0, s, g.n, g.edge_offsets, g.edge_sender, ro.h, ea.Y, ea.cut, ro.density,
                                                   up, l.radial.out_t, l.radial.out_b, l.tp, message, density);
 }
 
@@ -716,7 +717,7 @@ void launch_message_backward(cudaStream_t s, int layer, const DeviceGeometry &g,
   if (!g.n)
     return;
 #define MH1_BWD(L, A)                                                                                              \
-  message_backward_kernel<L, A><<<g.n, 128, 0, s>>>(g.n, g.edge_offsets, g.edge_sender, g.edge_vector, ro.h, ro.dh, \
+  lapis::launch(message_backward_kernel<L, A>, g.n, 128, 0, s, g.n, g.edge_offsets, g.edge_sender, g.edge_vector, ro.h, ro.dh, \
                                                     ea.cut, ro.density, up, l.radial.out_t, l.radial.out_b, l.tp,  \
                                                     message_grad, density_grad, up_grad, edge_force)
   if (layer == 0) {
@@ -736,6 +737,6 @@ void launch_message_backward(cudaStream_t s, int layer, const DeviceGeometry &g,
 void launch_force_gather(cudaStream_t s, const DeviceGeometry &g, const float4 *edge_force, float *force,
                          float *virial) {
   if (g.n && g.edge_capacity)
-    force_gather_kernel<<<(g.n * 32 + 255) / 256, 256, 0, s>>>(g, edge_force, force, virial);
+    lapis::launch(force_gather_kernel, (g.n * 32 + 255) / 256, 256, 0, s, g, edge_force, force, virial);
 }
 } // namespace mace

@@ -18,6 +18,12 @@ using namespace lapis;
 
 struct MH1::Model {
   ModelData data;
+  bool profiling = false;
+  std::vector<cudaEvent_t> events;
+  ~Model() {
+    for (auto e : events)
+      cudaEventDestroy(e);
+  }
 };
 
 MH1::MH1(const std::string &archive, Options o, const std::string &head)
@@ -30,36 +36,45 @@ MH1::MH1(const std::string &archive, Options o, const std::string &head)
 MH1::MH1(const std::string &archive, Options o) : MH1(archive, o, {}) {}
 MH1::~MH1() = default;
 size_t MH1::parameter_bytes() const { return model_->data.bytes; }
+void MH1::set_profiling(bool enabled) { model_->profiling = enabled; }
 
 namespace {
-// Opt-in per-stage timing (MACE_PROFILE_MH1=1), like the reference's StageTimer
-// (mace/src/mh1.cu:53-82): CUDA events on the model stream, printed to stderr.
+// Per-stage timing (like the reference's StageTimer, mace/src/mh1.cu:53-82): CUDA events
+// recorded on the model stream between stages, taken from a persistent pool so that the
+// timed path creates no events.
 struct StageTimer {
   cudaStream_t stream;
-  bool enabled = std::getenv("MACE_PROFILE_MH1") != nullptr;
-  std::vector<std::pair<std::string, cudaEvent_t>> events;
-  explicit StageTimer(cudaStream_t s) : stream(s) { mark("start"); }
+  bool enabled, print;
+  std::vector<cudaEvent_t> &pool;
+  std::vector<std::string> names;
+  StageTimer(cudaStream_t s, bool on, std::vector<cudaEvent_t> &events)
+      : stream(s), enabled(on || std::getenv("MACE_PROFILE_MH1")), print(std::getenv("MACE_PROFILE_MH1")),
+        pool(events) {
+    mark("start");
+  }
   void mark(const std::string &name) {
     if (!enabled)
       return;
-    cudaEvent_t e;
-    check(cudaEventCreate(&e));
-    events.emplace_back(name, e);
-    check(cudaEventRecord(e, stream));
-  }
-  void report() {
-    if (!enabled || events.empty())
-      return;
-    check(cudaEventSynchronize(events.back().second));
-    for (size_t k = 1; k < events.size(); ++k) {
-      float ms = 0;
-      check(cudaEventElapsedTime(&ms, events[k - 1].second, events[k].second));
-      std::fprintf(stderr, "MH1 %s: %.4f ms\n", events[k].first.c_str(), ms);
+    if (names.size() == pool.size()) {
+      cudaEvent_t e;
+      check(cudaEventCreate(&e));
+      pool.push_back(e);
     }
+    check(cudaEventRecord(pool[names.size()], stream));
+    names.push_back(name);
   }
-  ~StageTimer() {
-    for (auto &e : events)
-      cudaEventDestroy(e.second);
+  void report(Diagnostics &d) {
+    d.stages.clear();
+    if (!enabled || names.size() < 2)
+      return;
+    check(cudaEventSynchronize(pool[names.size() - 1]));
+    for (size_t k = 1; k < names.size(); ++k) {
+      float ms = 0;
+      check(cudaEventElapsedTime(&ms, pool[k - 1], pool[k]));
+      d.stages.emplace_back(names[k], ms);
+      if (print)
+        std::fprintf(stderr, "MH1 %s: %.4f ms\n", names[k].c_str(), ms);
+    }
   }
 };
 } // namespace
@@ -72,7 +87,7 @@ Result MH1::evaluate() {
   size_t E = size_t(c.geometry.edge_capacity);
   if (n > INT_MAX / 9728)
     throw Error("MH1 node dimensions exceed v1 int32 capacity");
-  StageTimer timer(s);
+  StageTimer timer(s, model_->profiling, model_->events);
   auto node = [&](const std::string &name, size_t width) { return c.array<float>(name, size_t(n) * width); };
   const float *cst = m.constants;
   int *species = c.array<int>("mh.species", n);
@@ -165,8 +180,10 @@ Result MH1::evaluate() {
   launch_force_gather(s, c.geometry, edge_force, force, virial);
   check(cudaGetLastError());
   timer.mark("forces");
+  timer.mark("finish-enqueue");
   auto result = c.finish(energy, force, virial, m.e0_z);
-  timer.report();
+  c.diagnostics.launches = launch_counter();
+  timer.report(c.diagnostics);
   return result;
 }
 } // namespace mace

@@ -12,6 +12,7 @@
 // Normalisation and gating are fused into one pass (forward) and one pass with the
 // normalisation VJP (backward); the reference launches them separately.
 #include "model.hpp"
+#include "../lapis/launch.cuh"
 
 namespace mace {
 namespace {
@@ -253,11 +254,11 @@ unsigned blocks_for(size_t count, int threads) { return unsigned((count + thread
 
 void launch_species(cudaStream_t s, const lapis::DeviceGeometry &g, const int *lookup, int *species) {
   if (g.n)
-    species_kernel<<<blocks_for(g.n, 256), 256, 0, s>>>(g, lookup, species);
+    lapis::launch(species_kernel, blocks_for(g.n, 256), 256, 0, s, g, lookup, species);
 }
 void launch_embed(cudaStream_t s, int n, const int *species, const float *embedding, float *x) {
   if (n)
-    embed_kernel<<<blocks_for(size_t(n) * 512, 256), 256, 0, s>>>(n, species, embedding, x);
+    lapis::launch(embed_kernel, blocks_for(size_t(n) * 512, 256), 256, 0, s, n, species, embedding, x);
 }
 
 void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bool backward, bool add) {
@@ -269,12 +270,12 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
     const float *w = l.weight + p.weight_offset;
     if (!backward) {
       dim3 grid((p.out_mul + BN - 1) / BN, (n + BM - 1) / BM, p.dim);
-      gemm_kernel<false><<<grid, 256, 0, s>>>(n, p.out_mul, p.in_mul, x + size_t(p.in_offset) * n, p.in_mul,
+      lapis::launch(gemm_kernel<false>, grid, 256, 0, s, n, p.out_mul, p.in_mul, x + size_t(p.in_offset) * n, p.in_mul,
                                               (long long)n * p.in_mul, w, p.out_mul, y + size_t(p.out_offset) * n,
                                               p.out_mul, (long long)n * p.out_mul);
     } else {
       dim3 grid((p.in_mul + BN - 1) / BN, (n + BM - 1) / BM, p.dim);
-      gemm_kernel<true><<<grid, 256, 0, s>>>(n, p.in_mul, p.out_mul, x + size_t(p.out_offset) * n, p.out_mul,
+      lapis::launch(gemm_kernel<true>, grid, 256, 0, s, n, p.in_mul, p.out_mul, x + size_t(p.out_offset) * n, p.out_mul,
                                              (long long)n * p.out_mul, w, p.out_mul, y + size_t(p.in_offset) * n,
                                              p.in_mul, (long long)n * p.in_mul);
     }
@@ -284,35 +285,35 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
 void launch_normalize_gate(cudaStream_t s, int n, const float *raw, const float *res, const float *density,
                            float alpha, float beta, float scalar_scale, float gate_scale, float *pre, float *gate) {
   if (n)
-    normalize_gate_kernel<<<blocks_for(size_t(n) * 512, 256), 256, 0, s>>>(n, raw, res, density, alpha, beta,
+    lapis::launch(normalize_gate_kernel, blocks_for(size_t(n) * 512, 256), 256, 0, s, n, raw, res, density, alpha, beta,
                                                                            scalar_scale, gate_scale, pre, gate);
 }
 void launch_gate_norm_backward(cudaStream_t s, int n, const float *pre, const float *raw, const float *density,
                                const float *gate_grad, float alpha, float beta, float scalar_scale, float gate_scale,
                                float *pre_grad, float *raw_grad, float *density_grad) {
   if (n)
-    gate_norm_backward_kernel<<<n, 128, 0, s>>>(n, pre, raw, density, gate_grad, alpha, beta, scalar_scale,
+    lapis::launch(gate_norm_backward_kernel, n, 128, 0, s, n, pre, raw, density, gate_grad, alpha, beta, scalar_scale,
                                                 gate_scale, pre_grad, raw_grad, density_grad);
 }
 void launch_product(cudaStream_t s, int n, const Layer &l, const float *x, float *y) {
   if (n)
-    product_kernel<<<n * 4, 128, 0, s>>>(n, l.poly, l.pcoef, l.npoly, l.pouts, x, y);
+    lapis::launch(product_kernel, n * 4, 128, 0, s, n, l.poly, l.pcoef, l.npoly, l.pouts, x, y);
 }
 void launch_product_backward(cudaStream_t s, int n, const Layer &l, const float *x, const float *grad, float *xg) {
   if (n)
-    product_backward_kernel<<<n * 4, 128, 0, s>>>(n, l.poly, l.pcoef, l.npoly, l.pouts, x, grad, xg);
+    lapis::launch(product_backward_kernel, n * 4, 128, 0, s, n, l.poly, l.pcoef, l.npoly, l.pouts, x, grad, xg);
 }
 void launch_add(cudaStream_t s, size_t count, const float *a, float *b, float scale) {
   if (count)
-    add_kernel<<<blocks_for(count, 256), 256, 0, s>>>(count, a, b, scale);
+    lapis::launch(add_kernel, blocks_for(count, 256), 256, 0, s, count, a, b, scale);
 }
 void launch_fill(cudaStream_t s, size_t count, float *a, float value) {
   if (count)
-    fill_kernel<<<blocks_for(count, 256), 256, 0, s>>>(count, a, value);
+    lapis::launch(fill_kernel, blocks_for(count, 256), 256, 0, s, count, a, value);
 }
 void launch_readout_act(cudaStream_t s, int count, const float *x, const float *grad, float *y, float scale,
                         bool backward) {
   if (count)
-    readout_act_kernel<<<blocks_for(count, 256), 256, 0, s>>>(count, x, grad, y, scale, backward);
+    lapis::launch(readout_act_kernel, blocks_for(count, 256), 256, 0, s, count, x, grad, y, scale, backward);
 }
 } // namespace mace

@@ -31,6 +31,8 @@ def load(path=None) -> ct.CDLL:
     lib.mace_calculate_device.restype = ct.c_int
     lib.mace_diagnostics.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_size_t]
     lib.mace_diagnostics.restype = ct.c_int
+    lib.mace_profile.argtypes = [ct.c_void_p, ct.c_int]
+    lib.mace_profile.restype = ct.c_int
     lib.mace_last_edges.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_longlong]
     lib.mace_last_edges.restype = ct.c_longlong
     lib.lapis_neighbor_edges.argtypes = [ct.c_int, ct.c_void_p, ct.c_void_p, ct.c_float, ct.c_int, ct.c_longlong,
@@ -93,6 +95,10 @@ class NativeMH1:
     def calculate_device(self, n, xyz_ptr, z_ptr, cell):
         """Device-resident inputs (raw device pointers on the handle's GPU)."""
         return self._call(self.lib.mace_calculate_device, n, xyz_ptr, z_ptr, cell)
+
+    def profile(self, enable=True):
+        if self.lib.mace_profile(self.handle, int(enable)):
+            raise RuntimeError(_error(self.lib))
 
     def last_edges(self):
         count = self.lib.mace_last_edges(self.handle, None, 0)
