@@ -53,6 +53,25 @@ MACE_EXPORT int mace_profile(void *handle, int enable);
  * Returns the edge count (may exceed capacity) or -1 (message in mace_last_error). */
 MACE_EXPORT long long lapis_neighbor_edges(int n, const float *xyz, const float *cell, float cutoff, int backend,
                                            long long grid_bytes, int *out, long long capacity);
+/* Neighbour list that allocates no GPU memory.  No counterpart in the reference.
+ * For callers that cannot allocate device memory -- hosts that own a fixed device memory pool,
+ * run inside another framework's allocator, or forbid allocation during their time step --
+ * this builds the same directed edge list as the calculator's neighbour step but keeps all
+ * of its scratch in one fixed-size array that the library places in every GPU that loads it
+ * (about 512 KiB, held until the process exits).  Inputs are device arrays xyz [n][3] and
+ * atomic numbers [n] plus the host cell (3 x 3 rows); outputs are caller-owned device arrays:
+ * row [n + 1] (CSR offsets by input atom index), and for each edge the sender, the image
+ * shift (3 ints) and the displacement (float4: dx, dy, dz, r; 16-byte aligned).  Candidates
+ * are enumerated by brute force over all atoms and periodic images.  Limits: n <= 16384.
+ * Returns the edge count E; if E exceeds `capacity` only row is written, so the caller can
+ * retry with larger buffers.  Returns -1 on error (message in mace_last_error), including
+ * n above the limit.  Runs on the current device and on `stream` (NULL = default stream) and
+ * blocks until done.  The first call on a device looks up that device's copy of the array;
+ * make that first call before capturing any stream.  Every call reuses the same array, so
+ * calls that overlap on the GPU race with each other: serialise them. */
+MACE_EXPORT long long lapis_neighbor_list_static(int n, const float *xyz, const int *elements, const float *cell,
+                                                 float cutoff, int *row, int *sender, int *shift, float *vector,
+                                                 long long capacity, void *stream);
 #ifdef __cplusplus
 }
 #endif

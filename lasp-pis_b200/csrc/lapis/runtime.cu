@@ -651,3 +651,170 @@ Result Calculator::calculate(const Structure &s) {
   }
 }
 } // namespace lapis
+
+// ---------------------------------------------------------------------------------------
+// Neighbour list without device allocation.
+//
+// For callers that must not allocate GPU memory themselves or through this library -- for
+// example a host code that already owns every device buffer (a fixed-size memory pool, an
+// embedding in another framework's allocator, or a driver that forbids allocation while it
+// runs) -- lapis_neighbor_list_static builds the same CSR edge list as Context::prepare but
+// keeps every intermediate in one file-scope device array of fixed size instead of calling
+// cudaMalloc.  The caller passes device inputs and device outputs.  Limits: at most
+// kStaticMaxAtoms atoms; brute-force candidate enumeration (all atoms x all periodic images),
+// which is what the reference does for small or skewed cells.
+// ---------------------------------------------------------------------------------------
+namespace lapis {
+namespace {
+constexpr int kStaticMaxAtoms = 16384;
+// Word layout: wrapped xyz [3N] | winding [3N] | bin [N] | per-receiver counts [N + 1] |
+// grid counts [2] | status [4] | ConnStats (8 words, 8-byte aligned at the end).
+constexpr size_t kStaticWords = size_t(kStaticMaxAtoms) * 8 + 1 + 2 + 4 + 1 + 8;
+// One array per GPU that loads this library, held until process exit (~512 KiB).
+static __device__ __align__(256) int g_static_scratch[kStaticWords];
+
+struct StaticScratch {
+  int *base = nullptr;
+  bool ready = false;
+};
+StaticScratch g_static_by_device[64];
+std::atomic_flag g_static_lock = ATOMIC_FLAG_INIT;
+
+// Device address of g_static_scratch for the current device (the host-side symbol is only a
+// stand-in).  Resolved once per device, on that device.
+int *static_scratch_address() {
+  int device = 0;
+  check(cudaGetDevice(&device));
+  if (device < 0 || device >= 64)
+    throw Error("Device index out of range for the static neighbour-list scratch");
+  while (g_static_lock.test_and_set(std::memory_order_acquire)) {
+  }
+  struct Unlock {
+    ~Unlock() { g_static_lock.clear(std::memory_order_release); }
+  } unlock;
+  auto &slot = g_static_by_device[device];
+  if (!slot.ready) {
+    void *p = nullptr;
+    check(cudaGetSymbolAddress(&p, g_static_scratch));
+    slot.base = static_cast<int *>(p);
+    slot.ready = true;
+  }
+  return slot.base;
+}
+} // namespace
+} // namespace lapis
+
+#include "mace/c_api.h"
+
+// thread-local error text shared with the C ABI in c_api.cpp
+namespace lapis {
+void set_c_api_error(const std::string &message);
+}
+
+long long lapis_neighbor_list_static(int n, const float *xyz, const int *elements, const float *cell, float cutoff,
+                                     int *row, int *sender, int *shift, float *vector, long long capacity,
+                                     void *stream_handle) {
+  using namespace lapis;
+  try {
+    set_c_api_error("");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
+    if (n < 0 || n > kStaticMaxAtoms)
+      throw Error("lapis_neighbor_list_static supports 0.." + std::to_string(kStaticMaxAtoms) + " atoms, got " +
+                  std::to_string(n));
+    if (!cell || !row || (n && (!xyz || !elements)) || (capacity > 0 && (!sender || !shift || !vector)))
+      throw Error("Null structure data");
+    if (capacity < 0)
+      throw Error("Negative edge capacity");
+    if (reinterpret_cast<uintptr_t>(vector) % 16)
+      throw Error("Edge vector output must be 16-byte aligned");
+    if (!std::isfinite(cutoff) || cutoff <= 0 || !std::isfinite(cutoff * cutoff))
+      throw Error("Invalid atom count or cutoff");
+    double h[9];
+    for (int k = 0; k < 9; ++k) {
+      h[k] = cell[k];
+      if (!std::isfinite(h[k]))
+        throw Error("Nonfinite cell");
+    }
+    double det = h[0] * (h[4] * h[8] - h[5] * h[7]) - h[1] * (h[3] * h[8] - h[5] * h[6]) +
+                 h[2] * (h[3] * h[7] - h[4] * h[6]);
+    double scale = 0;
+    for (double a : h)
+      scale = std::max(scale, std::abs(a));
+    if (!std::isfinite(det) || scale == 0 || std::abs(det) < 1e-10 * scale * scale * scale)
+      throw Error("Singular or ill-conditioned cell");
+    WrapParams wp;
+    double *inv = wp.inv;
+    inv[0] = (h[4] * h[8] - h[5] * h[7]) / det;
+    inv[1] = (h[2] * h[7] - h[1] * h[8]) / det;
+    inv[2] = (h[1] * h[5] - h[2] * h[4]) / det;
+    inv[3] = (h[5] * h[6] - h[3] * h[8]) / det;
+    inv[4] = (h[0] * h[8] - h[2] * h[6]) / det;
+    inv[5] = (h[2] * h[3] - h[0] * h[5]) / det;
+    inv[6] = (h[3] * h[7] - h[4] * h[6]) / det;
+    inv[7] = (h[1] * h[6] - h[0] * h[7]) / det;
+    inv[8] = (h[0] * h[4] - h[1] * h[3]) / det;
+    std::copy(h, h + 9, wp.h);
+    wp.dims[0] = wp.dims[1] = wp.dims[2] = 1;
+    int images[3];
+    for (int k = 0; k < 3; ++k) {
+      double height = 1 / std::sqrt(inv[k] * inv[k] + inv[3 + k] * inv[3 + k] + inv[6 + k] * inv[6 + k]);
+      double im = std::ceil(cutoff / height);
+      if (im > 1000000)
+        throw Error("Excessive periodic image range");
+      images[k] = std::max(1, int(im));
+    }
+    if (double(2 * images[0] + 1) * (2 * images[1] + 1) * (2 * images[2] + 1) > INT_MAX)
+      throw Error("Periodic image tuples exceed v1 int32 capacity");
+    int *base = static_scratch_address();
+    const size_t N = kStaticMaxAtoms;
+    float *wxyz = reinterpret_cast<float *>(base);
+    int *wind = base + 3 * N, *bin = base + 6 * N, *counts = base + 7 * N, *grid = base + 8 * N + 1;
+    int *status = grid + 2;
+    auto *stats = reinterpret_cast<ConnStats *>(base + kStaticWords - 8);
+    // The array keeps the previous call's contents: clear what must start at zero.
+    check(cudaMemsetAsync(grid, 0, 6 * sizeof(int), stream));
+    check(cudaMemsetAsync(stats, 0, sizeof(ConnStats), stream));
+    check(cudaMemsetAsync(counts, 0, (size_t(n) + 1) * sizeof(int), stream));
+    Traverse tv;
+    tv.n = n;
+    tv.grid[0] = tv.grid[1] = tv.grid[2] = 1;
+    std::copy(images, images + 3, tv.images);
+    std::copy(cell, cell + 9, tv.h);
+    tv.cutoff2 = cutoff * cutoff;
+    tv.xyz = wxyz;
+    tv.bins = bin;
+    tv.offsets = nullptr;
+    tv.winding = wind;
+    tv.stats = stats;
+    if (n) {
+      wrap_atoms<<<(n + 255) / 256, 256, 0, stream>>>(n, xyz, elements, wp, wxyz, wind, bin, grid, status);
+      decide_backend<<<1, 1, 0, stream>>>(stats, 1, 0, 0.0);
+      neighbour_pass<<<(n * 32 + 255) / 256, 256, 0, stream>>>(tv, counts, nullptr, nullptr, nullptr, nullptr);
+    }
+    scan_exclusive<<<1, 1024, 0, stream>>>(counts, row, n, &stats->total_edges);
+    check(cudaGetLastError());
+    long long total = 0;
+    int host_status = 0;
+    check(cudaMemcpyAsync(&total, &stats->total_edges, sizeof(total), cudaMemcpyDeviceToHost, stream));
+    check(cudaMemcpyAsync(&host_status, status, sizeof(int), cudaMemcpyDeviceToHost, stream));
+    check(cudaStreamSynchronize(stream));
+    if (host_status == kStatusBadElement)
+      throw Error("Invalid atomic number");
+    if (host_status == kStatusNonfinite)
+      throw Error("Nonfinite coordinate");
+    if (host_status == kStatusWinding)
+      throw Error("Coordinate winding exceeds int32 range");
+    if (total > INT_MAX)
+      throw Error("Directed edge count exceeds int32 capacity");
+    if (n && total && total <= capacity) {
+      neighbour_pass<<<(n * 32 + 255) / 256, 256, 0, stream>>>(tv, nullptr, row, sender, shift,
+                                                               reinterpret_cast<float4 *>(vector));
+      check(cudaGetLastError());
+      check(cudaStreamSynchronize(stream));
+    }
+    return total;
+  } catch (const std::exception &e) {
+    lapis::set_c_api_error(e.what());
+    return -1;
+  }
+}

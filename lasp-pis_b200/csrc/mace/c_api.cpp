@@ -14,6 +14,11 @@ using namespace lapis;
 using mace::MH1;
 namespace {
 thread_local std::string error;
+} // namespace
+namespace lapis {
+void set_c_api_error(const std::string &message) { error = message; }
+} // namespace lapis
+namespace {
 
 struct Handle {
   int device = 0;
