@@ -47,6 +47,12 @@ MACE_EXPORT long long mace_last_edges(void *handle, int *out, long long capacity
 /* Turn per-stage device timing on/off for later calls; mace_diagnostics then reports
  * "stages" (name, device ms) and "launches" of the last call.  Returns 0 or -1. */
 MACE_EXPORT int mace_profile(void *handle, int enable);
+/* Test hook for the node-linear GEMMs: C[z] (+)= A[z] * B on the current device for z < batch,
+ * A [batch][M][K], B [K][N], C [batch][M][N] row-major device arrays; mode 0 runs the FP32
+ * SIMT kernel, mode 1 the tensor-core (tcgen05, split-tf32) kernel.  Blocks; returns 0 or -1.
+ * No counterpart in the reference. */
+MACE_EXPORT int mace_debug_gemm(int M, int N, int K, int batch, const float *A, const float *B, float *C,
+                                int accumulate, int mode);
 /* Lapis neighbour list alone (no model): directed edges of a structure at `cutoff` with
  * backend 0/1/2 and an optional grid byte budget (0 = default), in input atom indices,
  * canonically sorted, 5 ints each as in mace_last_edges.  Runs on the current device.

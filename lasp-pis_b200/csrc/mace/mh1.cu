@@ -90,6 +90,7 @@ Result MH1::evaluate() {
   StageTimer timer(s, model_->profiling, model_->events);
   auto node = [&](const std::string &name, size_t width) { return c.array<float>(name, size_t(n) * width); };
   const float *cst = m.constants;
+  int *status = c.geometry.status;
   int *species = c.array<int>("mh.species", n);
   float *energy = node("mh.e", 1), *force = node("mh.f", 3), *virial = node("mh.v", 9);
   float *x0 = node("mh.embedding", 512);
@@ -117,21 +118,21 @@ Result MH1::evaluate() {
     hidden[k] = node(p + ".hidden", k ? 512 : 2048);
     ro[k] = RadialOut{c.array<float>(p + ".h", E * 64), c.array<float>(p + ".dh", E * 64),
                       c.array<float2>(p + ".den", E)};
-    linear(s, n, l.up, input, up[k]);
-    linear(s, n, l.res, up[k], res);
-    linear(s, n, l.skip, input, skip);
+    linear(s, n, l.up, input, up[k], false, false, status);
+    linear(s, n, l.res, up[k], res, false, false, status);
+    linear(s, n, l.skip, input, skip, false, false, status);
     launch_radial(s, c.geometry, l, pair, ea, ro[k]);
     timer.mark("forward" + std::to_string(k) + ".linears/radial");
     launch_message_forward(s, k, c.geometry, l, ea, ro[k], up[k], msg, rho[k]);
     timer.mark("forward" + std::to_string(k) + ".messages");
-    linear(s, n, l.one, msg, raw[k]);
+    linear(s, n, l.one, msg, raw[k], false, false, status);
     launch_normalize_gate(s, n, raw[k], res, rho[k], l.alpha, l.beta, cst[11], cst[12], pre[k], gate);
-    linear(s, n, l.two, gate, pin[k]);
+    linear(s, n, l.two, gate, pin[k], false, false, status);
     launch_product(s, n, l, pin[k], poly);
-    linear(s, n, l.plin, poly, hidden[k]);
+    linear(s, n, l.plin, poly, hidden[k], false, false, status);
     launch_add(s, size_t(n) * (k ? 512 : 2048), skip, hidden[k], 1.f);
     if (k == 0) {
-      linear(s, n, m.read0, hidden[0], node_e);
+      linear(s, n, m.read0, hidden[0], node_e, false, false, status);
       launch_add(s, n, node_e, energy, cst[6]);
     }
     input = hidden[k];
@@ -139,9 +140,9 @@ Result MH1::evaluate() {
   }
   float *rpre = node("mh.r.pre", 16), *rhid = node("mh.r.hidden", 16), *rgrad = node("mh.r.grad", 16),
         *rdpre = node("mh.r.dpre", 16);
-  linear(s, n, m.read1up, hidden[1], rpre);
+  linear(s, n, m.read1up, hidden[1], rpre, false, false, status);
   launch_readout_act(s, n * 16, rpre, nullptr, rhid, cst[13], false);
-  linear(s, n, m.read1down, rhid, node_e);
+  linear(s, n, m.read1down, rhid, node_e, false, false, status);
   launch_add(s, n, node_e, energy, cst[6]);
   // ---- analytical backward ----
   float *one = node_e;
@@ -151,29 +152,29 @@ Result MH1::evaluate() {
   float *msggrad = msg, *upgrad = node("mh.b.up", 512);
   float4 *edge_force = c.array<float4>("mh.edge.force", E);
   launch_fill(s, n, one, cst[6]);
-  linear(s, n, m.read1down, one, rgrad, true);
+  linear(s, n, m.read1down, one, rgrad, true, false, status);
   launch_readout_act(s, n * 16, rpre, rgrad, rdpre, cst[13], true);
-  linear(s, n, m.read1up, rdpre, hgrad1, true);
+  linear(s, n, m.read1up, rdpre, hgrad1, true, false, status);
   timer.mark("readouts");
   float *hgrad = hgrad1;
   for (int k = 1; k >= 0; --k) {
     const Layer &l = m.layers[k];
     if (k == 0)
-      linear(s, n, m.read0, one, hgrad, true, true);
-    linear(s, n, l.plin, hgrad, pgrad, true);
+      linear(s, n, m.read0, one, hgrad, true, true, status);
+    linear(s, n, l.plin, hgrad, pgrad, true, false, status);
     launch_product_backward(s, n, l, pin[k], pgrad, pingrad);
-    linear(s, n, l.two, pingrad, gategrad, true);
+    linear(s, n, l.two, pingrad, gategrad, true, false, status);
     launch_gate_norm_backward(s, n, pre[k], raw[k], rho[k], gategrad, l.alpha, l.beta, cst[11], cst[12], pregrad,
                               rawgrad, rhograd);
-    linear(s, n, l.one, rawgrad, msggrad, true);
+    linear(s, n, l.one, rawgrad, msggrad, true, false, status);
     if (k == 1)
-      linear(s, n, l.res, pregrad, upgrad, true);
+      linear(s, n, l.res, pregrad, upgrad, true, false, status);
     timer.mark("backward" + std::to_string(k) + ".node");
     launch_message_backward(s, k, c.geometry, l, ea, ro[k], up[k], msggrad, rhograd, upgrad, edge_force, k == 0);
     timer.mark("backward" + std::to_string(k) + ".edges");
     if (k == 1) {
-      linear(s, n, l.skip, hgrad, hgrad0, true);
-      linear(s, n, l.up, upgrad, hgrad0, true, true);
+      linear(s, n, l.skip, hgrad, hgrad0, true, false, status);
+      linear(s, n, l.up, upgrad, hgrad0, true, true, status);
       hgrad = hgrad0;
     }
   }

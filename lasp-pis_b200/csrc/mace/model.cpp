@@ -32,6 +32,16 @@ float *Device::upload(const void *data, size_t bytes) {
   return static_cast<float *>(p);
 }
 
+void split_tf32(const float *w, size_t count, float *hi, float *lo) {
+  for (size_t k = 0; k < count; ++k) {
+    uint32_t bits;
+    std::memcpy(&bits, w + k, 4);
+    bits = (bits + 0x1000u) & 0xffffe000u;
+    std::memcpy(hi + k, &bits, 4);
+    lo[k] = w[k] - hi[k];
+  }
+}
+
 namespace {
 struct Archive {
   std::map<std::string, std::vector<char>> records;
@@ -182,6 +192,24 @@ void ModelData::load(const std::string &path) {
       l.paths.push_back(p);
     }
     l.weight = up(w);
+    for (const auto &p : l.paths) {
+      TCWeights t;
+      if (tc_gemm_supported(p.out_mul, p.in_mul) && tc_gemm_supported(p.in_mul, p.out_mul)) {
+        size_t cnt = size_t(p.in_mul) * p.out_mul;
+        const float *src = w.data() + p.weight_offset;
+        std::vector<float> wt(cnt), hi(cnt), lo(cnt);
+        for (int i = 0; i < p.in_mul; ++i)
+          for (int o = 0; o < p.out_mul; ++o)
+            wt[size_t(o) * p.in_mul + i] = src[size_t(i) * p.out_mul + o];
+        split_tf32(wt.data(), cnt, hi.data(), lo.data());
+        t.fwd_hi = up(hi);
+        t.fwd_lo = up(lo);
+        split_tf32(src, cnt, hi.data(), lo.data());
+        t.bwd_hi = up(hi);
+        t.bwd_lo = up(lo);
+      }
+      l.tc.push_back(t);
+    }
     return l;
   };
   auto get_radial = [&](const std::string &key, int depth, int outputs) {

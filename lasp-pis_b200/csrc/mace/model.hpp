@@ -15,9 +15,16 @@ namespace mace {
 struct LinearPath {
   int in_offset, out_offset, in_mul, out_mul, dim, weight_offset;
 };
+// Tensor-core copies of one path's weight W [in_mul][out_mul], split as W = hi + lo with hi
+// rounded to tf32: forward planes are K-major for Y = X W ([out_mul][in_mul]), backward
+// planes for X_grad = Y_grad W^T ([in_mul][out_mul]).  Null when the shape is not eligible.
+struct TCWeights {
+  const float *fwd_hi = nullptr, *fwd_lo = nullptr, *bwd_hi = nullptr, *bwd_lo = nullptr;
+};
 struct Linear {
   int input = 0, output = 0;
   std::vector<LinearPath> paths;
+  std::vector<TCWeights> tc;     // per path
   const float *weight = nullptr; // device, [in_mul][out_mul] per path
 };
 // Radial MLP weights, transposed at load for coalesced per-unit access.
@@ -94,8 +101,18 @@ void launch_message_backward(cudaStream_t, int layer, const lapis::DeviceGeometr
 void launch_force_gather(cudaStream_t, const lapis::DeviceGeometry &, const float4 *edge_force, float *force,
                          float *virial);
 
+// Equivariant linear over n nodes: Y (+)= X W per path and component, or the transposed
+// product for the backward.  Paths with tensor-core-eligible shapes run on tc_gemm.
 void linear(cudaStream_t, int n, const Linear &, const float *x, float *y, bool backward = false,
-            bool add = false);
+            bool add = false, int *status = nullptr);
+// Tensor-core GEMM (tc_gemm.cu): C[z] (+)= A[z] B, B = Bhi + Blo given K-major [N][K].
+bool tc_gemm_supported(int N, int K);
+void tc_gemm(cudaStream_t, int M, int N, int K, int batch, const float *A, long long strideA, const float *Bhi,
+             const float *Blo, float *C, int ldc, long long strideC, bool accumulate, int *status);
+// Host split of a weight matrix into tf32-rounded hi and the fp32 remainder lo.
+void split_tf32(const float *w, size_t count, float *hi, float *lo);
+// Use the tensor-core path in linear() (default true; MACE_SIMT_LINEARS=1 disables).
+bool tensor_core_linears();
 void launch_normalize_gate(cudaStream_t, int n, const float *raw, const float *res, const float *density,
                            float alpha, float beta, float scalar_scale, float gate_scale, float *pre,
                            float *gate);

@@ -13,6 +13,9 @@
 // normalisation VJP (backward); the reference launches them separately.
 #include "model.hpp"
 #include "../lapis/launch.cuh"
+#include <cstdlib>
+#include <string>
+#include <vector>
 
 namespace mace {
 namespace {
@@ -261,23 +264,44 @@ void launch_embed(cudaStream_t s, int n, const int *species, const float *embedd
     lapis::launch(embed_kernel, blocks_for(size_t(n) * 512, 256), 256, 0, s, n, species, embedding, x);
 }
 
-void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bool backward, bool add) {
+bool tensor_core_linears() {
+  static const bool on = [] {
+    const char *v = std::getenv("MACE_SIMT_LINEARS");
+    return !(v && v[0] == '1');
+  }();
+  return on;
+}
+
+void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bool backward, bool add, int *status) {
   if (!n)
     return;
   if (!add)
     lapis::check(cudaMemsetAsync(y, 0, size_t(n) * (backward ? l.input : l.output) * 4, s));
-  for (const auto &p : l.paths) {
+  bool tc = tensor_core_linears() && status;
+  for (size_t q = 0; q < l.paths.size(); ++q) {
+    const auto &p = l.paths[q];
     const float *w = l.weight + p.weight_offset;
+    const TCWeights &t = l.tc[q];
     if (!backward) {
+      if (tc && t.fwd_hi) {
+        tc_gemm(s, n, p.out_mul, p.in_mul, p.dim, x + size_t(p.in_offset) * n, (long long)n * p.in_mul, t.fwd_hi,
+                t.fwd_lo, y + size_t(p.out_offset) * n, p.out_mul, (long long)n * p.out_mul, true, status);
+        continue;
+      }
       dim3 grid((p.out_mul + BN - 1) / BN, (n + BM - 1) / BM, p.dim);
-      lapis::launch(gemm_kernel<false>, grid, 256, 0, s, n, p.out_mul, p.in_mul, x + size_t(p.in_offset) * n, p.in_mul,
-                                              (long long)n * p.in_mul, w, p.out_mul, y + size_t(p.out_offset) * n,
-                                              p.out_mul, (long long)n * p.out_mul);
+      lapis::launch(gemm_kernel<false>, grid, 256, 0, s, n, p.out_mul, p.in_mul, x + size_t(p.in_offset) * n,
+                    p.in_mul, (long long)n * p.in_mul, w, p.out_mul, y + size_t(p.out_offset) * n, p.out_mul,
+                    (long long)n * p.out_mul);
     } else {
+      if (tc && t.bwd_hi) {
+        tc_gemm(s, n, p.in_mul, p.out_mul, p.dim, x + size_t(p.out_offset) * n, (long long)n * p.out_mul,
+                t.bwd_hi, t.bwd_lo, y + size_t(p.in_offset) * n, p.in_mul, (long long)n * p.in_mul, true, status);
+        continue;
+      }
       dim3 grid((p.in_mul + BN - 1) / BN, (n + BM - 1) / BM, p.dim);
-      lapis::launch(gemm_kernel<true>, grid, 256, 0, s, n, p.in_mul, p.out_mul, x + size_t(p.out_offset) * n, p.out_mul,
-                                             (long long)n * p.out_mul, w, p.out_mul, y + size_t(p.in_offset) * n,
-                                             p.in_mul, (long long)n * p.in_mul);
+      lapis::launch(gemm_kernel<true>, grid, 256, 0, s, n, p.in_mul, p.out_mul, x + size_t(p.out_offset) * n,
+                    p.out_mul, (long long)n * p.out_mul, w, p.out_mul, y + size_t(p.in_offset) * n, p.in_mul,
+                    (long long)n * p.in_mul);
     }
   }
 }
@@ -317,3 +341,58 @@ void launch_readout_act(cudaStream_t s, int count, const float *x, const float *
     lapis::launch(readout_act_kernel, blocks_for(count, 256), 256, 0, s, count, x, grad, y, scale, backward);
 }
 } // namespace mace
+
+namespace lapis {
+void set_c_api_error(const std::string &message);
+}
+
+extern "C" int mace_debug_gemm(int M, int N, int K, int batch, const float *A, const float *B, float *C,
+                               int accumulate, int mode) {
+  using namespace mace;
+  float *hi = nullptr, *lo = nullptr;
+  int *status = nullptr;
+  try {
+    lapis::set_c_api_error("");
+    if (M < 0 || N <= 0 || K <= 0 || batch <= 0 || !A || !B || !C)
+      throw lapis::Error("Invalid GEMM arguments");
+    if (mode == 0) {
+      if (!accumulate)
+        lapis::check(cudaMemset(C, 0, size_t(batch) * M * N * 4));
+      dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, batch);
+      lapis::launch(gemm_kernel<false>, grid, 256, 0, cudaStream_t(0), M, N, K, A, K, (long long)M * K, B, N, C, N,
+                    (long long)M * N);
+    } else {
+      std::vector<float> b(size_t(K) * N), bt(b.size()), h(b.size()), l(b.size());
+      lapis::check(cudaMemcpy(b.data(), B, b.size() * 4, cudaMemcpyDeviceToHost));
+      for (int k = 0; k < K; ++k)
+        for (int n = 0; n < N; ++n)
+          bt[size_t(n) * K + k] = b[size_t(k) * N + n];
+      split_tf32(bt.data(), bt.size(), h.data(), l.data());
+      lapis::check(cudaMalloc(&hi, h.size() * 4));
+      lapis::check(cudaMalloc(&lo, l.size() * 4));
+      lapis::check(cudaMalloc(&status, 4));
+      lapis::check(cudaMemcpy(hi, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
+      lapis::check(cudaMemcpy(lo, l.data(), l.size() * 4, cudaMemcpyHostToDevice));
+      lapis::check(cudaMemset(status, 0, 4));
+      tc_gemm(cudaStream_t(0), M, N, K, batch, A, (long long)M * K, hi, lo, C, N, (long long)M * N, accumulate != 0,
+              status);
+    }
+    lapis::check(cudaGetLastError());
+    lapis::check(cudaDeviceSynchronize());
+    int st = 0;
+    if (status)
+      lapis::check(cudaMemcpy(&st, status, 4, cudaMemcpyDeviceToHost));
+    cudaFree(hi);
+    cudaFree(lo);
+    cudaFree(status);
+    if (st)
+      throw lapis::Error("tensor-core GEMM reported status " + std::to_string(st));
+    return 0;
+  } catch (const std::exception &e) {
+    cudaFree(hi);
+    cudaFree(lo);
+    cudaFree(status);
+    lapis::set_c_api_error(e.what());
+    return -1;
+  }
+}

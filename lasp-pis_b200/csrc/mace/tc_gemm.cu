@@ -1,0 +1,326 @@
+// FP32-accurate GEMM on the Blackwell tensor cores (tcgen05, kind::tf32, 3-term split).
+//
+//   C[z] (+)= A[z] * B      A: [M][K] fp32 row-major per batch z (node features),
+//                           B: given as two K-major tf32 planes Bhi/Blo [N][K] with
+//                              B = Bhi + Blo (split once at model load).
+// Each A tile is split on the fly into hi = round_tf32(a) and lo = a - hi, and the tile
+// product is accumulated in TMEM as  A_hi*B_hi + A_lo*B_hi + A_hi*B_lo  (the dropped
+// A_lo*B_lo term is below 2^-22 relative), so the result carries FP32-level error while the
+// work runs on the tensor pipe.
+//
+// CTA = 6 warps, one 128 x 128 output tile:
+//   warp 0      TMA producer (A, Bhi, Blo per 32-wide K slab, SWIZZLE_128B, 3-stage ring)
+//   warp 1      MMA issuer (one elected thread; UMMA 128 x 128 x 8, accumulator in TMEM)
+//   warps 2..5  split A into hi/lo in shared memory, then the epilogue (TMEM -> registers
+//               -> C, adding to C when accumulate is set)
+// Every mbarrier wait is bounded: on time-out the CTA records an error code in *status,
+// stops issuing work, waits (bounded) for issued MMAs and frees its TMEM.
+#include "../lapis/launch.cuh"
+#include "model.hpp"
+#include <cuda.h>
+#include <mutex>
+
+namespace mace {
+namespace {
+constexpr int kBM = 128, kBN = 128, kBK = 32, kStages = 3;
+constexpr int kTileBytes = kBM * kBK * 4;        // 16 KiB (A, A_lo, Bhi, Blo tiles are equal)
+constexpr int kStageBytes = 4 * kTileBytes;      // A | A_lo | Bhi | Blo
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 /* align */ + 256 /* barriers */;
+constexpr int kThreads = 192;
+constexpr long long kWaitCycles = 1000000000ll;   // bounded wait: ~0.5 s of SM clock
+constexpr int kStatusGemmTimeout = 7;
+
+__device__ __forceinline__ unsigned smem_u32(const void *p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(unsigned bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(unsigned bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(unsigned bar, unsigned parity) {
+  unsigned ok;
+  asm volatile("{\n\t.reg .pred p;\n\t"
+               "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+               "selp.u32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok)
+               : "r"(bar), "r"(parity)
+               : "memory");
+  return ok != 0;
+}
+// Bounded wait; returns false (and flags the CTA) on time-out.
+__device__ __forceinline__ bool mbar_wait(unsigned bar, unsigned parity, volatile int *abort_flag) {
+  long long start = clock64();
+  for (unsigned it = 1;; ++it) {
+    if (mbar_try(bar, parity))
+      return true;
+    if (*abort_flag)
+      return false;
+    if (!(it & 255) && clock64() - start > kWaitCycles) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_3d(unsigned dst, const CUtensorMap *map, int x, int y, int z,
+                                            unsigned bar) {
+  asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+               "[%5];" ::"r"(dst),
+               "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(unsigned dst, const CUtensorMap *map, int x, int y, unsigned bar) {
+  asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+               "[%4];" ::"r"(dst),
+               "l"(map), "r"(x), "r"(y), "r"(bar)
+               : "memory");
+}
+// Shared-memory matrix descriptor: K-major, SWIZZLE_128B, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t smem_desc(unsigned addr) {
+  uint64_t d = 0;
+  d |= uint64_t((addr >> 4) & 0x3fff);      // start address
+  d |= uint64_t(1) << 16;                   // leading byte offset (unused for swizzled K-major)
+  d |= uint64_t(1024 >> 4) << 32;           // stride byte offset
+  d |= uint64_t(1) << 46;                   // descriptor version (sm_100)
+  d |= uint64_t(2) << 61;                   // SWIZZLE_128B
+  return d;
+}
+// Instruction descriptor: D fp32, A/B tf32, both K-major, M = 128, N = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(kBN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
+
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile("{\n\t.reg .pred p;\n\t"
+               "setp.ne.b32 p, %4, 0;\n\t"
+               "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+               "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit(unsigned bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+               "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                 "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                 "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+                 "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+                 "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int k = 0; k < 32; ++k)
+    v[k] = __uint_as_float(r[k]);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBhi,
+                   const __grid_constant__ CUtensorMap tmBlo, float *C, int ldc, long long strideC, int M, int N,
+                   int K, int accumulate, int *status) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
+  // bars: full[S] | lo_ready[S] | empty[S] | done
+  __shared__ uint32_t tmem_base;
+  __shared__ volatile int abort_flag;
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM, z = blockIdx.z;
+  int ktiles = K / kBK;
+  unsigned full0 = smem_u32(bars), lo0 = smem_u32(bars + kStages), empty0 = smem_u32(bars + 2 * kStages),
+           done = smem_u32(bars + 3 * kStages);
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(lo0 + 8 * s, 128);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(kBN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  uint32_t tmem = tmem_base;
+  __shared__ int mma_done_issued; // whether the final commit to `done` was issued
+  if (threadIdx.x == 0)
+    mma_done_issued = 0;
+  __syncthreads();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kt = 0; kt < ktiles; ++kt) {
+        int s = kt % kStages;
+        if (kt >= kStages && !mbar_wait(empty0 + 8 * s, ((kt / kStages) - 1) & 1, &abort_flag))
+          break;
+        unsigned base = smem_u32(smem + s * kStageBytes);
+        mbar_expect_tx(full0 + 8 * s, 3 * kTileBytes);
+        tma_load_3d(base, &tmA, kt * kBK, m0, z, full0 + 8 * s);
+        tma_load_2d(base + 2 * kTileBytes, &tmBhi, kt * kBK, n0, full0 + 8 * s);
+        tma_load_2d(base + 3 * kTileBytes, &tmBlo, kt * kBK, n0, full0 + 8 * s);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = true;
+      for (int kt = 0; kt < ktiles && ok; ++kt) {
+        int s = kt % kStages;
+        ok = mbar_wait(lo0 + 8 * s, (kt / kStages) & 1, &abort_flag);
+        if (!ok)
+          break;
+        tc_fence_after();
+        unsigned base = smem_u32(smem + s * kStageBytes);
+#pragma unroll
+        for (int j = 0; j < kBK / 8; ++j) {
+          uint64_t a_hi = smem_desc(base + 32 * j), a_lo = smem_desc(base + kTileBytes + 32 * j);
+          uint64_t b_hi = smem_desc(base + 2 * kTileBytes + 32 * j), b_lo = smem_desc(base + 3 * kTileBytes + 32 * j);
+          umma_tf32(tmem, a_hi, b_hi, (kt | j) ? 1u : 0u);
+          umma_tf32(tmem, a_lo, b_hi, 1u);
+          umma_tf32(tmem, a_hi, b_lo, 1u);
+        }
+        umma_commit(empty0 + 8 * s);
+      }
+      umma_commit(done);
+      mma_done_issued = 1;
+    }
+  } else {
+    // Split warps: A -> (hi, lo) in place / alongside, 32 floats per thread per stage.
+    int t = threadIdx.x - 64;
+    bool ok = true;
+    for (int kt = 0; kt < ktiles && ok; ++kt) {
+      int s = kt % kStages;
+      ok = mbar_wait(full0 + 8 * s, (kt / kStages) & 1, &abort_flag);
+      if (!ok)
+        break;
+      float4 *a = reinterpret_cast<float4 *>(smem + s * kStageBytes);
+      float4 *lo = reinterpret_cast<float4 *>(smem + s * kStageBytes + kTileBytes);
+#pragma unroll
+      for (int q = 0; q < kTileBytes / 16 / 128; ++q) {
+        float4 v = a[t + 128 * q], h, l;
+        h.x = __uint_as_float((__float_as_uint(v.x) + 0x1000u) & 0xffffe000u);
+        h.y = __uint_as_float((__float_as_uint(v.y) + 0x1000u) & 0xffffe000u);
+        h.z = __uint_as_float((__float_as_uint(v.z) + 0x1000u) & 0xffffe000u);
+        h.w = __uint_as_float((__float_as_uint(v.w) + 0x1000u) & 0xffffe000u);
+        l.x = v.x - h.x, l.y = v.y - h.y, l.z = v.z - h.z, l.w = v.w - h.w;
+        a[t + 128 * q] = h;
+        lo[t + 128 * q] = l;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(lo0 + 8 * s);
+    }
+    // Epilogue: TMEM lane = tile row; this warp owns rows 32 * (warp % 4) ...
+    bool go = ok && mbar_wait(done, 0, &abort_flag);
+    if (__all_sync(0xffffffffu, go)) {
+      tc_fence_after();
+      int quarter = warp & 3;
+      int row = m0 + quarter * 32 + lane;
+      float *crow = C + z * strideC + size_t(row) * ldc + n0;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kBN; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem + (uint32_t(quarter * 32) << 16) + uint32_t(c0), v);
+        if (row < M) {
+          float4 *dst = reinterpret_cast<float4 *>(crow + c0);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            float4 o = accumulate ? dst[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+            o.x += v[4 * q], o.y += v[4 * q + 1], o.z += v[4 * q + 2], o.w += v[4 * q + 3];
+            dst[q] = o;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (abort_flag && threadIdx.x == 0)
+    atomicCAS(status, 0, kStatusGemmTimeout);
+  if (warp == 1) {
+    if (abort_flag && mma_done_issued) {
+      // Drain: the final commit was issued; wait (bounded) for the MMAs before freeing TMEM.
+      long long start = clock64();
+      while (!mbar_try(done, 0) && clock64() - start < kWaitCycles) {
+      }
+    }
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBN));
+  }
+}
+
+using EncodeFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                              const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn encoder() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  });
+  if (!fn)
+    throw lapis::Error("cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+// Tensor map over `rows` x `cols` fp32 (row-major, ld = cols) [x `batch` planes when rank 3],
+// box 32 (cols) x 128 (rows) [x 1].
+CUtensorMap make_map(const float *base, int cols, int rows, int rank, int batch, long long batch_stride) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * 4) % 16 || (batch_stride * 4) % 16)
+    throw lapis::Error("tensor-core GEMM operand is not 16-byte aligned");
+  CUtensorMap map;
+  cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(rows), cuuint64_t(batch)};
+  cuuint64_t strides[2] = {cuuint64_t(cols) * 4, cuuint64_t(batch_stride) * 4};
+  cuuint32_t box[3] = {kBK, kBM, 1};
+  cuuint32_t elem[3] = {1, 1, 1};
+  CUresult r = encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, cuuint32_t(rank), const_cast<float *>(base), dims,
+                         strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw lapis::Error("cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+  return map;
+}
+} // namespace
+
+bool tc_gemm_supported(int N, int K) { return N % kBN == 0 && K % kBK == 0 && K >= kBK; }
+
+// C[z] (+)= A[z] * B  with B = Bhi + Blo given K-major ([N][K]); batch z = 0..batch-1.
+void tc_gemm(cudaStream_t s, int M, int N, int K, int batch, const float *A, long long strideA, const float *Bhi,
+             const float *Blo, float *C, int ldc, long long strideC, bool accumulate, int *status) {
+  if (!M || !batch)
+    return;
+  if (!tc_gemm_supported(N, K))
+    throw lapis::Error("tensor-core GEMM shape unsupported");
+  if ((reinterpret_cast<uintptr_t>(C) & 15) || ldc % 4)
+    throw lapis::Error("tensor-core GEMM output is not 16-byte aligned");
+  // A as [batch][M][K] (always a rank-3 map: the kernel issues 3D loads); B as [N][K].
+  CUtensorMap ma = make_map(A, K, M, 3, batch, batch > 1 ? strideA : (long long)M * K);
+  CUtensorMap mh = make_map(Bhi, K, N, 2, 1, 0), ml = make_map(Blo, K, N, 2, 1, 0);
+  static thread_local int configured_device = -1;
+  int device = 0;
+  lapis::check(cudaGetDevice(&device));
+  if (configured_device != device) {
+    lapis::check(cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    configured_device = device;
+  }
+  dim3 grid(N / kBN, (M + kBM - 1) / kBM, batch);
+  lapis::launch(tc_gemm_kernel, grid, kThreads, kSmemBytes, s, ma, mh, ml, C, ldc, strideC, M, N, K,
+                int(accumulate), status);
+}
+} // namespace mace
