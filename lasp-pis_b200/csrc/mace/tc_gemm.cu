@@ -8,11 +8,18 @@
 // A_lo*B_lo term is below 2^-22 relative), so the result carries FP32-level error while the
 // work runs on the tensor pipe.
 //
+// The tensor pipe adds products into its accumulator with truncation toward zero, which
+// biases long accumulations coherently.  So the dominant A_hi*B_hi term is computed FRESH
+// for every K = 8 step into one of two TMEM buffers and drained into FP32 registers with
+// round-to-nearest adds (overlapping the next step), while the two correction terms, 2^-11
+// smaller, accumulate over all of K in a third TMEM buffer drained once at the end.
+//
 // CTA = 6 warps, one 128 x 128 output tile:
 //   warp 0      TMA producer (A, Bhi, Blo per 32-wide K slab, SWIZZLE_128B, 3-stage ring)
-//   warp 1      MMA issuer (one elected thread; UMMA 128 x 128 x 8, accumulator in TMEM)
-//   warps 2..5  split A into hi/lo in shared memory, then the epilogue (TMEM -> registers
-//               -> C, adding to C when accumulate is set)
+//   warp 1      MMA issuer (one elected thread; UMMA 128 x 128 x 8)
+//   warps 2..5  split A into hi/lo in shared memory, drain the hi*hi buffers into per-row
+//               FP32 registers, add the correction buffer, write the tile (adding to C
+//               when accumulate)
 // Every mbarrier wait is bounded: on time-out the CTA records an error code in *status,
 // stops issuing work, waits (bounded) for issued MMAs and frees its TMEM.
 #include "../lapis/launch.cuh"
@@ -26,6 +33,7 @@ constexpr int kBM = 128, kBN = 128, kBK = 32, kStages = 3;
 constexpr int kTileBytes = kBM * kBK * 4;        // 16 KiB (A, A_lo, Bhi, Blo tiles are equal)
 constexpr int kStageBytes = 4 * kTileBytes;      // A | A_lo | Bhi | Blo
 constexpr int kSmemBytes = kStages * kStageBytes + 1024 /* align */ + 256 /* barriers */;
+constexpr int kTmemCols = 4 * kBN; // hi*hi buffers 0/1, correction buffer at 2 (512 columns)
 constexpr int kThreads = 192;
 constexpr long long kWaitCycles = 1000000000ll;   // bounded wait: ~0.5 s of SM clock
 constexpr int kStatusGemmTimeout = 7;
@@ -127,14 +135,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
-  // bars: full[S] | lo_ready[S] | empty[S] | done
+  // bars: full[S] | lo_ready[S] | empty[S] | done | tmem_full[2] | tmem_free[2]
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM, z = blockIdx.z;
   int ktiles = K / kBK;
   unsigned full0 = smem_u32(bars), lo0 = smem_u32(bars + kStages), empty0 = smem_u32(bars + 2 * kStages),
-           done = smem_u32(bars + 3 * kStages);
+           done = smem_u32(bars + 3 * kStages), tfull0 = smem_u32(bars + 3 * kStages + 1),
+           tfree0 = smem_u32(bars + 3 * kStages + 3);
   if (threadIdx.x == 0) {
     abort_flag = 0;
     for (int s = 0; s < kStages; ++s) {
@@ -143,12 +152,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(empty0 + 8 * s, 1);
     }
     mbar_init(done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8 * b, 1);
+      mbar_init(tfree0 + 8 * b, 128);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
-                 "r"(kBN));
+                 "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -176,6 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       bool ok = true;
+      uint32_t corr = tmem + uint32_t(2 * kBN);
       for (int kt = 0; kt < ktiles && ok; ++kt) {
         int s = kt % kStages;
         ok = mbar_wait(lo0 + 8 * s, (kt / kStages) & 1, &abort_flag);
@@ -183,13 +197,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         tc_fence_after();
         unsigned base = smem_u32(smem + s * kStageBytes);
-#pragma unroll
+#pragma unroll 1
         for (int j = 0; j < kBK / 8; ++j) {
+          int g = kt * (kBK / 8) + j, b = g & 1;
+          if (g >= 2 && !(ok = mbar_wait(tfree0 + 8 * b, ((g >> 1) - 1) & 1, &abort_flag)))
+            break;
+          tc_fence_after();
           uint64_t a_hi = smem_desc(base + 32 * j), a_lo = smem_desc(base + kTileBytes + 32 * j);
           uint64_t b_hi = smem_desc(base + 2 * kTileBytes + 32 * j), b_lo = smem_desc(base + 3 * kTileBytes + 32 * j);
-          umma_tf32(tmem, a_hi, b_hi, (kt | j) ? 1u : 0u);
-          umma_tf32(tmem, a_lo, b_hi, 1u);
-          umma_tf32(tmem, a_hi, b_lo, 1u);
+          umma_tf32(tmem + uint32_t(b * kBN), a_hi, b_hi, 0u);
+          umma_tf32(corr, a_lo, b_hi, g ? 1u : 0u);
+          umma_tf32(corr, a_hi, b_lo, 1u);
+          umma_commit(tfull0 + 8 * b);
         }
         umma_commit(empty0 + 8 * s);
       }
@@ -197,14 +216,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_done_issued = 1;
     }
   } else {
-    // Split warps: A -> (hi, lo) in place / alongside, 32 floats per thread per stage.
-    int t = threadIdx.x - 64;
+    // Split warps: A -> (hi, lo), 32 floats per thread per stage; after converting slab kt,
+    // drain the hi*hi products of slab kt - 1 (4 steps) so the MMAs of kt overlap the drain.
+    int t = threadIdx.x - 64, quarter = warp & 3;
+    uint32_t lane_addr = tmem + (uint32_t(quarter * 32) << 16);
+    float acc[kBN];
+#pragma unroll
+    for (int c = 0; c < kBN; ++c)
+      acc[c] = 0.f;
     bool ok = true;
+    auto drain = [&](uint32_t col, uint32_t bar, int parity, bool release) {
+      bool go = bar ? mbar_wait(bar, parity, &abort_flag) : true;
+      if (!__all_sync(0xffffffffu, go))
+        return false;
+      tc_fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < kBN; c0 += 32) {
+        float v[32];
+        tmem_ld32(lane_addr + col + uint32_t(c0), v);
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+          acc[c0 + k] += v[k];
+      }
+      tc_fence_before();
+      if (release)
+        mbar_arrive(tfree0 + 8 * ((col / kBN) & 1));
+      return true;
+    };
+    auto drain_slab = [&](int kt) {
+      for (int j = 0; j < kBK / 8; ++j) {
+        int g = kt * (kBK / 8) + j, b = g & 1;
+        if (!drain(uint32_t(b * kBN), tfull0 + 8 * b, (g >> 1) & 1, true))
+          return false;
+      }
+      return true;
+    };
     for (int kt = 0; kt < ktiles && ok; ++kt) {
       int s = kt % kStages;
       ok = mbar_wait(full0 + 8 * s, (kt / kStages) & 1, &abort_flag);
-      if (!ok)
+      if (!__all_sync(0xffffffffu, ok)) {
+        ok = false;
         break;
+      }
       float4 *a = reinterpret_cast<float4 *>(smem + s * kStageBytes);
       float4 *lo = reinterpret_cast<float4 *>(smem + s * kStageBytes + kTileBytes);
 #pragma unroll
@@ -220,26 +273,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(lo0 + 8 * s);
+      if (kt > 0)
+        ok = drain_slab(kt - 1);
     }
-    // Epilogue: TMEM lane = tile row; this warp owns rows 32 * (warp % 4) ...
-    bool go = ok && mbar_wait(done, 0, &abort_flag);
-    if (__all_sync(0xffffffffu, go)) {
-      tc_fence_after();
-      int quarter = warp & 3;
+    if (ok)
+      ok = drain_slab(ktiles - 1);
+    if (ok)
+      ok = drain(uint32_t(2 * kBN), done, 0, false);
+    if (__all_sync(0xffffffffu, ok)) {
       int row = m0 + quarter * 32 + lane;
-      float *crow = C + z * strideC + size_t(row) * ldc + n0;
-#pragma unroll 1
-      for (int c0 = 0; c0 < kBN; c0 += 32) {
-        float v[32];
-        tmem_ld32(tmem + (uint32_t(quarter * 32) << 16) + uint32_t(c0), v);
-        if (row < M) {
-          float4 *dst = reinterpret_cast<float4 *>(crow + c0);
+      if (row < M) {
+        float4 *dst = reinterpret_cast<float4 *>(C + z * strideC + size_t(row) * ldc + n0);
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            float4 o = accumulate ? dst[q] : make_float4(0.f, 0.f, 0.f, 0.f);
-            o.x += v[4 * q], o.y += v[4 * q + 1], o.z += v[4 * q + 2], o.w += v[4 * q + 3];
-            dst[q] = o;
-          }
+        for (int q = 0; q < kBN / 4; ++q) {
+          float4 o = accumulate ? dst[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+          o.x += acc[4 * q], o.y += acc[4 * q + 1], o.z += acc[4 * q + 2], o.w += acc[4 * q + 3];
+          dst[q] = o;
         }
       }
     }
@@ -256,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
 }
 
