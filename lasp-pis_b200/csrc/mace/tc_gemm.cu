@@ -9,10 +9,11 @@
 // work runs on the tensor pipe.
 //
 // The tensor pipe adds products into its accumulator with truncation toward zero, which
-// biases long accumulations coherently.  So the dominant A_hi*B_hi term is computed FRESH
-// for every K = 8 step into one of two TMEM buffers and drained into FP32 registers with
-// round-to-nearest adds (overlapping the next step), while the two correction terms, 2^-11
-// smaller, accumulate over all of K in a third TMEM buffer drained once at the end.
+// biases long accumulations coherently.  So the dominant A_hi*B_hi term is accumulated
+// FRESH for every 32-wide K slab (4 MMAs) into one of two TMEM buffers and drained into
+// FP32 registers with round-to-nearest adds (overlapping the next slab), while the two
+// correction terms, 2^-11 smaller, accumulate over all of K in a third TMEM buffer drained
+// once at the end.
 //
 // CTA = 6 warps, one 128 x 128 output tile:
 //   warp 0      TMA producer (A, Bhi, Blo per 32-wide K slab, SWIZZLE_128B, 3-stage ring)
@@ -197,19 +198,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         tc_fence_after();
         unsigned base = smem_u32(smem + s * kStageBytes);
-#pragma unroll 1
+        int b = kt & 1;
+        if (kt >= 2 && !(ok = mbar_wait(tfree0 + 8 * b, ((kt >> 1) - 1) & 1, &abort_flag)))
+          break;
+        tc_fence_after();
+#pragma unroll
         for (int j = 0; j < kBK / 8; ++j) {
-          int g = kt * (kBK / 8) + j, b = g & 1;
-          if (g >= 2 && !(ok = mbar_wait(tfree0 + 8 * b, ((g >> 1) - 1) & 1, &abort_flag)))
-            break;
-          tc_fence_after();
           uint64_t a_hi = smem_desc(base + 32 * j), a_lo = smem_desc(base + kTileBytes + 32 * j);
           uint64_t b_hi = smem_desc(base + 2 * kTileBytes + 32 * j), b_lo = smem_desc(base + 3 * kTileBytes + 32 * j);
-          umma_tf32(tmem + uint32_t(b * kBN), a_hi, b_hi, 0u);
-          umma_tf32(corr, a_lo, b_hi, g ? 1u : 0u);
+          umma_tf32(tmem + uint32_t(b * kBN), a_hi, b_hi, j ? 1u : 0u);
+          umma_tf32(corr, a_lo, b_hi, (kt | j) ? 1u : 0u);
           umma_tf32(corr, a_hi, b_lo, 1u);
-          umma_commit(tfull0 + 8 * b);
         }
+        umma_commit(tfull0 + 8 * b);
         umma_commit(empty0 + 8 * s);
       }
       umma_commit(done);
@@ -217,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // Split warps: A -> (hi, lo), 32 floats per thread per stage; after converting slab kt,
-    // drain the hi*hi products of slab kt - 1 (4 steps) so the MMAs of kt overlap the drain.
+    // drain the hi*hi products of slab kt - 1 so the MMAs of kt overlap the drain.
     int t = threadIdx.x - 64, quarter = warp & 3;
     uint32_t lane_addr = tmem + (uint32_t(quarter * 32) << 16);
     float acc[kBN];
@@ -244,12 +245,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
     auto drain_slab = [&](int kt) {
-      for (int j = 0; j < kBK / 8; ++j) {
-        int g = kt * (kBK / 8) + j, b = g & 1;
-        if (!drain(uint32_t(b * kBN), tfull0 + 8 * b, (g >> 1) & 1, true))
-          return false;
-      }
-      return true;
+      int b = kt & 1;
+      return drain(uint32_t(b * kBN), tfull0 + 8 * b, (kt >> 1) & 1, true);
     };
     for (int kt = 0; kt < ktiles && ok; ++kt) {
       int s = kt % kStages;

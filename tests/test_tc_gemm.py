@@ -33,3 +33,22 @@ def test_gemm_matches_fp64(library, shape, mode):
         scale = A.double().abs() @ B.double().abs() + (C0.double().abs() if accumulate else 0)
         err = ((C.double() - ref).abs() / scale).max().item()
         assert err < 1e-6, (shape, mode, accumulate, err)
+
+
+def test_tensor_core_error_close_to_fp32(library):
+    """RMS error of the tensor-core GEMM within 4x that of the FP32 SIMT kernel (K = 2048)."""
+    import torch
+    lib = ct.CDLL(str(library))
+    lib.mace_debug_gemm.argtypes = [ct.c_int] * 4 + [ct.c_void_p] * 3 + [ct.c_int, ct.c_int]
+    M, N, K = 2000, 256, 2048
+    g = torch.Generator(device="cuda").manual_seed(5)
+    A = torch.randn(1, M, K, device="cuda", generator=g)
+    B = torch.randn(K, N, device="cuda", generator=g) / K ** 0.5
+    ref = A.double() @ B.double()
+    rms = []
+    for mode in (0, 1):
+        C = torch.zeros(1, M, N, device="cuda")
+        assert lib.mace_debug_gemm(M, N, K, 1, A.data_ptr(), B.data_ptr(), C.data_ptr(), 0, mode) == 0
+        rms.append(((C.double() - ref) ** 2).mean().sqrt().item() / ref.abs().mean().item())
+    print("relative rms error simt %.3e tcgen05 %.3e" % tuple(rms))
+    assert rms[1] <= 4 * rms[0] + 1e-8, rms
