@@ -25,108 +25,26 @@
 // stops issuing work, waits (bounded) for issued MMAs and frees its TMEM.
 #include "../lapis/launch.cuh"
 #include "model.hpp"
+#include "tcgen05.cuh"
 #include <cuda.h>
 #include <mutex>
 
 namespace mace {
 namespace {
+using namespace tc;
 constexpr int kBM = 128, kBN = 128, kBK = 32, kStages = 3;
 constexpr int kTileBytes = kBM * kBK * 4;        // 16 KiB (A, A_lo, Bhi, Blo tiles are equal)
 constexpr int kStageBytes = 4 * kTileBytes;      // A | A_lo | Bhi | Blo
 constexpr int kSmemBytes = kStages * kStageBytes + 1024 /* align */ + 256 /* barriers */;
 constexpr int kTmemCols = 4 * kBN; // hi*hi buffers 0/1, correction buffer at 2 (512 columns)
 constexpr int kThreads = 192;
-constexpr long long kWaitCycles = 1000000000ll;   // bounded wait: ~0.5 s of SM clock
 constexpr int kStatusGemmTimeout = 7;
 
-__device__ __forceinline__ unsigned smem_u32(const void *p) {
-  return static_cast<unsigned>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(unsigned bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(unsigned bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(unsigned bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(unsigned bar, unsigned parity) {
-  unsigned ok;
-  asm volatile("{\n\t.reg .pred p;\n\t"
-               "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-               "selp.u32 %0, 1, 0, p;\n\t}"
-               : "=r"(ok)
-               : "r"(bar), "r"(parity)
-               : "memory");
-  return ok != 0;
-}
-// Bounded wait; returns false (and flags the CTA) on time-out.
-__device__ __forceinline__ bool mbar_wait(unsigned bar, unsigned parity, volatile int *abort_flag) {
-  long long start = clock64();
-  for (unsigned it = 1;; ++it) {
-    if (mbar_try(bar, parity))
-      return true;
-    if (*abort_flag)
-      return false;
-    if (!(it & 255) && clock64() - start > kWaitCycles) {
-      *abort_flag = 1;
-      return false;
-    }
-  }
-}
-__device__ __forceinline__ void tma_load_3d(unsigned dst, const CUtensorMap *map, int x, int y, int z,
-                                            unsigned bar) {
-  asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-               "[%5];" ::"r"(dst),
-               "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
-               : "memory");
-}
-__device__ __forceinline__ void tma_load_2d(unsigned dst, const CUtensorMap *map, int x, int y, unsigned bar) {
-  asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-               "[%4];" ::"r"(dst),
-               "l"(map), "r"(x), "r"(y), "r"(bar)
-               : "memory");
-}
-// Shared-memory matrix descriptor: K-major, SWIZZLE_128B, 8-row groups 1024 B apart.
-__device__ __forceinline__ uint64_t smem_desc(unsigned addr) {
-  uint64_t d = 0;
-  d |= uint64_t((addr >> 4) & 0x3fff);      // start address
-  d |= uint64_t(1) << 16;                   // leading byte offset (unused for swizzled K-major)
-  d |= uint64_t(1024 >> 4) << 32;           // stride byte offset
-  d |= uint64_t(1) << 46;                   // descriptor version (sm_100)
-  d |= uint64_t(2) << 61;                   // SWIZZLE_128B
-  return d;
-}
 // Instruction descriptor: D fp32, A/B tf32, both K-major, M = 128, N = 128.
 constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(kBN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
 
 __device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
-  asm volatile("{\n\t.reg .pred p;\n\t"
-               "setp.ne.b32 p, %4, 0;\n\t"
-               "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-               "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate));
-}
-__device__ __forceinline__ void umma_commit(unsigned bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-               "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                 "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-                 "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-                 "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
-                 "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-               : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int k = 0; k < 32; ++k)
-    v[k] = __uint_as_float(r[k]);
+  umma_tf32_desc(tmem_d, a, b, kIdesc, accumulate);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
