@@ -123,7 +123,10 @@ Result MH1::evaluate() {
     linear(s, n, l.skip, input, skip, false, false, status);
     launch_radial(s, c.geometry, l, pair, ea, ro[k]);
     timer.mark("forward" + std::to_string(k) + ".linears/radial");
-    launch_message_forward(s, k, c.geometry, l, ea, ro[k], up[k], msg, rho[k]);
+    if (tensor_core_edges())
+      launch_message_forward_tc(s, k, c.geometry, l, ea, ro[k], up[k], msg, rho[k]);
+    else
+      launch_message_forward(s, k, c.geometry, l, ea, ro[k], up[k], msg, rho[k]);
     timer.mark("forward" + std::to_string(k) + ".messages");
     linear(s, n, l.one, msg, raw[k], false, false, status);
     launch_normalize_gate(s, n, raw[k], res, rho[k], l.alpha, l.beta, cst[11], cst[12], pre[k], gate);
@@ -170,7 +173,10 @@ Result MH1::evaluate() {
     if (k == 1)
       linear(s, n, l.res, pregrad, upgrad, true, false, status);
     timer.mark("backward" + std::to_string(k) + ".node");
-    launch_message_backward(s, k, c.geometry, l, ea, ro[k], up[k], msggrad, rhograd, upgrad, edge_force, k == 0);
+    if (tensor_core_edges())
+      launch_message_backward_tc(s, k, c.geometry, l, ea, ro[k], up[k], msggrad, rhograd, upgrad, edge_force, k == 0);
+    else
+      launch_message_backward(s, k, c.geometry, l, ea, ro[k], up[k], msggrad, rhograd, upgrad, edge_force, k == 0);
     timer.mark("backward" + std::to_string(k) + ".edges");
     if (k == 1) {
       linear(s, n, l.skip, hgrad, hgrad0, true, false, status);

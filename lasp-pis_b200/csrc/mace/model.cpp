@@ -235,7 +235,14 @@ void ModelData::load(const std::string &path) {
       r.beta[k] = up(a.get<float>(key + "." + std::to_string(k * 3 + 1) + ".bias"));
     }
     std::string out = key + "." + std::to_string(depth * 3);
-    r.out_t = up(transposed(a.get<float>(out + ".weight"), outputs, 64, out + ".weight"));
+    auto ow = a.get<float>(out + ".weight");
+    r.out_t = up(transposed(ow, outputs, 64, out + ".weight"));
+    if (outputs % 128 == 0) {
+      std::vector<float> hi(ow.size()), lo(ow.size());
+      split_tf32(ow.data(), ow.size(), hi.data(), lo.data());
+      r.out_hi = up(hi);
+      r.out_lo = up(lo);
+    }
     r.out_b = up(a.get<float>(out + ".bias"));
     r.depth = depth;
     r.outputs = outputs;

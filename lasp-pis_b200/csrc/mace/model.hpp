@@ -7,6 +7,7 @@
 #pragma once
 #include "lapis/runtime.hpp"
 #include "tp_table.h"
+#include <cuda.h>
 #include <string>
 #include <vector>
 
@@ -36,6 +37,7 @@ struct Radial {
   const float *bias[3], *gamma[3], *beta[3];
   const float *out_t;           // [64][outputs]
   const float *out_b;           // [outputs]
+  const float *out_hi, *out_lo; // [outputs][64] tf32 split of the projection (tensor cores)
   int depth, outputs;
 };
 struct PolyTerm {
@@ -98,6 +100,14 @@ void launch_message_forward(cudaStream_t, int layer, const lapis::DeviceGeometry
 void launch_message_backward(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &,
                              EdgeArrays, RadialOut, const float *up, const float *message_grad,
                              const float *density_grad, float *up_grad, float4 *edge_force, bool accumulate);
+// Tensor-core versions (edge_tc.cu): same contracts as the SIMT launches above.
+void launch_message_forward_tc(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &, EdgeArrays,
+                               RadialOut, const float *up, float *message, float *density);
+void launch_message_backward_tc(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &,
+                                EdgeArrays, RadialOut, const float *up, const float *message_grad,
+                                const float *density_grad, float *up_grad, float4 *edge_force, bool accumulate);
+CUtensorMap tc_map_2d(const float *base, int cols, long long rows, int box_cols, int box_rows);
+bool tensor_core_edges();
 void launch_force_gather(cudaStream_t, const lapis::DeviceGeometry &, const float4 *edge_force, float *force,
                          float *virial);
 

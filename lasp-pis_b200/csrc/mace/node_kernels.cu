@@ -264,6 +264,14 @@ void launch_embed(cudaStream_t s, int n, const int *species, const float *embedd
     lapis::launch(embed_kernel, blocks_for(size_t(n) * 512, 256), 256, 0, s, n, species, embedding, x);
 }
 
+bool tensor_core_edges() {
+  static const bool on = [] {
+    const char *v = std::getenv("MACE_SIMT_EDGES");
+    return !(v && v[0] == '1');
+  }();
+  return on;
+}
+
 bool tensor_core_linears() {
   static const bool on = [] {
     const char *v = std::getenv("MACE_SIMT_LINEARS");

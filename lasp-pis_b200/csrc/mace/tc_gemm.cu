@@ -262,6 +262,22 @@ CUtensorMap make_map(const float *base, int cols, int rows, int rank, int batch,
 }
 } // namespace
 
+CUtensorMap tc_map_2d(const float *base, int cols, long long rows, int box_cols, int box_rows) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * 4) % 16 || box_cols * 4 > 128 || box_rows > 256)
+    throw lapis::Error("tensor map operand is not 16-byte aligned or the box is too large");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(cols) * 4};
+  cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
+  cuuint32_t elem[2] = {1, 1};
+  CUresult r = encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box,
+                         elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw lapis::Error("cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+  return map;
+}
+
 bool tc_gemm_supported(int N, int K) { return N % kBN == 0 && K % kBK == 0 && K >= kBK; }
 
 // C[z] (+)= A[z] * B  with B = Bhi + Blo given K-major ([N][K]); batch z = 0..batch-1.
