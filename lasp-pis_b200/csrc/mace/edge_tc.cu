@@ -196,13 +196,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             unsigned w = smem_u32(wring + st * 2 * kWSlab);
             uint32_t d = tmem + uint32_t(p * N);
+            // The tensor pipe truncates each accumulation toward zero, with an error relative
+            // to the accumulator: the small correction terms go first (K half 0: while the
+            // accumulator is small) and the dominant hi*hi terms after them.
+            if (kh == 0) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint64_t whi = smem_desc(w + 32 * j), wlo = smem_desc(w + kWSlab + 32 * j);
-              uint64_t bhi = smem_desc(b + kh * S::BREG + 32 * j), blo = smem_desc(b + (2 + kh) * S::BREG + 32 * j);
-              umma_tf32_desc(d, whi, bhi, S::IDESC, (kh | j) ? 1u : 0u);
-              umma_tf32_desc(d, wlo, bhi, S::IDESC, 1u);
-              umma_tf32_desc(d, whi, blo, S::IDESC, 1u);
+              for (int j = 0; j < 4; ++j) {
+                uint64_t whi = smem_desc(w + 32 * j), wlo = smem_desc(w + kWSlab + 32 * j);
+                uint64_t bhi = smem_desc(b + 32 * j), blo = smem_desc(b + 2 * S::BREG + 32 * j);
+                umma_tf32_desc(d, wlo, bhi, S::IDESC, j ? 1u : 0u);
+                umma_tf32_desc(d, whi, blo, S::IDESC, 1u);
+                umma_tf32_desc(d, whi, bhi, S::IDESC, 1u);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                uint64_t whi = smem_desc(w + 32 * j), wlo = smem_desc(w + kWSlab + 32 * j);
+                uint64_t bhi = smem_desc(b + S::BREG + 32 * j), blo = smem_desc(b + 3 * S::BREG + 32 * j);
+                umma_tf32_desc(d, wlo, bhi, S::IDESC, 1u);
+                umma_tf32_desc(d, whi, blo, S::IDESC, 1u);
+              }
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                uint64_t whi = smem_desc(w + 32 * j);
+                uint64_t bhi = smem_desc(b + S::BREG + 32 * j);
+                umma_tf32_desc(d, whi, bhi, S::IDESC, 1u);
+              }
             }
             umma_commit(wempty0 + 8 * st);
           }
