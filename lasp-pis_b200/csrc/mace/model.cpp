@@ -303,6 +303,11 @@ void ModelData::load(const std::string &path) {
           (t.degree >= 2 && (t.b < 0 || t.b >= 16)) || (t.degree == 3 && (t.c < 0 || t.c >= 16)))
         throw Error("Invalid MH1 polynomial index");
     l.poly = reinterpret_cast<const PolyTerm *>(device.upload(poly.data(), poly.size() * sizeof(PolyTerm)));
+    std::vector<int> packed;
+    for (auto t : poly)
+      packed.push_back(t.output | t.degree << 2 | t.a << 4 | (t.degree >= 2 ? t.b : 0) << 8 |
+                       (t.degree >= 3 ? t.c : 0) << 12);
+    l.poly_packed = reinterpret_cast<const int *>(device.upload(packed.data(), packed.size() * 4));
     l.pcoef = up(a.get<float>(p + ".product.coefficients"));
     l.plin = get_linear(p + ".product.linear", k ? 512 : 2048, k ? 512 : 2048);
   }

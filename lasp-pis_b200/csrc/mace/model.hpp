@@ -52,6 +52,7 @@ struct Layer {
   float alpha, beta;
   TPValues tp;
   const PolyTerm *poly; // device [npoly]
+  const int *poly_packed; // device [npoly]: out | degree << 2 | a << 4 | b << 8 | c << 12
   const float *pcoef;   // device [npoly][512]
   int npoly, pouts, paths, in_comp, out_comp;
 };

@@ -171,66 +171,103 @@ __global__ void __launch_bounds__(128) gate_norm_backward_kernel(int n, const fl
 }
 
 // Symmetric contraction: y[out][c] = sum_t coef[t][c] x[a][c] x[b][c] x[c'][c] (degree <= 3).
-__global__ void __launch_bounds__(128) product_kernel(int n, const PolyTerm *terms, const float *coef, int count,
+// CTA = 8 warps owning a 32-channel slice: the slice of every coefficient row and the packed
+// term table are staged in shared memory once, then each warp streams nodes (lane = channel)
+// with the node's 16 components in a per-warp shared array.  Terms are packed as
+// out | degree << 2 | a << 4 | b << 8 | c << 12 (b, c unused below the term's degree).
+constexpr int kProdWarps = 8, kProdNodes = 64;
+
+__global__ void __launch_bounds__(256) product_kernel(int n, const int *packed, const float *coef, int count,
                                                       int outputs, const float *x, float *y) {
-  __shared__ float v[16][128];
-  int t = threadIdx.x;
-  size_t q = size_t(blockIdx.x) * 128 + t;
-  int i = int(q / 512), c = int(q % 512);
+  extern __shared__ float ps[];
+  float *cs = ps;                                   // [count][32]
+  int *ts = reinterpret_cast<int *>(cs + count * 32); // [count]
+  float *vs = reinterpret_cast<float *>(ts + ((count + 3) & ~3)) + (threadIdx.x >> 5) * 16 * 32;
+  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, c0 = blockIdx.x * 32;
+  for (int k = threadIdx.x; k < count * 32; k += blockDim.x)
+    cs[k] = coef[size_t(k >> 5) * 512 + c0 + (k & 31)];
+  for (int k = threadIdx.x; k < count; k += blockDim.x)
+    ts[k] = packed[k];
+  __syncthreads();
+  int i0 = blockIdx.y * kProdNodes, i1 = min(n, i0 + kProdNodes);
+  for (int i = i0 + warp; i < i1; i += kProdWarps) {
 #pragma unroll
-  for (int m = 0; m < 16; ++m)
-    v[m][t] = x[(size_t(m) * n + i) * 512 + c];
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int k = 0; k < count; ++k) {
-    PolyTerm tm = terms[k];
-    float w = coef[size_t(k) * 512 + c];
-    float val = w * v[tm.a][t];
-    if (tm.degree >= 2)
-      val *= v[tm.b][t];
-    if (tm.degree >= 3)
-      val *= v[tm.c][t];
-    if (tm.output == 0)
-      acc[0] += val;
-    else if (tm.output == 1)
-      acc[1] += val;
-    else if (tm.output == 2)
-      acc[2] += val;
-    else
-      acc[3] += val;
+    for (int m = 0; m < 16; ++m)
+      vs[m * 32 + lane] = x[(size_t(m) * n + i) * 512 + c0 + lane];
+    __syncwarp();
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < count; ++k) {
+      int t = ts[k];
+      int out = t & 3, deg = (t >> 2) & 3;
+      float val = cs[k * 32 + lane] * vs[((t >> 4) & 15) * 32 + lane];
+      if (deg >= 2)
+        val *= vs[((t >> 8) & 15) * 32 + lane];
+      if (deg >= 3)
+        val *= vs[((t >> 12) & 15) * 32 + lane];
+      if (out == 0)
+        acc[0] += val;
+      else if (out == 1)
+        acc[1] += val;
+      else if (out == 2)
+        acc[2] += val;
+      else
+        acc[3] += val;
+    }
+    for (int o = 0; o < outputs; ++o)
+      y[(size_t(o) * n + i) * 512 + c0 + lane] = acc[o];
+    __syncwarp();
   }
-  for (int o = 0; o < outputs; ++o)
-    y[(size_t(o) * n + i) * 512 + c] = acc[o];
 }
 
-__global__ void __launch_bounds__(128) product_backward_kernel(int n, const PolyTerm *terms, const float *coef,
+__global__ void __launch_bounds__(256) product_backward_kernel(int n, const int *packed, const float *coef,
                                                                int count, int outputs, const float *x,
                                                                const float *grad, float *xg) {
-  __shared__ float v[16][128], g[16][128];
-  int t = threadIdx.x;
-  size_t q = size_t(blockIdx.x) * 128 + t;
-  int i = int(q / 512), c = int(q % 512);
+  extern __shared__ float ps[];
+  float *cs = ps;
+  int *ts = reinterpret_cast<int *>(cs + count * 32);
+  float *vs = reinterpret_cast<float *>(ts + ((count + 3) & ~3)) + (threadIdx.x >> 5) * 32 * 32;
+  float *gs = vs + 16 * 32;
+  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, c0 = blockIdx.x * 32;
+  for (int k = threadIdx.x; k < count * 32; k += blockDim.x)
+    cs[k] = coef[size_t(k >> 5) * 512 + c0 + (k & 31)];
+  for (int k = threadIdx.x; k < count; k += blockDim.x)
+    ts[k] = packed[k];
+  __syncthreads();
+  int i0 = blockIdx.y * kProdNodes, i1 = min(n, i0 + kProdNodes);
+  for (int i = i0 + warp; i < i1; i += kProdWarps) {
 #pragma unroll
-  for (int m = 0; m < 16; ++m) {
-    v[m][t] = x[(size_t(m) * n + i) * 512 + c];
-    g[m][t] = 0.f;
-  }
-  float G[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int o = 0; o < outputs; ++o)
-    G[o] = grad[(size_t(o) * n + i) * 512 + c];
-  for (int k = 0; k < count; ++k) {
-    PolyTerm tm = terms[k];
-    float gw = coef[size_t(k) * 512 + c] *
-               (tm.output == 0 ? G[0] : tm.output == 1 ? G[1] : tm.output == 2 ? G[2] : G[3]);
-    float a = v[tm.a][t], b = tm.degree >= 2 ? v[tm.b][t] : 1.f, d = tm.degree >= 3 ? v[tm.c][t] : 1.f;
-    g[tm.a][t] += gw * b * d;
-    if (tm.degree >= 2)
-      g[tm.b][t] += gw * a * d;
-    if (tm.degree >= 3)
-      g[tm.c][t] += gw * a * b;
-  }
+    for (int m = 0; m < 16; ++m) {
+      vs[m * 32 + lane] = x[(size_t(m) * n + i) * 512 + c0 + lane];
+      gs[m * 32 + lane] = 0.f;
+    }
+    float G[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int o = 0; o < outputs; ++o)
+      G[o] = grad[(size_t(o) * n + i) * 512 + c0 + lane];
+    __syncwarp();
+    for (int k = 0; k < count; ++k) {
+      int t = ts[k];
+      int out = t & 3, deg = (t >> 2) & 3, ia = (t >> 4) & 15, ib = (t >> 8) & 15, ic = (t >> 12) & 15;
+      float gw = cs[k * 32 + lane] * (out == 0 ? G[0] : out == 1 ? G[1] : out == 2 ? G[2] : G[3]);
+      float a = vs[ia * 32 + lane];
+      if (deg == 1) {
+        gs[ia * 32 + lane] += gw;
+      } else if (deg == 2) {
+        float b = vs[ib * 32 + lane];
+        gs[ia * 32 + lane] += gw * b;
+        gs[ib * 32 + lane] += gw * a;
+      } else {
+        float b = vs[ib * 32 + lane], d = vs[ic * 32 + lane];
+        gs[ia * 32 + lane] += gw * b * d;
+        gs[ib * 32 + lane] += gw * a * d;
+        gs[ic * 32 + lane] += gw * a * b;
+      }
+    }
+    __syncwarp();
 #pragma unroll
-  for (int m = 0; m < 16; ++m)
-    xg[(size_t(m) * n + i) * 512 + c] = g[m][t];
+    for (int m = 0; m < 16; ++m)
+      xg[(size_t(m) * n + i) * 512 + c0 + lane] = gs[m * 32 + lane];
+    __syncwarp();
+  }
 }
 
 __global__ void add_kernel(size_t count, const float *a, float *b, float scale) {
@@ -329,13 +366,27 @@ void launch_gate_norm_backward(cudaStream_t s, int n, const float *pre, const fl
     lapis::launch(gate_norm_backward_kernel, n, 128, 0, s, n, pre, raw, density, gate_grad, alpha, beta, scalar_scale,
                                                 gate_scale, pre_grad, raw_grad, density_grad);
 }
+size_t product_smem(int count, bool backward) {
+  return (size_t(count) * 32 + ((count + 3) & ~3)) * 4 + size_t(kProdWarps) * (backward ? 32 : 16) * 32 * 4;
+}
+
 void launch_product(cudaStream_t s, int n, const Layer &l, const float *x, float *y) {
-  if (n)
-    lapis::launch(product_kernel, n * 4, 128, 0, s, n, l.poly, l.pcoef, l.npoly, l.pouts, x, y);
+  if (!n)
+    return;
+  size_t smem = product_smem(l.npoly, false);
+  lapis::check(cudaFuncSetAttribute(product_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  dim3 grid(16, (n + kProdNodes - 1) / kProdNodes);
+  lapis::launch(product_kernel, grid, 256, smem, s, n, l.poly_packed, l.pcoef, l.npoly, l.pouts, x, y);
 }
 void launch_product_backward(cudaStream_t s, int n, const Layer &l, const float *x, const float *grad, float *xg) {
-  if (n)
-    lapis::launch(product_backward_kernel, n * 4, 128, 0, s, n, l.poly, l.pcoef, l.npoly, l.pouts, x, grad, xg);
+  if (!n)
+    return;
+  size_t smem = product_smem(l.npoly, true);
+  lapis::check(
+      cudaFuncSetAttribute(product_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  dim3 grid(16, (n + kProdNodes - 1) / kProdNodes);
+  lapis::launch(product_backward_kernel, grid, 256, smem, s, n, l.poly_packed, l.pcoef, l.npoly, l.pouts, x, grad,
+                xg);
 }
 void launch_add(cudaStream_t s, size_t count, const float *a, float *b, float scale) {
   if (count)
