@@ -302,13 +302,24 @@ void ModelData::load(const std::string &path) {
       if (t.degree < 1 || t.degree > 3 || t.output < 0 || t.output >= l.pouts || t.a < 0 || t.a >= 16 ||
           (t.degree >= 2 && (t.b < 0 || t.b >= 16)) || (t.degree == 3 && (t.c < 0 || t.c >= 16)))
         throw Error("Invalid MH1 polynomial index");
-    l.poly = reinterpret_cast<const PolyTerm *>(device.upload(poly.data(), poly.size() * sizeof(PolyTerm)));
-    std::vector<int> packed;
-    for (auto t : poly)
-      packed.push_back(t.output | t.degree << 2 | t.a << 4 | (t.degree >= 2 ? t.b : 0) << 8 |
-                       (t.degree >= 3 ? t.c : 0) << 12);
-    l.poly_packed = reinterpret_cast<const int *>(device.upload(packed.data(), packed.size() * 4));
-    l.pcoef = up(a.get<float>(p + ".product.coefficients"));
+    {
+      auto coef = a.get<float>(p + ".product.coefficients");
+      std::vector<int> abc;
+      std::vector<float> sorted;
+      int starts[4];
+      for (int o = 0; o < 4; ++o) {
+        starts[o] = int(abc.size());
+        for (size_t t = 0; t < poly.size(); ++t)
+          if (poly[t].output == o) {
+            const auto &q = poly[t];
+            abc.push_back(q.a | (q.degree >= 2 ? q.b : 16) << 8 | (q.degree >= 3 ? q.c : 16) << 16);
+            sorted.insert(sorted.end(), coef.begin() + t * 512, coef.begin() + (t + 1) * 512);
+          }
+      }
+      l.poly_out_start = make_int4(starts[0], starts[1], starts[2], starts[3]);
+      l.poly_abc = reinterpret_cast<const int *>(device.upload(abc.data(), abc.size() * 4));
+      l.poly_coef_sorted = up(sorted);
+    }
     l.plin = get_linear(p + ".product.linear", k ? 512 : 2048, k ? 512 : 2048);
   }
   read0 = get_linear("readout0", 2048, 1);

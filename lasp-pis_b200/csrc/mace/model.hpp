@@ -51,9 +51,12 @@ struct Layer {
   Radial radial, density;
   float alpha, beta;
   TPValues tp;
-  const PolyTerm *poly; // device [npoly]
-  const int *poly_packed; // device [npoly]: out | degree << 2 | a << 4 | b << 8 | c << 12
-  const float *pcoef;   // device [npoly][512]
+  // Terms sorted by output (stable): factor indices a | b << 8 | c << 16 with missing
+  // factors = 16 (a constant 1), coefficient rows in the same order, and the first term of
+  // each output (entries past `pouts` equal npoly).
+  const int *poly_abc;
+  const float *poly_coef_sorted;
+  int4 poly_out_start;
   int npoly, pouts, paths, in_comp, out_comp;
 };
 

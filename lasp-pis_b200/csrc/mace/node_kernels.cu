@@ -171,68 +171,77 @@ __global__ void __launch_bounds__(128) gate_norm_backward_kernel(int n, const fl
 }
 
 // Symmetric contraction: y[out][c] = sum_t coef[t][c] x[a][c] x[b][c] x[c'][c] (degree <= 3).
-// CTA = 8 warps owning a 32-channel slice: the slice of every coefficient row and the packed
-// term table are staged in shared memory once, then each warp streams nodes (lane = channel)
-// with the node's 16 components in a per-warp shared array.  Terms are packed as
-// out | degree << 2 | a << 4 | b << 8 | c << 12 (b, c unused below the term's degree).
-constexpr int kProdWarps = 8, kProdNodes = 64;
+// CTA = 8 warps owning a 32-channel slice: the slice of every coefficient row and the term
+// table are staged in shared memory once, then each warp streams nodes (lane = channel) with
+// the node's 16 components plus a constant 1 (index 16) in a per-warp shared array.  Terms
+// are sorted by output at load and their missing factors point at the constant, so every
+// term is the same branch-free coef * v[a] * v[b] * v[c]; four independent partial sums keep
+// the dependent shared-memory loads overlapped.
+constexpr int kProdWarps = 8, kProdNodes = 64, kProdV = 17;
 
-__global__ void __launch_bounds__(256) product_kernel(int n, const int *packed, const float *coef, int count,
-                                                      int outputs, const float *x, float *y) {
+__global__ void __launch_bounds__(256) product_kernel(int n, const int *abc, const float *coef, int count,
+                                                      const int4 out_start, int outputs, const float *x, float *y) {
   extern __shared__ float ps[];
-  float *cs = ps;                                   // [count][32]
-  int *ts = reinterpret_cast<int *>(cs + count * 32); // [count]
-  float *vs = reinterpret_cast<float *>(ts + ((count + 3) & ~3)) + (threadIdx.x >> 5) * 16 * 32;
+  float *cs = ps;                                     // [count][32]
+  int *ts = reinterpret_cast<int *>(cs + count * 32); // [count]  a | b << 8 | c << 16
+  float *vs = reinterpret_cast<float *>(ts + ((count + 3) & ~3)) + (threadIdx.x >> 5) * kProdV * 32;
   int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, c0 = blockIdx.x * 32;
   for (int k = threadIdx.x; k < count * 32; k += blockDim.x)
     cs[k] = coef[size_t(k >> 5) * 512 + c0 + (k & 31)];
   for (int k = threadIdx.x; k < count; k += blockDim.x)
-    ts[k] = packed[k];
+    ts[k] = abc[k];
+  vs[16 * 32 + lane] = 1.f;
   __syncthreads();
+  int bounds[5] = {out_start.x, out_start.y, out_start.z, out_start.w, count};
   int i0 = blockIdx.y * kProdNodes, i1 = min(n, i0 + kProdNodes);
   for (int i = i0 + warp; i < i1; i += kProdWarps) {
 #pragma unroll
     for (int m = 0; m < 16; ++m)
       vs[m * 32 + lane] = x[(size_t(m) * n + i) * 512 + c0 + lane];
     __syncwarp();
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int k = 0; k < count; ++k) {
-      int t = ts[k];
-      int out = t & 3, deg = (t >> 2) & 3;
-      float val = cs[k * 32 + lane] * vs[((t >> 4) & 15) * 32 + lane];
-      if (deg >= 2)
-        val *= vs[((t >> 8) & 15) * 32 + lane];
-      if (deg >= 3)
-        val *= vs[((t >> 12) & 15) * 32 + lane];
-      if (out == 0)
-        acc[0] += val;
-      else if (out == 1)
-        acc[1] += val;
-      else if (out == 2)
-        acc[2] += val;
-      else
-        acc[3] += val;
+    for (int o = 0; o < outputs; ++o) {
+      int k = bounds[o], end = bounds[o + 1];
+      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+      for (; k + 4 <= end; k += 4) {
+        int t0 = ts[k], t1 = ts[k + 1], t2 = ts[k + 2], t3 = ts[k + 3];
+        s0 = fmaf(cs[k * 32 + lane] * vs[(t0 & 255) * 32 + lane],
+                  vs[((t0 >> 8) & 255) * 32 + lane] * vs[(t0 >> 16) * 32 + lane], s0);
+        s1 = fmaf(cs[(k + 1) * 32 + lane] * vs[(t1 & 255) * 32 + lane],
+                  vs[((t1 >> 8) & 255) * 32 + lane] * vs[(t1 >> 16) * 32 + lane], s1);
+        s2 = fmaf(cs[(k + 2) * 32 + lane] * vs[(t2 & 255) * 32 + lane],
+                  vs[((t2 >> 8) & 255) * 32 + lane] * vs[(t2 >> 16) * 32 + lane], s2);
+        s3 = fmaf(cs[(k + 3) * 32 + lane] * vs[(t3 & 255) * 32 + lane],
+                  vs[((t3 >> 8) & 255) * 32 + lane] * vs[(t3 >> 16) * 32 + lane], s3);
+      }
+      for (; k < end; ++k) {
+        int t0 = ts[k];
+        s0 = fmaf(cs[k * 32 + lane] * vs[(t0 & 255) * 32 + lane],
+                  vs[((t0 >> 8) & 255) * 32 + lane] * vs[(t0 >> 16) * 32 + lane], s0);
+      }
+      y[(size_t(o) * n + i) * 512 + c0 + lane] = (s0 + s1) + (s2 + s3);
     }
-    for (int o = 0; o < outputs; ++o)
-      y[(size_t(o) * n + i) * 512 + c0 + lane] = acc[o];
     __syncwarp();
   }
 }
 
-__global__ void __launch_bounds__(256) product_backward_kernel(int n, const int *packed, const float *coef,
-                                                               int count, int outputs, const float *x,
+// VJP: g[a] += w G b c, g[b] += w G a c, g[c] += w G a b (missing factors are the constant 1,
+// whose gradient slot 16 is a discard).
+__global__ void __launch_bounds__(256) product_backward_kernel(int n, const int *abc, const float *coef, int count,
+                                                               const int4 out_start, int outputs, const float *x,
                                                                const float *grad, float *xg) {
   extern __shared__ float ps[];
   float *cs = ps;
   int *ts = reinterpret_cast<int *>(cs + count * 32);
-  float *vs = reinterpret_cast<float *>(ts + ((count + 3) & ~3)) + (threadIdx.x >> 5) * 32 * 32;
-  float *gs = vs + 16 * 32;
+  float *vs = reinterpret_cast<float *>(ts + ((count + 3) & ~3)) + (threadIdx.x >> 5) * 2 * kProdV * 32;
+  float *gs = vs + kProdV * 32;
   int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, c0 = blockIdx.x * 32;
   for (int k = threadIdx.x; k < count * 32; k += blockDim.x)
     cs[k] = coef[size_t(k >> 5) * 512 + c0 + (k & 31)];
   for (int k = threadIdx.x; k < count; k += blockDim.x)
-    ts[k] = packed[k];
+    ts[k] = abc[k];
+  vs[16 * 32 + lane] = 1.f;
   __syncthreads();
+  int bounds[5] = {out_start.x, out_start.y, out_start.z, out_start.w, count};
   int i0 = blockIdx.y * kProdNodes, i1 = min(n, i0 + kProdNodes);
   for (int i = i0 + warp; i < i1; i += kProdWarps) {
 #pragma unroll
@@ -240,26 +249,16 @@ __global__ void __launch_bounds__(256) product_backward_kernel(int n, const int 
       vs[m * 32 + lane] = x[(size_t(m) * n + i) * 512 + c0 + lane];
       gs[m * 32 + lane] = 0.f;
     }
-    float G[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int o = 0; o < outputs; ++o)
-      G[o] = grad[(size_t(o) * n + i) * 512 + c0 + lane];
     __syncwarp();
-    for (int k = 0; k < count; ++k) {
-      int t = ts[k];
-      int out = t & 3, deg = (t >> 2) & 3, ia = (t >> 4) & 15, ib = (t >> 8) & 15, ic = (t >> 12) & 15;
-      float gw = cs[k * 32 + lane] * (out == 0 ? G[0] : out == 1 ? G[1] : out == 2 ? G[2] : G[3]);
-      float a = vs[ia * 32 + lane];
-      if (deg == 1) {
-        gs[ia * 32 + lane] += gw;
-      } else if (deg == 2) {
-        float b = vs[ib * 32 + lane];
-        gs[ia * 32 + lane] += gw * b;
-        gs[ib * 32 + lane] += gw * a;
-      } else {
-        float b = vs[ib * 32 + lane], d = vs[ic * 32 + lane];
-        gs[ia * 32 + lane] += gw * b * d;
-        gs[ib * 32 + lane] += gw * a * d;
-        gs[ic * 32 + lane] += gw * a * b;
+    for (int o = 0; o < outputs; ++o) {
+      float G = grad[(size_t(o) * n + i) * 512 + c0 + lane];
+      for (int k = bounds[o]; k < bounds[o + 1]; ++k) {
+        int t = ts[k], ia = (t & 255) * 32 + lane, ib = ((t >> 8) & 255) * 32 + lane, ic = (t >> 16) * 32 + lane;
+        float gw = cs[k * 32 + lane] * G;
+        float a = vs[ia], b = vs[ib], d = vs[ic];
+        gs[ia] += gw * b * d;
+        gs[ib] += gw * a * d;
+        gs[ic] += gw * a * b;
       }
     }
     __syncwarp();
@@ -367,7 +366,7 @@ void launch_gate_norm_backward(cudaStream_t s, int n, const float *pre, const fl
                                                 gate_scale, pre_grad, raw_grad, density_grad);
 }
 size_t product_smem(int count, bool backward) {
-  return (size_t(count) * 32 + ((count + 3) & ~3)) * 4 + size_t(kProdWarps) * (backward ? 32 : 16) * 32 * 4;
+  return (size_t(count) * 32 + ((count + 3) & ~3)) * 4 + size_t(kProdWarps) * (backward ? 2 : 1) * kProdV * 32 * 4;
 }
 
 void launch_product(cudaStream_t s, int n, const Layer &l, const float *x, float *y) {
@@ -376,7 +375,8 @@ void launch_product(cudaStream_t s, int n, const Layer &l, const float *x, float
   size_t smem = product_smem(l.npoly, false);
   lapis::check(cudaFuncSetAttribute(product_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   dim3 grid(16, (n + kProdNodes - 1) / kProdNodes);
-  lapis::launch(product_kernel, grid, 256, smem, s, n, l.poly_packed, l.pcoef, l.npoly, l.pouts, x, y);
+  lapis::launch(product_kernel, grid, 256, smem, s, n, l.poly_abc, l.poly_coef_sorted, l.npoly, l.poly_out_start,
+                l.pouts, x, y);
 }
 void launch_product_backward(cudaStream_t s, int n, const Layer &l, const float *x, const float *grad, float *xg) {
   if (!n)
@@ -385,8 +385,8 @@ void launch_product_backward(cudaStream_t s, int n, const Layer &l, const float 
   lapis::check(
       cudaFuncSetAttribute(product_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   dim3 grid(16, (n + kProdNodes - 1) / kProdNodes);
-  lapis::launch(product_backward_kernel, grid, 256, smem, s, n, l.poly_packed, l.pcoef, l.npoly, l.pouts, x, grad,
-                xg);
+  lapis::launch(product_backward_kernel, grid, 256, smem, s, n, l.poly_abc, l.poly_coef_sorted, l.npoly,
+                l.poly_out_start, l.pouts, x, grad, xg);
 }
 void launch_add(cudaStream_t s, size_t count, const float *a, float *b, float scale) {
   if (count)
