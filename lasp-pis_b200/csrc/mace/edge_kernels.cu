@@ -103,7 +103,17 @@ __global__ void geometry_kernel(DeviceGeometry g, const int *species, const floa
       out.dbasis[size_t(e) * 10 + k] = b.d;
     }
     float Y[16];
-    harmonics<false>(d.x, d.y, d.z, r, Y, nullptr);
+    if (out.dY) {
+      float Gy[16][3];
+      harmonics<true>(d.x, d.y, d.z, r, Y, Gy);
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+#pragma unroll
+        for (int q = 0; q < 3; ++q)
+          out.dY[size_t(e) * 48 + 3 * k + q] = Gy[k][q];
+    } else {
+      harmonics<false>(d.x, d.y, d.z, r, Y, nullptr);
+    }
 #pragma unroll
     for (int k = 0; k < 16; ++k)
       out.Y[size_t(e) * 16 + k] = Y[k];

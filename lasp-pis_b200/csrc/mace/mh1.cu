@@ -9,6 +9,7 @@
 // baseline e0 is added in float64 for the total (mace/src/mh1.cu:890-896).
 #include "mace/mh1.hpp"
 #include "model.hpp"
+#include <algorithm>
 #include <climits>
 #include <cstdlib>
 #include <cstdio>
@@ -38,7 +39,39 @@ MH1::~MH1() = default;
 size_t MH1::parameter_bytes() const { return model_->data.bytes; }
 void MH1::set_profiling(bool enabled) { model_->profiling = enabled; }
 
+long long projection_chunk_edges() {
+  static const long long edges = [] {
+    const char *v = std::getenv("MACE_PROJECTION_CHUNK_EDGES");
+    long long k = v ? std::atoll(v) : 0;
+    return k > 0 ? k : 1ll << 20;
+  }();
+  return edges;
+}
+
 namespace {
+// Receiver-aligned chunks of at most projection_chunk_edges() edges (a receiver with more
+// edges gets a chunk of its own) for the projection path; a single chunk, without a host
+// copy of the CSR offsets, when all edges fit.
+std::vector<ProjectionChunk> projection_chunks(Context &c) {
+  int n = c.geometry.n;
+  long long E = c.geometry.edge_capacity, cap = projection_chunk_edges();
+  if (E <= cap)
+    return {ProjectionChunk{0, n, 0, E}};
+  std::vector<int> row(size_t(n) + 1);
+  check(cudaMemcpyAsync(row.data(), c.geometry.edge_offsets, row.size() * sizeof(int), cudaMemcpyDeviceToHost,
+                        c.stream));
+  check(cudaStreamSynchronize(c.stream));
+  std::vector<ProjectionChunk> chunks;
+  for (int r = 0; r < n;) {
+    int r1 = r + 1;
+    while (r1 < n && row[r1 + 1] - row[r] <= cap)
+      ++r1;
+    chunks.push_back(ProjectionChunk{r, r1, row[r], row[r1]});
+    r = r1;
+  }
+  return chunks;
+}
+
 // Per-stage timing (like the reference's StageTimer, mace/src/mh1.cu:53-82): CUDA events
 // recorded on the model stream between stages, taken from a persistent pool so that the
 // timed path creates no events.
@@ -97,12 +130,25 @@ Result MH1::evaluate() {
   launch_species(s, c.geometry, m.lookup, species);
   launch_embed(s, n, species, m.embedding, x0);
   launch_zbl(s, c.geometry, m.constants_dev, m.zbl_radii, m.zbl_c, cst[7], energy, force, virial);
+  // Projection path: radial projections on the tensor cores into chunk buffers, tensor
+  // products from those (default); otherwise the fused SIMT or tcgen05 edge kernels.
+  bool projection = !tensor_core_edges() && tensor_core_linears() && m.layers[0].radial.out_hi &&
+                    m.layers[1].radial.out_hi;
+  std::vector<ProjectionChunk> chunks;
+  long long chunk_cap = 0;
+  if (projection) {
+    chunks = projection_chunks(c);
+    for (auto &k : chunks)
+      chunk_cap = std::max(chunk_cap, k.e1 - k.e0);
+  }
   EdgeArrays ea{c.array<float>("mh.edge.basis", E * 10), c.array<float>("mh.edge.dbasis", E * 10),
-                c.array<float2>("mh.edge.cut", E), c.array<float>("mh.edge.Y", E * 16)};
+                c.array<float2>("mh.edge.cut", E), c.array<float>("mh.edge.Y", E * 16),
+                projection ? c.array<float>("mh.edge.dY", E * 48) : nullptr};
   int *pair = c.array<int>("mh.edge.pair", E);
   launch_edge_geometry(s, c.geometry, species, m.constants_dev, m.radii, m.bessel, ea, pair);
   timer.mark("embedding/ZBL/geometry");
   RadialOut ro[2];
+  float *proj[2] = {nullptr, nullptr}; // [R | dR] per layer, chunk_cap rows each
   float *up[2], *rho[2], *raw[2], *pre[2], *pin[2], *hidden[2];
   float *res = node("mh.t.res", 9728), *skip = node("mh.t.skip", 2048), *msg = node("mh.t.msg", 5120),
         *gate = node("mh.t.gate", 8192), *poly = node("mh.t.poly", 2048), *node_e = node("mh.t.energy", 1);
@@ -116,14 +162,22 @@ Result MH1::evaluate() {
     pre[k] = node(p + ".pre", 9728);
     pin[k] = node(p + ".pin", 8192);
     hidden[k] = node(p + ".hidden", k ? 512 : 2048);
-    ro[k] = RadialOut{c.array<float>(p + ".h", E * 64), c.array<float>(p + ".dh", E * 64),
-                      c.array<float2>(p + ".den", E)};
+    float *hd = c.array<float>(p + ".hd", 2 * E * 64); // h then dh/dr, one GEMM batch apart
+    ro[k] = RadialOut{hd, hd + E * 64, c.array<float2>(p + ".den", E)};
+    int width = l.paths * 128;
+    proj[k] = projection ? c.array<float>(p + ".proj", size_t(2 * chunk_cap) * width) : nullptr;
     linear(s, n, l.up, input, up[k], false, false, status);
     linear(s, n, l.res, up[k], res, false, false, status);
     linear(s, n, l.skip, input, skip, false, false, status);
     launch_radial(s, c.geometry, l, pair, ea, ro[k]);
     timer.mark("forward" + std::to_string(k) + ".linears/radial");
-    if (tensor_core_edges())
+    if (projection) {
+      for (auto &q : chunks) {
+        tc_gemm(s, int(q.e1 - q.e0), width, 64, 1, ro[k].h + q.e0 * 64, 0, l.radial.out_hi, l.radial.out_lo,
+                proj[k], width, 0, false, status);
+        launch_message_forward_proj(s, k, c.geometry, l, ea, ro[k], q, proj[k], up[k], msg, rho[k]);
+      }
+    } else if (tensor_core_edges())
       launch_message_forward_tc(s, k, c.geometry, l, ea, ro[k], up[k], msg, rho[k]);
     else
       launch_message_forward(s, k, c.geometry, l, ea, ro[k], up[k], msg, rho[k]);
@@ -173,7 +227,21 @@ Result MH1::evaluate() {
     if (k == 1)
       linear(s, n, l.res, pregrad, upgrad, true, false, status);
     timer.mark("backward" + std::to_string(k) + ".node");
-    if (tensor_core_edges())
+    if (projection) {
+      int width = l.paths * 128;
+      float *R = proj[k], *dR = proj[k] + size_t(chunk_cap) * width;
+      for (auto &q : chunks) {
+        int rows = int(q.e1 - q.e0);
+        if (chunks.size() == 1) // R is still in place from the forward pass
+          tc_gemm(s, rows, width, 64, 1, ro[k].dh + q.e0 * 64, 0, l.radial.out_hi, l.radial.out_lo, dR, width, 0,
+                  false, status);
+        else
+          tc_gemm(s, rows, width, 64, 2, ro[k].h + q.e0 * 64, (long long)E * 64, l.radial.out_hi,
+                  l.radial.out_lo, R, width, (long long)chunk_cap * width, false, status);
+        launch_message_backward_proj(s, k, c.geometry, l, ea, ro[k], q, R, dR, up[k], msggrad, rhograd, upgrad,
+                                     edge_force, k == 0);
+      }
+    } else if (tensor_core_edges())
       launch_message_backward_tc(s, k, c.geometry, l, ea, ro[k], up[k], msggrad, rhograd, upgrad, edge_force, k == 0);
     else
       launch_message_backward(s, k, c.geometry, l, ea, ro[k], up[k], msggrad, rhograd, upgrad, edge_force, k == 0);

@@ -84,6 +84,7 @@ struct EdgeArrays {
   float *basis, *dbasis; // [E][10]
   float2 *cut;           // [E] (cut, dcut)
   float *Y;              // [E][16]
+  float *dY;             // [E][16][3] dY/dd (written when non-null)
 };
 struct RadialOut {
   float *h, *dh;        // [E][64]
@@ -112,6 +113,23 @@ void launch_message_backward_tc(cudaStream_t, int layer, const lapis::DeviceGeom
                                 const float *density_grad, float *up_grad, float4 *edge_force, bool accumulate);
 CUtensorMap tc_map_2d(const float *base, int cols, long long rows, int box_cols, int box_rows);
 bool tensor_core_edges();
+// Projection path (edge_proj.cu): the radial projection R = h W (and dR = dh W) runs as a
+// tensor-core GEMM into a buffer covering the edges of receivers [r0, r1) = [e0, e1); the
+// tensor-product kernels read rows e - e0.
+struct ProjectionChunk {
+  int r0, r1;
+  long long e0, e1;
+};
+void launch_message_forward_proj(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &, EdgeArrays,
+                                 RadialOut, const ProjectionChunk &, const float *R, const float *up,
+                                 float *message, float *density);
+void launch_message_backward_proj(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &,
+                                  EdgeArrays, RadialOut, const ProjectionChunk &, const float *R, const float *dR,
+                                  const float *up, const float *message_grad, const float *density_grad,
+                                  float *up_grad, float4 *edge_force, bool accumulate);
+// Edges per projection chunk (bounds the R / dR buffers at 2 x 1280 floats per edge):
+// 2^20, or MACE_PROJECTION_CHUNK_EDGES when set to a positive value.
+long long projection_chunk_edges();
 void launch_force_gather(cudaStream_t, const lapis::DeviceGeometry &, const float4 *edge_force, float *force,
                          float *virial);
 

@@ -1,6 +1,6 @@
 // FP32-accurate GEMM on the Blackwell tensor cores (tcgen05, kind::tf32, 3-term split).
 //
-//   C[z] (+)= A[z] * B      A: [M][K] fp32 row-major per batch z (node features),
+//   C[z] (+)= A[z] * B      A: [M][K] fp32 row-major per batch z (node or edge features),
 //                           B: given as two K-major tf32 planes Bhi/Blo [N][K] with
 //                              B = Bhi + Blo (split once at model load).
 // Each A tile is split on the fly into hi = round_tf32(a) and lo = a - hi, and the tile
@@ -12,32 +12,41 @@
 // biases long accumulations coherently.  So the dominant A_hi*B_hi term is accumulated
 // FRESH for every 32-wide K slab (4 MMAs) into one of two TMEM buffers and drained into
 // FP32 registers with round-to-nearest adds (overlapping the next slab), while the two
-// correction terms, 2^-11 smaller, accumulate over all of K in a third TMEM buffer drained
-// once at the end.
+// correction terms, 2^-11 smaller, accumulate over all of K in a per-tile correction
+// buffer drained once at the end of the tile.
 //
-// CTA = 6 warps, one 128 x 128 output tile:
-//   warp 0      TMA producer (A, Bhi, Blo per 32-wide K slab, SWIZZLE_128B, 3-stage ring)
+// Persistent: one CTA per SM walks the 128 x 128 output tiles (n fastest, so the CTAs that
+// run together share A tiles in L2) with a continuous pipeline across tiles.  TMEM holds
+// two slab buffers and two correction buffers (512 columns), so the MMAs of tile t+1 run
+// while tile t is drained and stored.  CTA = 8 warps (two per SM sub-partition, so the
+// drain warps may hold a full 128-column row of FP32 accumulators):
+//   warp 0      TMA producer (A, Bhi, Blo per 32-wide K slab, SWIZZLE_128B, 2-stage ring)
 //   warp 1      MMA issuer (one elected thread; UMMA 128 x 128 x 8)
-//   warps 2..5  split A into hi/lo in shared memory, drain the hi*hi buffers into per-row
-//               FP32 registers, add the correction buffer, write the tile (adding to C
-//               when accumulate)
+//   warps 2..5  drain TMEM (lane = output row) into FP32 registers, stage the row in
+//               shared memory and write it with one bulk copy per row (a bulk fp32 add
+//               into C when accumulating); rows past M are skipped
+//   warps 6..7  split A into hi/lo in shared memory
 // Every mbarrier wait is bounded: on time-out the CTA records an error code in *status,
 // stops issuing work, waits (bounded) for issued MMAs and frees its TMEM.
 #include "../lapis/launch.cuh"
 #include "model.hpp"
 #include "tcgen05.cuh"
 #include <cuda.h>
+#include <algorithm>
+#include <climits>
 #include <mutex>
 
 namespace mace {
 namespace {
 using namespace tc;
-constexpr int kBM = 128, kBN = 128, kBK = 32, kStages = 3;
+constexpr int kBM = 128, kBN = 128, kBK = 32, kStages = 2;
 constexpr int kTileBytes = kBM * kBK * 4;        // 16 KiB (A, A_lo, Bhi, Blo tiles are equal)
 constexpr int kStageBytes = 4 * kTileBytes;      // A | A_lo | Bhi | Blo
-constexpr int kSmemBytes = kStages * kStageBytes + 1024 /* align */ + 256 /* barriers */;
-constexpr int kTmemCols = 4 * kBN; // hi*hi buffers 0/1, correction buffer at 2 (512 columns)
-constexpr int kThreads = 192;
+constexpr int kRowStage = (kBN + 4) * 4;         // one staged output row, padded (528 B)
+constexpr int kStagingBytes = kBM * kRowStage;   // 66 KiB
+constexpr int kSmemBytes = 1024 /* align */ + kStages * kStageBytes + kStagingBytes + 256 /* barriers */;
+constexpr int kTmemCols = 4 * kBN; // hi*hi slab buffers 0/1, correction buffers 2/3 (512 columns)
+constexpr int kThreads = 256;
 constexpr int kStatusGemmTimeout = 7;
 
 // Instruction descriptor: D fp32, A/B tf32, both K-major, M = 128, N = 128.
@@ -47,34 +56,48 @@ __device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t a, uint64_t 
   umma_tf32_desc(tmem_d, a, b, kIdesc, accumulate);
 }
 
+struct TileGrid {
+  int nN, nM, tiles;
+  __device__ void coords(int t, int &n0, int &m0, int &z) const {
+    n0 = (t % nN) * kBN;
+    int r = t / nN;
+    m0 = (r % nM) * kBM;
+    z = r / nM;
+  }
+};
+
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBhi,
-                   const __grid_constant__ CUtensorMap tmBlo, float *C, int ldc, long long strideC, int M, int N,
-                   int K, int accumulate, int *status) {
+                   const __grid_constant__ CUtensorMap tmBlo, float *C, int ldc, long long strideC, int M,
+                   TileGrid tg, int K, int accumulate, int *status) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
-  // bars: full[S] | lo_ready[S] | empty[S] | done | tmem_full[2] | tmem_free[2]
+  unsigned char *staging = smem + kStages * kStageBytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(staging + kStagingBytes);
+  // bars: full[S] | ready[S] | empty[S] | tfull[2] | tfree[2] | cfull[2] | cfree[2] | done
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
+  __shared__ int mma_done_issued; // whether the final commit to `done` was issued
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM, z = blockIdx.z;
   int ktiles = K / kBK;
-  unsigned full0 = smem_u32(bars), lo0 = smem_u32(bars + kStages), empty0 = smem_u32(bars + 2 * kStages),
-           done = smem_u32(bars + 3 * kStages), tfull0 = smem_u32(bars + 3 * kStages + 1),
-           tfree0 = smem_u32(bars + 3 * kStages + 3);
+  unsigned full0 = smem_u32(bars), ready0 = full0 + 8 * kStages, empty0 = ready0 + 8 * kStages,
+           tfull0 = empty0 + 8 * kStages, tfree0 = tfull0 + 16, cfull0 = tfree0 + 16, cfree0 = cfull0 + 16,
+           done = cfree0 + 16;
   if (threadIdx.x == 0) {
     abort_flag = 0;
+    mma_done_issued = 0;
     for (int s = 0; s < kStages; ++s) {
       mbar_init(full0 + 8 * s, 1);
-      mbar_init(lo0 + 8 * s, 128);
+      mbar_init(ready0 + 8 * s, 64);
       mbar_init(empty0 + 8 * s, 1);
     }
-    mbar_init(done, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull0 + 8 * b, 1);
       mbar_init(tfree0 + 8 * b, 128);
+      mbar_init(cfull0 + 8 * b, 1);
+      mbar_init(cfree0 + 8 * b, 128);
     }
+    mbar_init(done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -87,126 +110,145 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   uint32_t tmem = tmem_base;
-  __shared__ int mma_done_issued; // whether the final commit to `done` was issued
-  if (threadIdx.x == 0)
-    mma_done_issued = 0;
-  __syncthreads();
 
   if (warp == 0) {
+    // ---------------- TMA producer ----------------
     if (lane == 0) {
-      for (int kt = 0; kt < ktiles; ++kt) {
-        int s = kt % kStages;
-        if (kt >= kStages && !mbar_wait(empty0 + 8 * s, ((kt / kStages) - 1) & 1, &abort_flag))
-          break;
-        unsigned base = smem_u32(smem + s * kStageBytes);
-        mbar_expect_tx(full0 + 8 * s, 3 * kTileBytes);
-        tma_load_3d(base, &tmA, kt * kBK, m0, z, full0 + 8 * s);
-        tma_load_2d(base + 2 * kTileBytes, &tmBhi, kt * kBK, n0, full0 + 8 * s);
-        tma_load_2d(base + 3 * kTileBytes, &tmBlo, kt * kBK, n0, full0 + 8 * s);
+      int g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tg.tiles && ok; t += gridDim.x) {
+        int n0, m0, z;
+        tg.coords(t, n0, m0, z);
+        for (int kt = 0; kt < ktiles; ++kt, ++g) {
+          int s = g % kStages;
+          if (g >= kStages && !(ok = mbar_wait(empty0 + 8 * s, ((g / kStages) - 1) & 1, &abort_flag)))
+            break;
+          unsigned base = smem_u32(smem + s * kStageBytes);
+          mbar_expect_tx(full0 + 8 * s, 3 * kTileBytes);
+          tma_load_3d(base, &tmA, kt * kBK, m0, z, full0 + 8 * s);
+          tma_load_2d(base + 2 * kTileBytes, &tmBhi, kt * kBK, n0, full0 + 8 * s);
+          tma_load_2d(base + 3 * kTileBytes, &tmBlo, kt * kBK, n0, full0 + 8 * s);
+        }
       }
     }
   } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
     if (lane == 0) {
       bool ok = true;
-      uint32_t corr = tmem + uint32_t(2 * kBN);
-      for (int kt = 0; kt < ktiles && ok; ++kt) {
-        int s = kt % kStages;
-        ok = mbar_wait(lo0 + 8 * s, (kt / kStages) & 1, &abort_flag);
-        if (!ok)
+      int g = 0, i = 0;
+      for (int t = blockIdx.x; t < tg.tiles && ok; t += gridDim.x, ++i) {
+        int c = i & 1;
+        if (i >= 2 && !(ok = mbar_wait(cfree0 + 8 * c, ((i >> 1) - 1) & 1, &abort_flag)))
           break;
-        tc_fence_after();
-        unsigned base = smem_u32(smem + s * kStageBytes);
-        int b = kt & 1;
-        if (kt >= 2 && !(ok = mbar_wait(tfree0 + 8 * b, ((kt >> 1) - 1) & 1, &abort_flag)))
-          break;
-        tc_fence_after();
+        uint32_t corr = tmem + uint32_t((2 + c) * kBN);
+        for (int kt = 0; kt < ktiles; ++kt, ++g) {
+          int s = g % kStages, b = g & 1;
+          if (!(ok = mbar_wait(ready0 + 8 * s, (g / kStages) & 1, &abort_flag)))
+            break;
+          if (g >= 2 && !(ok = mbar_wait(tfree0 + 8 * b, ((g >> 1) - 1) & 1, &abort_flag)))
+            break;
+          tc_fence_after();
+          unsigned base = smem_u32(smem + s * kStageBytes);
 #pragma unroll
-        for (int j = 0; j < kBK / 8; ++j) {
-          uint64_t a_hi = smem_desc(base + 32 * j), a_lo = smem_desc(base + kTileBytes + 32 * j);
-          uint64_t b_hi = smem_desc(base + 2 * kTileBytes + 32 * j), b_lo = smem_desc(base + 3 * kTileBytes + 32 * j);
-          umma_tf32(tmem + uint32_t(b * kBN), a_hi, b_hi, j ? 1u : 0u);
-          umma_tf32(corr, a_lo, b_hi, (kt | j) ? 1u : 0u);
-          umma_tf32(corr, a_hi, b_lo, 1u);
+          for (int j = 0; j < kBK / 8; ++j) {
+            uint64_t a_hi = smem_desc(base + 32 * j), a_lo = smem_desc(base + kTileBytes + 32 * j);
+            uint64_t b_hi = smem_desc(base + 2 * kTileBytes + 32 * j), b_lo = smem_desc(base + 3 * kTileBytes + 32 * j);
+            umma_tf32(tmem + uint32_t(b * kBN), a_hi, b_hi, j ? 1u : 0u);
+            umma_tf32(corr, a_lo, b_hi, (kt | j) ? 1u : 0u);
+            umma_tf32(corr, a_hi, b_lo, 1u);
+          }
+          umma_commit(tfull0 + 8 * b);
+          umma_commit(empty0 + 8 * s);
         }
-        umma_commit(tfull0 + 8 * b);
-        umma_commit(empty0 + 8 * s);
+        if (ok)
+          umma_commit(cfull0 + 8 * c);
       }
       umma_commit(done);
       mma_done_issued = 1;
     }
-  } else {
-    // Split warps: A -> (hi, lo), 32 floats per thread per stage; after converting slab kt,
-    // drain the hi*hi products of slab kt - 1 so the MMAs of kt overlap the drain.
-    int t = threadIdx.x - 64, quarter = warp & 3;
-    uint32_t lane_addr = tmem + (uint32_t(quarter * 32) << 16);
-    float acc[kBN];
-#pragma unroll
-    for (int c = 0; c < kBN; ++c)
-      acc[c] = 0.f;
+  } else if (warp >= 6) {
+    // ---------------- A split: hi in place, lo beside it ----------------
+    int t = threadIdx.x - 192, g = 0;
     bool ok = true;
-    auto drain = [&](uint32_t col, uint32_t bar, int parity, bool release) {
-      bool go = bar ? mbar_wait(bar, parity, &abort_flag) : true;
-      if (!__all_sync(0xffffffffu, go))
-        return false;
-      tc_fence_after();
-#pragma unroll
-      for (int c0 = 0; c0 < kBN; c0 += 32) {
-        float v[32];
-        tmem_ld32(lane_addr + col + uint32_t(c0), v);
-#pragma unroll
-        for (int k = 0; k < 32; ++k)
-          acc[c0 + k] += v[k];
-      }
-      tc_fence_before();
-      if (release)
-        mbar_arrive(tfree0 + 8 * ((col / kBN) & 1));
-      return true;
-    };
-    auto drain_slab = [&](int kt) {
-      int b = kt & 1;
-      return drain(uint32_t(b * kBN), tfull0 + 8 * b, (kt >> 1) & 1, true);
-    };
-    for (int kt = 0; kt < ktiles && ok; ++kt) {
-      int s = kt % kStages;
-      ok = mbar_wait(full0 + 8 * s, (kt / kStages) & 1, &abort_flag);
-      if (!__all_sync(0xffffffffu, ok)) {
-        ok = false;
-        break;
-      }
-      float4 *a = reinterpret_cast<float4 *>(smem + s * kStageBytes);
-      float4 *lo = reinterpret_cast<float4 *>(smem + s * kStageBytes + kTileBytes);
-#pragma unroll
-      for (int q = 0; q < kTileBytes / 16 / 128; ++q) {
-        float4 v = a[t + 128 * q], h, l;
-        h.x = __uint_as_float((__float_as_uint(v.x) + 0x1000u) & 0xffffe000u);
-        h.y = __uint_as_float((__float_as_uint(v.y) + 0x1000u) & 0xffffe000u);
-        h.z = __uint_as_float((__float_as_uint(v.z) + 0x1000u) & 0xffffe000u);
-        h.w = __uint_as_float((__float_as_uint(v.w) + 0x1000u) & 0xffffe000u);
-        l.x = v.x - h.x, l.y = v.y - h.y, l.z = v.z - h.z, l.w = v.w - h.w;
-        a[t + 128 * q] = h;
-        lo[t + 128 * q] = l;
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive(lo0 + 8 * s);
-      if (kt > 0)
-        ok = drain_slab(kt - 1);
-    }
-    if (ok)
-      ok = drain_slab(ktiles - 1);
-    if (ok)
-      ok = drain(uint32_t(2 * kBN), done, 0, false);
-    if (__all_sync(0xffffffffu, ok)) {
-      int row = m0 + quarter * 32 + lane;
-      if (row < M) {
-        float4 *dst = reinterpret_cast<float4 *>(C + z * strideC + size_t(row) * ldc + n0);
-#pragma unroll
-        for (int q = 0; q < kBN / 4; ++q) {
-          float4 o = accumulate ? dst[q] : make_float4(0.f, 0.f, 0.f, 0.f);
-          o.x += acc[4 * q], o.y += acc[4 * q + 1], o.z += acc[4 * q + 2], o.w += acc[4 * q + 3];
-          dst[q] = o;
+    for (int tile = blockIdx.x; tile < tg.tiles && ok; tile += gridDim.x)
+      for (int kt = 0; kt < ktiles; ++kt, ++g) {
+        int s = g % kStages;
+        ok = mbar_wait(full0 + 8 * s, (g / kStages) & 1, &abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
         }
+        float4 *a = reinterpret_cast<float4 *>(smem + s * kStageBytes);
+        float4 *lo = reinterpret_cast<float4 *>(smem + s * kStageBytes + kTileBytes);
+#pragma unroll
+        for (int q = 0; q < kTileBytes / 16 / 64; ++q) {
+          float4 v = a[t + 64 * q], h, l;
+          h.x = tf32_hi(v.x), h.y = tf32_hi(v.y), h.z = tf32_hi(v.z), h.w = tf32_hi(v.w);
+          l.x = v.x - h.x, l.y = v.y - h.y, l.z = v.z - h.z, l.w = v.w - h.w;
+          a[t + 64 * q] = h;
+          lo[t + 64 * q] = l;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(ready0 + 8 * s);
+      }
+  } else {
+    // ---------------- drain + store: lane = output row ----------------
+    int quarter = warp & 3, row_in_tile = quarter * 32 + lane;
+    uint32_t lane_addr = tmem + (uint32_t(quarter * 32) << 16);
+    unsigned char *my_row = staging + row_in_tile * kRowStage;
+    bool ok = true;
+    int g = 0, i = 0;
+    for (int t = blockIdx.x; t < tg.tiles && ok; t += gridDim.x, ++i) {
+      int n0, m0, z;
+      tg.coords(t, n0, m0, z);
+      float acc[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN; ++c)
+        acc[c] = 0.f;
+      auto drain = [&](uint32_t col, uint32_t full, int parity, uint32_t release) {
+        bool go = mbar_wait(full, parity, &abort_flag);
+        if (!__all_sync(0xffffffffu, go))
+          return false;
+        tc_fence_after();
+#pragma unroll
+        for (int c0 = 0; c0 < kBN; c0 += 32) {
+          float v[32];
+          tmem_ld32(lane_addr + col + uint32_t(c0), v);
+#pragma unroll
+          for (int k = 0; k < 32; ++k)
+            acc[c0 + k] += v[k];
+        }
+        tc_fence_before();
+        mbar_arrive(release);
+        return true;
+      };
+      for (int kt = 0; kt < ktiles && ok; ++kt, ++g) {
+        int b = g & 1;
+        ok = drain(uint32_t(b * kBN), tfull0 + 8 * b, (g >> 1) & 1, tfree0 + 8 * b);
+      }
+      int c = i & 1;
+      if (ok)
+        ok = drain(uint32_t((2 + c) * kBN), cfull0 + 8 * c, (i >> 1) & 1, cfree0 + 8 * c);
+      if (!ok)
+        break;
+      // The previous tile's copy must have read this row's staging before it is rewritten.
+      bulk_wait_read();
+      float4 *dst = reinterpret_cast<float4 *>(my_row);
+#pragma unroll
+      for (int q = 0; q < kBN / 4; ++q)
+        dst[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      int row = m0 + row_in_tile;
+      if (row < M) {
+        float *out = C + z * strideC + size_t(row) * ldc + n0;
+        if (accumulate)
+          bulk_add_f32(out, smem_u32(my_row), kBN * 4);
+        else
+          bulk_store(out, smem_u32(my_row), kBN * 4);
+        bulk_commit();
       }
     }
+    bulk_wait();
   }
   tc_fence_before();
   __syncthreads();
@@ -287,20 +329,26 @@ void tc_gemm(cudaStream_t s, int M, int N, int K, int batch, const float *A, lon
     return;
   if (!tc_gemm_supported(N, K))
     throw lapis::Error("tensor-core GEMM shape unsupported");
-  if ((reinterpret_cast<uintptr_t>(C) & 15) || ldc % 4)
+  if ((reinterpret_cast<uintptr_t>(C) & 15) || ldc % 4 || (batch > 1 && strideC % 4))
     throw lapis::Error("tensor-core GEMM output is not 16-byte aligned");
   // A as [batch][M][K] (always a rank-3 map: the kernel issues 3D loads); B as [N][K].
   CUtensorMap ma = make_map(A, K, M, 3, batch, batch > 1 ? strideA : (long long)M * K);
   CUtensorMap mh = make_map(Bhi, K, N, 2, 1, 0), ml = make_map(Blo, K, N, 2, 1, 0);
-  static thread_local int configured_device = -1;
+  static thread_local int configured_device = -1, sms = 148;
   int device = 0;
   lapis::check(cudaGetDevice(&device));
   if (configured_device != device) {
     lapis::check(cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    lapis::check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
     configured_device = device;
   }
-  dim3 grid(N / kBN, (M + kBM - 1) / kBM, batch);
-  lapis::launch(tc_gemm_kernel, grid, kThreads, kSmemBytes, s, ma, mh, ml, C, ldc, strideC, M, N, K,
+  TileGrid tg{N / kBN, (M + kBM - 1) / kBM, 0};
+  long long tiles = (long long)tg.nN * tg.nM * batch;
+  if (tiles > INT_MAX)
+    throw lapis::Error("tensor-core GEMM has too many tiles");
+  tg.tiles = int(tiles);
+  int grid = int(std::min<long long>(tiles, sms));
+  lapis::launch(tc_gemm_kernel, grid, kThreads, kSmemBytes, s, ma, mh, ml, C, ldc, strideC, M, tg, K,
                 int(accumulate), status);
 }
 } // namespace mace

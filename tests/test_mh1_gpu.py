@@ -96,6 +96,35 @@ def test_matches_reference_cuda(engine, name):
     check_close(r, g, fscale=3.0)
 
 
+ENGINE_VARIANT = """
+import sys, numpy as np
+sys.path[:0] = {paths!r}
+from lasp_b200 import structures
+from mace_inference import NativeMH1
+s = structures.load("C2", {data!r})
+with NativeMH1({archive!r}, backend=0, library={library!r}) as m:
+    r = m.calculate(s.positions, s.numbers, s.cell)
+np.savez({out!r}, **r)
+"""
+
+
+@pytest.mark.parametrize("env", [{"MACE_PROJECTION_CHUNK_EDGES": "3000"}, {"MACE_SIMT_LINEARS": "1"}],
+                         ids=["projection-chunks", "simt-edges"])
+def test_engine_variants_match_oracle(library, archive_path, oracle_model, env, tmp_path):
+    """The chunked projection path (many receiver-aligned chunks, R recomputed in the backward)
+    and the SIMT edge/linear path give the oracle's results as well."""
+    import os
+    import sys
+    out = tmp_path / "r.npz"
+    paths = [str(ROOT / "lasp-pis_b200" / "python")]
+    code = ENGINE_VARIANT.format(paths=paths, data=str(DATA), archive=str(archive_path), library=str(library),
+                                 out=str(out))
+    r = subprocess.run([sys.executable, "-c", code], env={**os.environ, **env}, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]
+    s = structures.load("C2", DATA)
+    check_close(dict(np.load(out)), oracle_model.calculate(s.positions, s.numbers, s.cell))
+
+
 def test_native_behaviour(engine):
     """Backends agree, permutation, empty structure, error recovery (mace/tests/native.py:41-72)."""
     xyz, z, cell = scenarios.native_case()
