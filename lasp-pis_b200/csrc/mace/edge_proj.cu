@@ -2,7 +2,7 @@
 //
 // The radial projection of the reference's MH1Pair (mace/src/mh1.cu:331-353),
 //     R[e][p*128 + c] = sum_a h[e][a] W[a][p*128 + c]        (and dR from dh/dr),
-// is one dense E x 64 x (P*128) GEMM per layer.  Here it runs on the tensor cores (tc_gemm,
+// is one dense E x 64 x (P*128) GEMM per layer.  It runs on the tensor cores (tc_gemm,
 // tf32 hi/lo split with FP32 drains) into an HBM buffer, chunked by receivers, and the
 // kernels below consume it:
 //   forward   messages and density, as mace/src/mh1.cu:331-389 (w = cut * (R + b));
@@ -11,202 +11,325 @@
 // Q_p = sum_t cg G[out] u[in] Y[sh] (then dE/dr = sum_p Q_p dw_p), per harmonic
 // T_sh = sum_t cg G[out] u[in] w_p (then dE/dd = sum_sh T_sh dY_sh), and the sender
 // up-gradient sum_t cg G[out] Y[sh] w_p.  dY comes precomputed from the geometry kernel.
-// CTA per receiver, thread per channel; per-edge scalars are reduced over the 128 channels
-// with warp shuffles and a 4-warp shared-memory sum in a fixed order.
+//
+// CTA per receiver: warps 0..3 are the channels (thread = channel), warp 4 streams the
+// receiver's edges through a 2-stage shared-memory ring in tiles of T edges with bulk
+// copies completing on an mbarrier -- the R (and dR) rows (contiguous, receiver-major),
+// the sender's up-projected features, Y (and dY) -- plus per-edge metadata, so the channel
+// warps read only shared memory.  Per-edge scalars are reduced over the 128 channels with
+// warp shuffles and a 4-warp shared-memory sum in a fixed order.  Waits are bounded.
 #include "../lapis/launch.cuh"
 #include "edge_common.cuh"
 #include "model.hpp"
+#include "tcgen05.cuh"
 
 namespace mace {
 using lapis::DeviceGeometry;
 namespace {
 using namespace edge;
+using tc::bulk_load;
+using tc::mbar_arrive;
+using tc::mbar_expect_tx;
+using tc::mbar_init;
+using tc::mbar_wait;
+using tc::smem_u32;
 
-template <int L>
-__global__ void __launch_bounds__(128) message_forward_proj_kernel(int n, int r0, int e_base, const int *row,
-                                                                   const int *sender, const float *R,
-                                                                   const float *Y, const float2 *cut,
-                                                                   const float2 *den, const float *up,
-                                                                   const float *Wb, TPValues cg, float *msg,
-                                                                   float *rho) {
-  using T = Traits<L>;
-  constexpr int P = T::P, NC = T::NC, IN = T::IN;
-  int i = r0 + blockIdx.x, c = threadIdx.x;
-  float out[NC];
-#pragma unroll
-  for (int k = 0; k < NC; ++k)
-    out[k] = 0.f;
-  float bias[P];
-#pragma unroll
-  for (int p = 0; p < P; ++p)
-    bias[p] = Wb[p * 128 + c];
-  int begin = row[i], end = row[i + 1];
-  float rsum = 0.f;
-#pragma unroll 1
-  for (int e = begin; e < end; ++e) {
-    const float *Re = R + size_t(e - e_base) * (P * 128) + c;
-    float rv[P];
-#pragma unroll
-    for (int p = 0; p < P; ++p)
-      rv[p] = __ldcs(Re + p * 128);
-    int j = __ldg(sender + e);
-    float cv = __ldg(&cut[e].x);
-    float u[IN];
-#pragma unroll
-    for (int q = 0; q < IN; ++q)
-      u[q] = __ldg(up + (size_t(q) * n + j) * 128 + c);
-    float y[16];
-    const float4 *y4 = reinterpret_cast<const float4 *>(Y + size_t(e) * 16);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float4 v = __ldg(y4 + k);
-      y[4 * k] = v.x, y[4 * k + 1] = v.y, y[4 * k + 2] = v.z, y[4 * k + 3] = v.w;
-    }
-    float w[P];
-#pragma unroll
-    for (int p = 0; p < P; ++p)
-      w[p] = cv * (rv[p] + bias[p]);
-    Unroll<0, T::NT>::run([&](auto tc) {
-      constexpr int t = decltype(tc)::value;
-      constexpr TPTerm q = T::term(t);
-      out[q.out] = fmaf(cg.v[t] * y[q.sh], u[q.in] * w[q.path], out[q.out]);
-    });
-    if (c == 0)
-      rsum += den[e].x;
-  }
-#pragma unroll
-  for (int k = 0; k < NC; ++k)
-    msg[(size_t(k) * n + i) * 128 + c] = out[k];
-  if (c == 0)
-    rho[i] = rsum;
+constexpr int kStatusEdgeTimeout = 8;
+constexpr int kStages = 2, kThreads = 160;
+
+struct EdgeMeta {
+  float4 vec; // d, r
+  float2 cut, den;
+  int sender, pad[3];
+};
+
+template <int L, bool Bwd> struct Stage {
+  static constexpr int P = Traits<L>::P, IN = Traits<L>::IN;
+  static constexpr int T = 2;                         // edges per tile
+  static constexpr int ROW = P * 128 * 4;             // bytes of one R row
+  static constexpr int R = 0, DR = R + T * ROW, U = DR + (Bwd ? T * ROW : 0), Y = U + T * IN * 512;
+  static constexpr int DY = Y + T * 64, META = DY + (Bwd ? T * 192 : 0), BYTES = META + T * sizeof(EdgeMeta);
+  static constexpr unsigned tx(int cnt) { return cnt * ((Bwd ? 2 : 1) * ROW + IN * 512 + 64 + (Bwd ? 192 : 0)); }
+};
+
+struct ProjArgs {
+  int n, r0, e_base;
+  const int *row, *sender;
+  const float4 *vec;
+  const float *R, *dR, *Y, *dY;
+  const float2 *cut, *den;
+  const float *up, *bias;
+  const float *msg_grad, *rho_grad; // backward inputs
+  float *msg, *rho;                 // forward outputs
+  float *up_grad;                   // backward, layer 1
+  float4 *edge_force;               // backward output
+  int *status;
+};
+
+// OR of `x` over the 128 channel threads (named barrier 1); also a barrier among them.
+__device__ __forceinline__ bool channels_any(bool x) {
+  unsigned r;
+  asm volatile("{\n\t.reg .pred p, q;\n\t"
+               "setp.ne.u32 q, %1, 0;\n\t"
+               "bar.red.or.pred p, 1, 128, q;\n\t"
+               "selp.u32 %0, 1, 0, p;\n\t}"
+               : "=r"(r)
+               : "r"(unsigned(x))
+               : "memory");
+  return r != 0;
 }
 
-constexpr int kTile = 8; // edges per shared-memory reduction round
+template <int L, bool Bwd, bool Accumulate>
+__global__ void __launch_bounds__(kThreads) edge_proj_kernel(ProjArgs a, TPValues cg) {
+  using S = Stage<L, Bwd>;
+  using Tr = Traits<L>;
+  constexpr int P = Tr::P, NC = Tr::NC, IN = Tr::IN, T = S::T;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(8) uint64_t bars[2 * kStages]; // full[s] | empty[s]
+  __shared__ float red[2][4][T][4];
+  __shared__ volatile int abort_flag;
+  int i = a.r0 + blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int begin = a.row[i], end = a.row[i + 1], ntiles = (end - begin + T - 1) / T;
+  unsigned full0 = smem_u32(bars), empty0 = full0 + 8 * kStages;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full0 + 8 * s, 32);
+      mbar_init(empty0 + 8 * s, 128);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
 
-template <int L, bool Accumulate>
-__global__ void __launch_bounds__(128) message_backward_proj_kernel(
-    int n, int r0, int e_base, const int *row, const int *sender, const float4 *vec, const float *R,
-    const float *dR, const float *Y, const float *dY, const float2 *cut, const float2 *den, const float *up,
-    const float *Wb, TPValues cg, const float *msg_grad, const float *rho_grad, float *up_grad,
-    float4 *edge_force) {
-  using T = Traits<L>;
-  constexpr int P = T::P, NC = T::NC, IN = T::IN;
-  __shared__ float red[2][4][kTile][4];
-  int i = r0 + blockIdx.x, c = threadIdx.x, lane = c & 31, warp = c >> 5;
-  float G[NC];
+  if (warp == 4) {
+    // ---------------- producer ----------------
+    for (int t = 0; t < ntiles; ++t) {
+      int s = t % kStages;
+      bool ok = t < kStages || mbar_wait(empty0 + 8 * s, ((t / kStages) - 1) & 1, &abort_flag);
+      if (!__all_sync(0xffffffffu, ok))
+        break;
+      unsigned char *st = smem + s * S::BYTES;
+      unsigned sb = smem_u32(st), full = full0 + 8 * s;
+      int e0 = begin + t * T, cnt = min(T, end - e0), j = 0;
+      if (lane < cnt) {
+        int e = e0 + lane;
+        EdgeMeta m;
+        m.vec = a.vec[e];
+        m.cut = a.cut[e];
+        m.den = a.den[e];
+        m.sender = j = a.sender[e];
+        reinterpret_cast<EdgeMeta *>(st + S::META)[lane] = m;
+      }
+      __syncwarp();
+      if (lane == 0)
+        mbar_expect_tx(full, S::tx(cnt));
+      __syncwarp();
+      if (lane == 0) {
+        size_t r = size_t(e0 - a.e_base) * (P * 128);
+        bulk_load(sb + S::R, a.R + r, cnt * S::ROW, full);
+        if constexpr (Bwd)
+          bulk_load(sb + S::DR, a.dR + r, cnt * S::ROW, full);
+        bulk_load(sb + S::Y, a.Y + size_t(e0) * 16, cnt * 64, full);
+        if constexpr (Bwd)
+          bulk_load(sb + S::DY, a.dY + size_t(e0) * 48, cnt * 192, full);
+      }
+      if (lane < cnt) {
 #pragma unroll
-  for (int k = 0; k < NC; ++k)
-    G[k] = msg_grad[(size_t(k) * n + i) * 128 + c];
+        for (int q = 0; q < IN; ++q)
+          bulk_load(sb + S::U + (lane * IN + q) * 512, a.up + (size_t(q) * a.n + j) * 128, 512, full);
+      }
+      if (lane != 0)
+        mbar_arrive(full);
+    }
+    return;
+  }
+
+  // ---------------- channels ----------------
+  int c = threadIdx.x;
   float bias[P];
 #pragma unroll
   for (int p = 0; p < P; ++p)
-    bias[p] = Wb[p * 128 + c];
-  float rg = rho_grad[i];
-  int begin = row[i], end = row[i + 1];
-  for (int base = begin, tile = 0; base < end; base += kTile, ++tile) {
-    int cnt = min(kTile, end - base);
-    float(*rd)[kTile][4] = red[tile & 1];
-#pragma unroll 1
-    for (int k = 0; k < cnt; ++k) {
-      int e = base + k;
-      size_t off = size_t(e - e_base) * (P * 128) + c;
-      float rv[P], drv[P];
+    bias[p] = a.bias[p * 128 + c];
+  float acc[Bwd ? 1 : NC], G[Bwd ? NC : 1], rg = 0.f, rsum = 0.f;
+  if constexpr (Bwd) {
 #pragma unroll
-      for (int p = 0; p < P; ++p) {
-        rv[p] = __ldcs(R + off + p * 128);
-        drv[p] = __ldcs(dR + off + p * 128);
-      }
-      int j = __ldg(sender + e);
-      float2 cv = __ldg(cut + e);
-      float u[IN];
+    for (int k = 0; k < NC; ++k)
+      G[k] = a.msg_grad[(size_t(k) * a.n + i) * 128 + c];
+    rg = a.rho_grad[i];
+  } else {
+#pragma unroll
+    for (int k = 0; k < NC; ++k)
+      acc[k] = 0.f;
+  }
+  bool ok = true;
+  for (int t = 0; t < ntiles; ++t) {
+    int s = t % kStages;
+    ok = mbar_wait(full0 + 8 * s, (t / kStages) & 1, &abort_flag);
+    if (channels_any(!ok)) {
+      ok = false;
+      break;
+    }
+    const unsigned char *st = smem + s * S::BYTES;
+    const EdgeMeta *meta = reinterpret_cast<const EdgeMeta *>(st + S::META);
+    int cnt = min(T, end - (begin + t * T));
+    for (int k = 0; k < cnt; ++k) {
+      const float *Rk = reinterpret_cast<const float *>(st + S::R + k * S::ROW) + c;
+      const float *Uk = reinterpret_cast<const float *>(st + S::U + k * IN * 512) + c;
+      const float4 *Y4 = reinterpret_cast<const float4 *>(st + S::Y + k * 64);
+      float2 cv = meta[k].cut;
+      float u[IN], y[16];
 #pragma unroll
       for (int q = 0; q < IN; ++q)
-        u[q] = __ldg(up + (size_t(q) * n + j) * 128 + c);
-      float y[16];
-      const float4 *y4 = reinterpret_cast<const float4 *>(Y + size_t(e) * 16);
+        u[q] = Uk[q * 128];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        float4 v = __ldg(y4 + q);
+        float4 v = Y4[q];
         y[4 * q] = v.x, y[4 * q + 1] = v.y, y[4 * q + 2] = v.z, y[4 * q + 3] = v.w;
       }
-      float w[P], dw[P];
+      if constexpr (!Bwd) {
+        float w[P];
 #pragma unroll
-      for (int p = 0; p < P; ++p) {
-        float s = rv[p] + bias[p];
-        w[p] = cv.x * s;
-        dw[p] = cv.x * drv[p] + cv.y * s;
-      }
-      float Q[P], Tsh[16], ug[IN];
+        for (int p = 0; p < P; ++p)
+          w[p] = cv.x * (Rk[p * 128] + bias[p]);
+        Unroll<0, Tr::NT>::run([&](auto tc_) {
+          constexpr int tt = decltype(tc_)::value;
+          constexpr TPTerm q = Tr::term(tt);
+          acc[q.out] = fmaf(cg.v[tt] * y[q.sh], u[q.in] * w[q.path], acc[q.out]);
+        });
+        rsum += meta[k].den.x;
+      } else {
+        const float *dRk = reinterpret_cast<const float *>(st + S::DR + k * S::ROW) + c;
+        float w[P], dw[P];
 #pragma unroll
-      for (int p = 0; p < P; ++p)
-        Q[p] = 0.f;
+        for (int p = 0; p < P; ++p) {
+          float sv = Rk[p * 128] + bias[p];
+          w[p] = cv.x * sv;
+          dw[p] = cv.x * dRk[p * 128] + cv.y * sv;
+        }
+        float Q[P], Tsh[16], ug[IN];
 #pragma unroll
-      for (int q = 0; q < 16; ++q)
-        Tsh[q] = 0.f;
+        for (int p = 0; p < P; ++p)
+          Q[p] = 0.f;
 #pragma unroll
-      for (int q = 0; q < IN; ++q)
-        ug[q] = 0.f;
-      Unroll<0, T::NT>::run([&](auto tc) {
-        constexpr int t = decltype(tc)::value;
-        constexpr TPTerm q = T::term(t);
-        float x = cg.v[t] * G[q.out];
-        float xu = x * u[q.in];
-        Q[q.path] = fmaf(xu, y[q.sh], Q[q.path]);
-        Tsh[q.sh] = fmaf(xu, w[q.path], Tsh[q.sh]);
-        if constexpr (L > 0)
-          ug[q.in] = fmaf(x, y[q.sh] * w[q.path], ug[q.in]);
-      });
-      if constexpr (L > 0) {
+        for (int q = 0; q < 16; ++q)
+          Tsh[q] = 0.f;
 #pragma unroll
         for (int q = 0; q < IN; ++q)
-          atomicAdd(up_grad + (size_t(q) * n + j) * 128 + c, ug[q]);
-      }
-      float dr = 0.f;
+          ug[q] = 0.f;
+        Unroll<0, Tr::NT>::run([&](auto tc_) {
+          constexpr int tt = decltype(tc_)::value;
+          constexpr TPTerm q = Tr::term(tt);
+          float x = cg.v[tt] * G[q.out];
+          float xu = x * u[q.in];
+          Q[q.path] = fmaf(xu, y[q.sh], Q[q.path]);
+          Tsh[q.sh] = fmaf(xu, w[q.path], Tsh[q.sh]);
+          if constexpr (L > 0)
+            ug[q.in] = fmaf(x, y[q.sh] * w[q.path], ug[q.in]);
+        });
+        if constexpr (L > 0) {
+          int j = meta[k].sender;
 #pragma unroll
-      for (int p = 0; p < P; ++p)
-        dr = fmaf(Q[p], dw[p], dr);
-      float gx = 0.f, gy = 0.f, gz = 0.f;
-      const float4 *g4 = reinterpret_cast<const float4 *>(dY + size_t(e) * 48);
+          for (int q = 0; q < IN; ++q)
+            atomicAdd(a.up_grad + (size_t(q) * a.n + j) * 128 + c, ug[q]);
+        }
+        float dr = 0.f;
 #pragma unroll
-      for (int q = 0; q < 12; ++q) {
-        float4 v = __ldg(g4 + q);
-        float gv[4] = {v.x, v.y, v.z, v.w};
+        for (int p = 0; p < P; ++p)
+          dr = fmaf(Q[p], dw[p], dr);
+        float gx = 0.f, gy = 0.f, gz = 0.f;
+        const float4 *g4 = reinterpret_cast<const float4 *>(st + S::DY + k * 192);
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          int idx = 4 * q + m, sh = idx / 3, ax = idx % 3;
-          float &g = ax == 0 ? gx : ax == 1 ? gy : gz;
-          g = fmaf(Tsh[sh], gv[m], g);
+        for (int q = 0; q < 12; ++q) {
+          float4 v = g4[q];
+          float gv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            int idx = 4 * q + m, sh = idx / 3, ax = idx % 3;
+            float &g = ax == 0 ? gx : ax == 1 ? gy : gz;
+            g = fmaf(Tsh[sh], gv[m], g);
+          }
+        }
+        dr = warp_allsum(dr);
+        gx = warp_allsum(gx);
+        gy = warp_allsum(gy);
+        gz = warp_allsum(gz);
+        if (lane == 0) {
+          float *rd = red[t & 1][warp][k];
+          rd[0] = dr, rd[1] = gx, rd[2] = gy, rd[3] = gz;
         }
       }
-      dr = warp_allsum(dr);
-      gx = warp_allsum(gx);
-      gy = warp_allsum(gy);
-      gz = warp_allsum(gz);
-      if (lane == 0) {
-        rd[warp][k][0] = dr;
-        rd[warp][k][1] = gx;
-        rd[warp][k][2] = gy;
-        rd[warp][k][3] = gz;
+    }
+    if constexpr (Bwd) {
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (c < cnt) {
+        int e = begin + t * T + c;
+        float sum[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          sum[q] = red[t & 1][0][c][q] + red[t & 1][1][c][q] + red[t & 1][2][c][q] + red[t & 1][3][c][q];
+        float4 v = meta[c].vec;
+        float r = v.w > 0.f ? v.w : 1e-10f;
+        float drt = sum[0] + rg * meta[c].den.y;
+        float4 f = make_float4(sum[1] + drt * v.x / r, sum[2] + drt * v.y / r, sum[3] + drt * v.z / r, 0.f);
+        if (Accumulate) {
+          float4 o = a.edge_force[e];
+          f.x += o.x, f.y += o.y, f.z += o.z;
+        }
+        a.edge_force[e] = f;
       }
     }
-    __syncthreads();
-    if (c < cnt) {
-      int e = base + c;
-      float s[4];
+    mbar_arrive(empty0 + 8 * s);
+  }
+  if constexpr (!Bwd) {
+    if (ok) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        s[q] = rd[0][c][q] + rd[1][c][q] + rd[2][c][q] + rd[3][c][q];
-      float4 v = vec[e];
-      float r = v.w > 0.f ? v.w : 1e-10f;
-      float drt = s[0] + rg * den[e].y;
-      float4 f = make_float4(s[1] + drt * v.x / r, s[2] + drt * v.y / r, s[3] + drt * v.z / r, 0.f);
-      if (Accumulate) {
-        float4 o = edge_force[e];
-        f.x += o.x, f.y += o.y, f.z += o.z;
-      }
-      edge_force[e] = f;
+      for (int k = 0; k < NC; ++k)
+        a.msg[(size_t(k) * a.n + i) * 128 + c] = acc[k];
+      if (c == 0)
+        a.rho[i] = rsum;
     }
   }
+  if (!ok) {
+    if (c == 0)
+      atomicCAS(a.status, 0, kStatusEdgeTimeout);
+    // Let the copies already issued land before the CTA's shared memory is released.
+    if (c < kStages) {
+      long long start = clock64();
+      int last = ntiles - 1 - ((ntiles - 1 - c) % kStages);
+      while (last >= 0 && !tc::mbar_try(full0 + 8 * (last % kStages), (last / kStages) & 1) &&
+             clock64() - start < tc::kWaitCycles) {
+      }
+    }
+  }
+}
+
+template <int L, bool Bwd, bool Accumulate>
+void launch_proj(cudaStream_t s, int blocks, const ProjArgs &a, const TPValues &cg) {
+  constexpr int smem = kStages * Stage<L, Bwd>::BYTES;
+  static_assert(Stage<L, Bwd>::BYTES % 128 == 0 || true, "");
+  lapis::check(
+      cudaFuncSetAttribute(edge_proj_kernel<L, Bwd, Accumulate>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  lapis::launch(edge_proj_kernel<L, Bwd, Accumulate>, blocks, kThreads, smem, s, a, cg);
+}
+
+ProjArgs proj_args(const DeviceGeometry &g, const Layer &l, EdgeArrays ea, RadialOut ro, const ProjectionChunk &k,
+                   const float *R, const float *up) {
+  ProjArgs a{};
+  a.n = g.n;
+  a.r0 = k.r0;
+  a.e_base = int(k.e0);
+  a.row = g.edge_offsets;
+  a.sender = g.edge_sender;
+  a.vec = g.edge_vector;
+  a.R = R;
+  a.Y = ea.Y;
+  a.dY = ea.dY;
+  a.cut = ea.cut;
+  a.den = ro.density;
+  a.up = up;
+  a.bias = l.radial.out_b;
+  a.status = g.status;
+  return a;
 }
 } // namespace
 
@@ -216,12 +339,13 @@ void launch_message_forward_proj(cudaStream_t s, int layer, const DeviceGeometry
   int blocks = k.r1 - k.r0;
   if (blocks <= 0)
     return;
+  ProjArgs a = proj_args(g, l, ea, ro, k, R, up);
+  a.msg = message;
+  a.rho = density;
   if (layer == 0)
-    lapis::launch(message_forward_proj_kernel<0>, blocks, 128, 0, s, g.n, k.r0, int(k.e0), g.edge_offsets,
-                  g.edge_sender, R, ea.Y, ea.cut, ro.density, up, l.radial.out_b, l.tp, message, density);
+    launch_proj<0, false, false>(s, blocks, a, l.tp);
   else
-    lapis::launch(message_forward_proj_kernel<1>, blocks, 128, 0, s, g.n, k.r0, int(k.e0), g.edge_offsets,
-                  g.edge_sender, R, ea.Y, ea.cut, ro.density, up, l.radial.out_b, l.tp, message, density);
+    launch_proj<1, false, false>(s, blocks, a, l.tp);
 }
 
 void launch_message_backward_proj(cudaStream_t s, int layer, const DeviceGeometry &g, const Layer &l,
@@ -231,21 +355,22 @@ void launch_message_backward_proj(cudaStream_t s, int layer, const DeviceGeometr
   int blocks = k.r1 - k.r0;
   if (blocks <= 0)
     return;
-#define MH1_BWD(L, A)                                                                                              \
-  lapis::launch(message_backward_proj_kernel<L, A>, blocks, 128, 0, s, g.n, k.r0, int(k.e0), g.edge_offsets,       \
-                g.edge_sender, g.edge_vector, R, dR, ea.Y, ea.dY, ea.cut, ro.density, up, l.radial.out_b, l.tp,     \
-                message_grad, density_grad, up_grad, edge_force)
+  ProjArgs a = proj_args(g, l, ea, ro, k, R, up);
+  a.dR = dR;
+  a.msg_grad = message_grad;
+  a.rho_grad = density_grad;
+  a.up_grad = up_grad;
+  a.edge_force = edge_force;
   if (layer == 0) {
     if (accumulate)
-      MH1_BWD(0, true);
+      launch_proj<0, true, true>(s, blocks, a, l.tp);
     else
-      MH1_BWD(0, false);
+      launch_proj<0, true, false>(s, blocks, a, l.tp);
   } else {
     if (accumulate)
-      MH1_BWD(1, true);
+      launch_proj<1, true, true>(s, blocks, a, l.tp);
     else
-      MH1_BWD(1, false);
+      launch_proj<1, true, false>(s, blocks, a, l.tp);
   }
-#undef MH1_BWD
 }
 } // namespace mace

@@ -27,6 +27,9 @@ struct Linear {
   std::vector<LinearPath> paths;
   std::vector<TCWeights> tc;     // per path
   const float *weight = nullptr; // device, [in_mul][out_mul] per path
+  // The paths' output blocks (forward) / input blocks (backward) are disjoint and cover the
+  // whole output, so a non-accumulating call can store each path's result directly.
+  bool fwd_tiles = false, bwd_tiles = false;
 };
 // Radial MLP weights, transposed at load for coalesced per-unit access.
 struct Radial {

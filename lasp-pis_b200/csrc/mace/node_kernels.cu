@@ -321,9 +321,14 @@ bool tensor_core_linears() {
 void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bool backward, bool add, int *status) {
   if (!n)
     return;
-  if (!add)
-    lapis::check(cudaMemsetAsync(y, 0, size_t(n) * (backward ? l.input : l.output) * 4, s));
   bool tc = tensor_core_linears() && status;
+  // Direct stores (no zero fill, no read-modify-write) when every path runs on the tensor
+  // cores and the paths' blocks tile the output.
+  bool store = !add && tc && (backward ? l.bwd_tiles : l.fwd_tiles);
+  for (const auto &t : l.tc)
+    store = store && (backward ? t.bwd_hi : t.fwd_hi);
+  if (!add && !store)
+    lapis::check(cudaMemsetAsync(y, 0, size_t(n) * (backward ? l.input : l.output) * 4, s));
   for (size_t q = 0; q < l.paths.size(); ++q) {
     const auto &p = l.paths[q];
     const float *w = l.weight + p.weight_offset;
@@ -331,7 +336,7 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
     if (!backward) {
       if (tc && t.fwd_hi) {
         tc_gemm(s, n, p.out_mul, p.in_mul, p.dim, x + size_t(p.in_offset) * n, (long long)n * p.in_mul, t.fwd_hi,
-                t.fwd_lo, y + size_t(p.out_offset) * n, p.out_mul, (long long)n * p.out_mul, true, status);
+                t.fwd_lo, y + size_t(p.out_offset) * n, p.out_mul, (long long)n * p.out_mul, !store, status);
         continue;
       }
       dim3 grid((p.out_mul + BN - 1) / BN, (n + BM - 1) / BM, p.dim);
@@ -341,7 +346,7 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
     } else {
       if (tc && t.bwd_hi) {
         tc_gemm(s, n, p.in_mul, p.out_mul, p.dim, x + size_t(p.out_offset) * n, (long long)n * p.out_mul,
-                t.bwd_hi, t.bwd_lo, y + size_t(p.in_offset) * n, p.in_mul, (long long)n * p.in_mul, true, status);
+                t.bwd_hi, t.bwd_lo, y + size_t(p.in_offset) * n, p.in_mul, (long long)n * p.in_mul, !store, status);
         continue;
       }
       dim3 grid((p.in_mul + BN - 1) / BN, (n + BM - 1) / BM, p.dim);

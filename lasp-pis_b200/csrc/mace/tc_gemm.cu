@@ -20,11 +20,12 @@
 // two slab buffers and two correction buffers (512 columns), so the MMAs of tile t+1 run
 // while tile t is drained and stored.  CTA = 8 warps (two per SM sub-partition, so the
 // drain warps may hold a full 128-column row of FP32 accumulators):
-//   warp 0      TMA producer (A, Bhi, Blo per 32-wide K slab, SWIZZLE_128B, 2-stage ring)
+//   warp 0      TMA producer (A, Bhi, Blo per 32-wide K slab, SWIZZLE_128B, 3-stage ring)
 //   warp 1      MMA issuer (one elected thread; UMMA 128 x 128 x 8)
-//   warps 2..5  drain TMEM (lane = output row) into FP32 registers, stage the row in
-//               shared memory and write it with one bulk copy per row (a bulk fp32 add
-//               into C when accumulating); rows past M are skipped
+//   warps 2..5  drain TMEM (lane = output row) into FP32 registers and write the tile in
+//               two 64-column halves: 32 x 32 boxes staged 128B-swizzled in shared memory
+//               and written by TMA tensor stores (fp32 add-reductions when accumulating);
+//               rows past M are clipped by the tensor map
 //   warps 6..7  split A into hi/lo in shared memory
 // Every mbarrier wait is bounded: on time-out the CTA records an error code in *status,
 // stops issuing work, waits (bounded) for issued MMAs and frees its TMEM.
@@ -39,12 +40,13 @@
 namespace mace {
 namespace {
 using namespace tc;
-constexpr int kBM = 128, kBN = 128, kBK = 32, kStages = 2;
+constexpr int kBM = 128, kBN = 128, kBK = 32, kStages = 3;
 constexpr int kTileBytes = kBM * kBK * 4;        // 16 KiB (A, A_lo, Bhi, Blo tiles are equal)
 constexpr int kStageBytes = 4 * kTileBytes;      // A | A_lo | Bhi | Blo
-constexpr int kRowStage = (kBN + 4) * 4;         // one staged output row, padded (528 B)
-constexpr int kStagingBytes = kBM * kRowStage;   // 66 KiB
-constexpr int kSmemBytes = 1024 /* align */ + kStages * kStageBytes + kStagingBytes + 256 /* barriers */;
+constexpr int kBoxBytes = 32 * 32 * 4;           // one 32 x 32 output box (4 KiB)
+constexpr int kStagingBytes = 4 * 2 * kBoxBytes; // half a tile: 4 drain warps x 2 boxes
+constexpr int kSmemBytes = 1024 /* align */ + kStages * kStageBytes + kStagingBytes + 128 /* barriers */;
+static_assert(kSmemBytes + 64 <= 232448, "shared memory budget");
 constexpr int kTmemCols = 4 * kBN; // hi*hi slab buffers 0/1, correction buffers 2/3 (512 columns)
 constexpr int kThreads = 256;
 constexpr int kStatusGemmTimeout = 7;
@@ -68,8 +70,8 @@ struct TileGrid {
 
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBhi,
-                   const __grid_constant__ CUtensorMap tmBlo, float *C, int ldc, long long strideC, int M,
-                   TileGrid tg, int K, int accumulate, int *status) {
+                   const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmC, TileGrid tg,
+                   int K, int accumulate, int *status) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char *staging = smem + kStages * kStageBytes;
@@ -193,9 +195,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
   } else {
     // ---------------- drain + store: lane = output row ----------------
-    int quarter = warp & 3, row_in_tile = quarter * 32 + lane;
+    int quarter = warp & 3;
     uint32_t lane_addr = tmem + (uint32_t(quarter * 32) << 16);
-    unsigned char *my_row = staging + row_in_tile * kRowStage;
+    unsigned char *boxes = staging + quarter * 2 * kBoxBytes; // this warp's two boxes
     bool ok = true;
     int g = 0, i = 0;
     for (int t = blockIdx.x; t < tg.tiles && ok; t += gridDim.x, ++i) {
@@ -226,29 +228,56 @@ __global__ void __launch_bounds__(kThreads, 1)
         int b = g & 1;
         ok = drain(uint32_t(b * kBN), tfull0 + 8 * b, (g >> 1) & 1, tfree0 + 8 * b);
       }
-      int c = i & 1;
-      if (ok)
-        ok = drain(uint32_t((2 + c) * kBN), cfull0 + 8 * c, (i >> 1) & 1, cfree0 + 8 * c);
       if (!ok)
         break;
-      // The previous tile's copy must have read this row's staging before it is rewritten.
-      bulk_wait_read();
-      float4 *dst = reinterpret_cast<float4 *>(my_row);
-#pragma unroll
-      for (int q = 0; q < kBN / 4; ++q)
-        dst[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      int row = m0 + row_in_tile;
-      if (row < M) {
-        float *out = C + z * strideC + size_t(row) * ldc + n0;
-        if (accumulate)
-          bulk_add_f32(out, smem_u32(my_row), kBN * 4);
-        else
-          bulk_store(out, smem_u32(my_row), kBN * 4);
-        bulk_commit();
+      // Correction buffer: added chunk by chunk while the tile is staged and stored.
+      int c = i & 1;
+      ok = mbar_wait(cfull0 + 8 * c, (i >> 1) & 1, &abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) {
+        ok = false;
+        break;
       }
+      tc_fence_after();
+      uint32_t corr = lane_addr + uint32_t((2 + c) * kBN);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        // The previous stores must have read the boxes before they are rewritten.
+        if (lane == 0)
+          bulk_wait_read();
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          float v[32];
+          tmem_ld32(corr + uint32_t(64 * h + 32 * j), v);
+          // Row `lane` of box j: 16-byte chunk q at position q ^ (lane & 7) (SWIZZLE_128B).
+          unsigned char *row = boxes + j * kBoxBytes + lane * 128;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float *a = acc + 64 * h + 32 * j + 4 * q;
+            *reinterpret_cast<float4 *>(row + ((q ^ (lane & 7)) << 4)) =
+                make_float4(a[0] + v[4 * q], a[1] + v[4 * q + 1], a[2] + v[4 * q + 2], a[3] + v[4 * q + 3]);
+          }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            unsigned src = smem_u32(boxes + j * kBoxBytes);
+            int x = n0 + 64 * h + 32 * j, y = m0 + 32 * quarter;
+            if (accumulate)
+              tma_add_3d(&tmC, src, x, y, z);
+            else
+              tma_store_3d(&tmC, src, x, y, z);
+          }
+          bulk_commit();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(cfree0 + 8 * c);
     }
-    bulk_wait();
+    if (lane == 0)
+      bulk_wait();
   }
   tc_fence_before();
   __syncthreads();
@@ -285,15 +314,18 @@ EncodeFn encoder() {
   return fn;
 }
 
-// Tensor map over `rows` x `cols` fp32 (row-major, ld = cols) [x `batch` planes when rank 3],
-// box 32 (cols) x 128 (rows) [x 1].
-CUtensorMap make_map(const float *base, int cols, int rows, int rank, int batch, long long batch_stride) {
-  if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * 4) % 16 || (batch_stride * 4) % 16)
+// Tensor map over `rows` x `cols` fp32 (row stride `ld` elements, default cols) [x `batch`
+// planes when rank 3], box 32 (cols) x `box_rows` (rows) [x 1], SWIZZLE_128B.
+CUtensorMap make_map(const float *base, int cols, int rows, int rank, int batch, long long batch_stride,
+                     int ld = 0, int box_rows = kBM) {
+  if (!ld)
+    ld = cols;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 4) % 16 || (batch_stride * 4) % 16)
     throw lapis::Error("tensor-core GEMM operand is not 16-byte aligned");
   CUtensorMap map;
   cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(rows), cuuint64_t(batch)};
-  cuuint64_t strides[2] = {cuuint64_t(cols) * 4, cuuint64_t(batch_stride) * 4};
-  cuuint32_t box[3] = {kBK, kBM, 1};
+  cuuint64_t strides[2] = {cuuint64_t(ld) * 4, cuuint64_t(batch_stride) * 4};
+  cuuint32_t box[3] = {kBK, cuuint32_t(box_rows), 1};
   cuuint32_t elem[3] = {1, 1, 1};
   CUresult r = encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, cuuint32_t(rank), const_cast<float *>(base), dims,
                          strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -334,6 +366,8 @@ void tc_gemm(cudaStream_t s, int M, int N, int K, int batch, const float *A, lon
   // A as [batch][M][K] (always a rank-3 map: the kernel issues 3D loads); B as [N][K].
   CUtensorMap ma = make_map(A, K, M, 3, batch, batch > 1 ? strideA : (long long)M * K);
   CUtensorMap mh = make_map(Bhi, K, N, 2, 1, 0), ml = make_map(Blo, K, N, 2, 1, 0);
+  // C as [batch][M][ldc], written in 32 x 32 boxes over its first N columns.
+  CUtensorMap mc = make_map(C, N, M, 3, batch, batch > 1 ? strideC : (long long)M * ldc, ldc, 32);
   static thread_local int configured_device = -1, sms = 148;
   int device = 0;
   lapis::check(cudaGetDevice(&device));
@@ -348,7 +382,6 @@ void tc_gemm(cudaStream_t s, int M, int N, int K, int batch, const float *A, lon
     throw lapis::Error("tensor-core GEMM has too many tiles");
   tg.tiles = int(tiles);
   int grid = int(std::min<long long>(tiles, sms));
-  lapis::launch(tc_gemm_kernel, grid, kThreads, kSmemBytes, s, ma, mh, ml, C, ldc, strideC, M, tg, K,
-                int(accumulate), status);
+  lapis::launch(tc_gemm_kernel, grid, kThreads, kSmemBytes, s, ma, mh, ml, mc, tg, K, int(accumulate), status);
 }
 } // namespace mace

@@ -121,15 +121,24 @@ __device__ __forceinline__ void tmem_ld4(uint32_t taddr, float (&v)[4]) {
     v[k] = __uint_as_float(r[k]);
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-// Per-thread bulk copies shared -> global (16-byte aligned, size a multiple of 16), as a
-// plain store or an fp32 add into global memory, tracked by the issuing thread's bulk groups.
-__device__ __forceinline__ void bulk_store(void *dst, unsigned src, unsigned bytes) {
-  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+// TMA tensor store / fp32 add-reduction of a shared-memory box into global memory (rows or
+// columns outside the tensor are skipped), tracked by the issuing thread's bulk groups.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, unsigned src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(map),
+               "r"(src), "r"(x), "r"(y), "r"(z)
                : "memory");
 }
-__device__ __forceinline__ void bulk_add_f32(void *dst, unsigned src, unsigned bytes) {
-  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(dst), "r"(src),
-               "r"(bytes)
+__device__ __forceinline__ void tma_add_3d(const CUtensorMap *map, unsigned src, int x, int y, int z) {
+  asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   map),
+               "r"(src), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+// Contiguous bulk copy global -> this CTA's shared memory, completing on an mbarrier
+// (addresses 16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(unsigned dst, const void *src, unsigned bytes, unsigned bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
