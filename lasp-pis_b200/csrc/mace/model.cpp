@@ -8,8 +8,10 @@
 // transposed at load (as the reference does) for coalesced per-unit reads, and the
 // tensor-product terms are mapped onto the term table compiled into the edge kernels.
 #include "model.hpp"
+#include "product_table.h"
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <map>
@@ -336,6 +338,26 @@ void ModelData::load(const std::string &path) {
           }
       }
       l.poly_out_start = make_int4(starts[0], starts[1], starts[2], starts[3]);
+      // Compiled kernels when the sorted terms are exactly this layer's compiled table.
+      auto matches = [&](const PolyABC *table, int count, const int *start, int outputs) {
+        if (int(abc.size()) != count || outputs != l.pouts || start[outputs] != count)
+          return false;
+        for (int o = 0; o < outputs; ++o)
+          if (starts[o] != start[o])
+            return false;
+        for (int t = 0; t < count; ++t)
+          if (abc[t] != (table[t].a | table[t].b << 8 | table[t].c << 16))
+            return false;
+        return true;
+      };
+      // (MACE_GENERIC_PRODUCT=1 keeps the table-driven kernels for every archive.)
+      l.poly_fixed = -1;
+      if (!std::getenv("MACE_GENERIC_PRODUCT")) {
+        if (k == 0 && matches(kPoly0, kPolyTerms0, kPolyStart0, 4))
+          l.poly_fixed = 0;
+        else if (k == 1 && matches(kPoly1, kPolyTerms1, kPolyStart1, 1))
+          l.poly_fixed = 1;
+      }
       l.poly_abc = reinterpret_cast<const int *>(device.upload(abc.data(), abc.size() * 4));
       l.poly_coef_sorted = up(sorted);
     }

@@ -60,6 +60,9 @@ struct Layer {
   const int *poly_abc;
   const float *poly_coef_sorted;
   int4 poly_out_start;
+  // Which compiled product table (product_table.h) the sorted terms equal, or -1 (generic
+  // table-driven kernels).
+  int poly_fixed = -1;
   int npoly, pouts, paths, in_comp, out_comp;
 };
 

@@ -12,6 +12,8 @@
 // Normalisation and gating are fused into one pass (forward) and one pass with the
 // normalisation VJP (backward); the reference launches them separately.
 #include "model.hpp"
+#include "product_table.h"
+#include <type_traits>
 #include "../lapis/launch.cuh"
 #include <cstdlib>
 #include <string>
@@ -269,6 +271,112 @@ __global__ void __launch_bounds__(256) product_backward_kernel(int n, const int 
   }
 }
 
+// Compiled product basis (product_table.h): the term structure is known at compile time,
+// so a thread keeps its nodes' 16 components (plus the constant 1 at index 16) and their
+// gradients in registers and every term is ((coef * v[a]) * v[b]) * v[c] with constant
+// indices.  Every partial product carries the term's own coefficient, so no product is
+// shared between terms and only the components and gradients stay live.  Thread = channel
+// of a 32-channel slice, two nodes at a time so each coefficient read from shared memory
+// serves both.
+template <int L> struct PolyTable;
+template <> struct PolyTable<0> {
+  static constexpr int NT = kPolyTerms0, NOUT = 4;
+  static constexpr int start(int o) { return kPolyStart0[o]; }
+  static constexpr PolyABC term(int k) { return kPoly0[k]; }
+};
+template <> struct PolyTable<1> {
+  static constexpr int NT = kPolyTerms1, NOUT = 1;
+  static constexpr int start(int o) { return kPolyStart1[o]; }
+  static constexpr PolyABC term(int k) { return kPoly1[k]; }
+};
+template <int I, int N> struct PUnroll {
+  template <class F> __device__ __forceinline__ static void run(F &&f) {
+    f(std::integral_constant<int, I>{});
+    PUnroll<I + 1, N>::run(f);
+  }
+};
+template <int N> struct PUnroll<N, N> {
+  template <class F> __device__ __forceinline__ static void run(F &&) {}
+};
+constexpr int kPolyPair = 2; // nodes per thread
+
+constexpr int kPolyWarps = 4;
+
+template <int L, bool Bwd>
+__global__ void __launch_bounds__(32 * kPolyWarps, Bwd ? 2 : 3)
+    product_fixed_kernel(int n, const float *coef, const float *x, const float *grad, float *y) {
+  using PT = PolyTable<L>;
+  extern __shared__ float cs[]; // [NT][32]
+  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, c0 = blockIdx.x * 32;
+  for (int k = threadIdx.x; k < PT::NT * 32; k += blockDim.x)
+    cs[k] = coef[size_t(k >> 5) * 512 + c0 + (k & 31)];
+  __syncthreads();
+  int i0 = blockIdx.y * kProdNodes, i1 = min(n, i0 + kProdNodes);
+  for (int ib = i0 + warp * kPolyPair; ib < i1; ib += kPolyWarps * kPolyPair) {
+    float v[kPolyPair][17];
+#pragma unroll
+    for (int q = 0; q < kPolyPair; ++q) {
+      int i = ib + q;
+#pragma unroll
+      for (int m = 0; m < 16; ++m)
+        v[q][m] = i < i1 ? x[(size_t(m) * n + i) * 512 + c0 + lane] : 0.f;
+      v[q][16] = 1.f;
+    }
+    if constexpr (!Bwd) {
+      PUnroll<0, PT::NOUT>::run([&](auto oc) {
+        constexpr int o = decltype(oc)::value;
+        float acc[kPolyPair] = {};
+        PUnroll<PT::start(o), PT::start(o + 1)>::run([&](auto kc) {
+          constexpr int k = decltype(kc)::value;
+          constexpr PolyABC t = PT::term(k);
+          float cf = cs[k * 32 + lane];
+#pragma unroll
+          for (int q = 0; q < kPolyPair; ++q)
+            acc[q] = fmaf((cf * v[q][t.a]) * v[q][t.b], v[q][t.c], acc[q]);
+        });
+#pragma unroll
+        for (int q = 0; q < kPolyPair; ++q)
+          if (ib + q < i1)
+            y[(size_t(o) * n + ib + q) * 512 + c0 + lane] = acc[q];
+      });
+    } else {
+      float g[kPolyPair][17];
+#pragma unroll
+      for (int q = 0; q < kPolyPair; ++q)
+#pragma unroll
+        for (int m = 0; m < 17; ++m)
+          g[q][m] = 0.f;
+      PUnroll<0, PT::NOUT>::run([&](auto oc) {
+        constexpr int o = decltype(oc)::value;
+        float G[kPolyPair];
+#pragma unroll
+        for (int q = 0; q < kPolyPair; ++q)
+          G[q] = ib + q < i1 ? grad[(size_t(o) * n + ib + q) * 512 + c0 + lane] : 0.f;
+        PUnroll<PT::start(o), PT::start(o + 1)>::run([&](auto kc) {
+          constexpr int k = decltype(kc)::value;
+          constexpr PolyABC t = PT::term(k);
+          float cf = cs[k * 32 + lane];
+#pragma unroll
+          for (int q = 0; q < kPolyPair; ++q) {
+            float w = cf * G[q];
+            g[q][t.a] = fmaf(w * v[q][t.b], v[q][t.c], g[q][t.a]);
+            if constexpr (t.b != 16)
+              g[q][t.b] = fmaf(w * v[q][t.a], v[q][t.c], g[q][t.b]);
+            if constexpr (t.c != 16)
+              g[q][t.c] = fmaf(w * v[q][t.a], v[q][t.b], g[q][t.c]);
+          }
+        });
+      });
+#pragma unroll
+      for (int q = 0; q < kPolyPair; ++q)
+        if (ib + q < i1)
+#pragma unroll
+          for (int m = 0; m < 16; ++m)
+            y[(size_t(m) * n + ib + q) * 512 + c0 + lane] = g[q][m];
+    }
+  }
+}
+
 __global__ void add_kernel(size_t count, const float *a, float *b, float scale) {
   size_t k = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (k < count)
@@ -374,9 +482,24 @@ size_t product_smem(int count, bool backward) {
   return (size_t(count) * 32 + ((count + 3) & ~3)) * 4 + size_t(kProdWarps) * (backward ? 2 : 1) * kProdV * 32 * 4;
 }
 
+template <int L, bool Bwd>
+void launch_product_fixed(cudaStream_t s, int n, const Layer &l, const float *x, const float *grad, float *y) {
+  int smem = PolyTable<L>::NT * 32 * 4;
+  lapis::check(cudaFuncSetAttribute(product_fixed_kernel<L, Bwd>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  dim3 grid(16, (n + kProdNodes - 1) / kProdNodes);
+  lapis::launch(product_fixed_kernel<L, Bwd>, grid, 32 * kPolyWarps, smem, s, n, l.poly_coef_sorted, x, grad, y);
+}
+
 void launch_product(cudaStream_t s, int n, const Layer &l, const float *x, float *y) {
   if (!n)
     return;
+  if (l.poly_fixed >= 0) {
+    if (l.poly_fixed == 0)
+      launch_product_fixed<0, false>(s, n, l, x, nullptr, y);
+    else
+      launch_product_fixed<1, false>(s, n, l, x, nullptr, y);
+    return;
+  }
   size_t smem = product_smem(l.npoly, false);
   lapis::check(cudaFuncSetAttribute(product_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   dim3 grid(16, (n + kProdNodes - 1) / kProdNodes);
@@ -386,6 +509,13 @@ void launch_product(cudaStream_t s, int n, const Layer &l, const float *x, float
 void launch_product_backward(cudaStream_t s, int n, const Layer &l, const float *x, const float *grad, float *xg) {
   if (!n)
     return;
+  if (l.poly_fixed >= 0) {
+    if (l.poly_fixed == 0)
+      launch_product_fixed<0, true>(s, n, l, x, grad, xg);
+    else
+      launch_product_fixed<1, true>(s, n, l, x, grad, xg);
+    return;
+  }
   size_t smem = product_smem(l.npoly, true);
   lapis::check(
       cudaFuncSetAttribute(product_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));

@@ -108,11 +108,13 @@ np.savez({out!r}, **r)
 """
 
 
-@pytest.mark.parametrize("env", [{"MACE_PROJECTION_CHUNK_EDGES": "3000"}, {"MACE_SIMT_LINEARS": "1"}],
-                         ids=["projection-chunks", "simt-edges"])
+@pytest.mark.parametrize("env", [{"MACE_PROJECTION_CHUNK_EDGES": "3000"}, {"MACE_SIMT_LINEARS": "1"},
+                                 {"MACE_GENERIC_PRODUCT": "1"}],
+                         ids=["projection-chunks", "simt-edges", "generic-product"])
 def test_engine_variants_match_oracle(library, archive_path, oracle_model, env, tmp_path):
-    """The chunked projection path (many receiver-aligned chunks, R recomputed in the backward)
-    and the SIMT edge/linear path give the oracle's results as well."""
+    """The chunked projection path (many receiver-aligned chunks, R recomputed in the backward),
+    the SIMT edge/linear path and the table-driven product kernels give the oracle's results
+    as well."""
     import os
     import sys
     out = tmp_path / "r.npz"
