@@ -35,6 +35,8 @@ ROOT = Path(__file__).resolve().parent
 sys.path[:0] = [str(ROOT / "lasp-pis_b200" / "python")]
 DATA = ROOT / "lasp-pis_b200" / "data"
 METRIC = "atoms*evals/s (E+F+virial), MH1-shape, C3 10k-atom cell"
+WORKLOADS = {"C1": "64-atom simple-cubic cell (a = 9 A)", "C2": "1,000-atom triclinic Poisson-disk cell",
+             "C3": "10,000-atom perturbed FCC cube, 46.4 A", "C5": "~200,000-atom perturbed BCC Fe/Ni/Cr slab"}
 UNIT = "atoms*evals/s"
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
@@ -264,8 +266,9 @@ def main():
             "metric": METRIC, "value": world * n * args.steps / (dev_ms * 1e-3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "C3: 10,000-atom perturbed FCC cube, 46.4 A, cutoff 6 A, seeded synthetic "
-                                   "MH1-shaped archive (seed 20261201)", "atoms_per_gpu": n, "edges_per_gpu": edges,
+            "config": {"workload": f"{args.config}: {WORKLOADS.get(args.config, args.config)}, cutoff 6 A, seeded "
+                                   "synthetic MH1-shaped archive (seed 20261201)", "atoms_per_gpu": n,
+                       "edges_per_gpu": edges,
                        "parallelism": f"dp{world} (independent structures)",
                        "l2": "256 MiB buffer written between timed steps (outside the per-step event windows)"},
             "e2e": {"value": world * n * args.steps / (e2e_ms * 1e-3), "unit": UNIT,

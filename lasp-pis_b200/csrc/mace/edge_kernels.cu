@@ -120,55 +120,105 @@ __global__ void geometry_kernel(DeviceGeometry g, const int *species, const floa
   }
 }
 
-// ---------------- radial MLP (warp per group of 4 edges) ----------------
+// ---------------- radial MLP (thread per edge) ----------------
+// Each thread owns one edge.  A layer's 64 outputs and their r-tangents accumulate in
+// registers from warp-wide broadcast float4 weight reads, then go to the thread's own padded
+// shared-memory row (stride 65: conflict-free), where LayerNorm (in-thread sums) and SiLU
+// run as rolled loops -- keeping the kernel small enough for the instruction cache -- and
+// leave the next layer's input in place.  The final rows are written out coalesced.
 struct RadialParams {
   Radial conv, dens;
 };
-// Shared layout: conv input [10][64], conv W1/W2 [64][64], density input [10][64], 13 x 64
-// vectors (biases, gammas, betas, density output), then per-warp staging [2][64][4].
-constexpr int kRadialSmemFloats = 640 + 2 * 4096 + 640 + 13 * 64 + 4 * 2 * 64 * 4;
+constexpr int kRadialThreads = 128, kRadialRow = 65;
+// Shared layout (floats): conv input [10][64], W2 / W3 [64 in][64 out], density input
+// [10][64], 13 vectors of 64, then per-thread rows [128][2][65] (value, tangent).
+constexpr int kRadialSmemFloats = 640 + 2 * 4096 + 640 + 13 * 64 + kRadialThreads * 2 * kRadialRow;
 
-// LayerNorm (biased variance, eps 1e-5) + SiLU with its tangent, for 4 edges in a warp;
-// lane holds units lane and lane + 32.
-__device__ __forceinline__ void ln_silu(float (&a)[4][2], float (&da)[4][2], const float *gamma,
-                                        const float *beta, int lane) {
+// Store accumulators to the row, then LayerNorm (biased variance, eps 1e-5) + SiLU with the
+// forward tangent, in place.
+__device__ __forceinline__ void row_ln_silu(const float (&a)[64], const float (&da)[64], float *row, float *drow,
+                                            const float *gamma, const float *beta) {
+  float s0 = 0.f, s1 = 0.f, d0 = 0.f, d1 = 0.f;
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    float mean = warp_allsum(a[e][0] + a[e][1]) * (1.f / 64);
-    float dmean = warp_allsum(da[e][0] + da[e][1]) * (1.f / 64);
-    a[e][0] -= mean, a[e][1] -= mean;
-    da[e][0] -= dmean, da[e][1] -= dmean;
-    float inv = rsqrtf(warp_allsum(a[e][0] * a[e][0] + a[e][1] * a[e][1]) * (1.f / 64) + 1e-5f);
-    float dinv = -inv * inv * inv * warp_allsum(a[e][0] * da[e][0] + a[e][1] * da[e][1]) * (1.f / 64);
+  for (int u = 0; u < 64; u += 2) {
+    row[u] = a[u], row[u + 1] = a[u + 1];
+    drow[u] = da[u], drow[u + 1] = da[u + 1];
+    s0 += a[u], s1 += a[u + 1];
+    d0 += da[u], d1 += da[u + 1];
+  }
+  float mean = (s0 + s1) * (1.f / 64), dmean = (d0 + d1) * (1.f / 64);
+  float v0 = 0.f, v1 = 0.f, c0 = 0.f, c1 = 0.f;
+#pragma unroll 4
+  for (int u = 0; u < 64; u += 2) {
+    float x0 = row[u] - mean, x1 = row[u + 1] - mean;
+    float t0 = drow[u] - dmean, t1 = drow[u + 1] - dmean;
+    v0 = fmaf(x0, x0, v0), v1 = fmaf(x1, x1, v1);
+    c0 = fmaf(x0, t0, c0), c1 = fmaf(x1, t1, c1);
+  }
+  float inv = rsqrtf((v0 + v1) * (1.f / 64) + 1e-5f);
+  float dinv = -inv * inv * inv * (c0 + c1) * (1.f / 64);
+#pragma unroll 2
+  for (int u = 0; u < 64; ++u) {
+    float xc = row[u] - mean, tc = drow[u] - dmean;
+    float x = xc * inv * gamma[u] + beta[u];
+    float sg = sigm(x);
+    float dx = (tc * inv + xc * dinv) * gamma[u];
+    row[u] = x * sg;
+    drow[u] = dx * sg * (1.f + x * (1.f - sg));
+  }
+}
+
+// First layer: a = b0 + source[zs] + target[zr] + W1 x, da = W1 dx.
+__device__ __forceinline__ void radial_input(float (&a)[64], float (&da)[64], const float *w1, const float *b0,
+                                             const float *source, const float *target, int zs, int zr,
+                                             const float (&x)[10], const float (&dx)[10]) {
+  const float4 *src = reinterpret_cast<const float4 *>(source + zs * 64);
+  const float4 *tgt = reinterpret_cast<const float4 *>(target + zr * 64);
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      int t = lane + 32 * q;
-      float u = a[e][q] * inv * gamma[t] + beta[t];
-      float s = sigm(u);
-      float du = (da[e][q] * inv + a[e][q] * dinv) * gamma[t];
-      a[e][q] = u * s;
-      da[e][q] = du * s * (1.f + u * (1.f - s));
+  for (int q = 0; q < 16; ++q) {
+    float4 sv = __ldg(src + q), tv = __ldg(tgt + q);
+    a[4 * q] = b0[4 * q] + sv.x + tv.x;
+    a[4 * q + 1] = b0[4 * q + 1] + sv.y + tv.y;
+    a[4 * q + 2] = b0[4 * q + 2] + sv.z + tv.z;
+    a[4 * q + 3] = b0[4 * q + 3] + sv.w + tv.w;
+    da[4 * q] = da[4 * q + 1] = da[4 * q + 2] = da[4 * q + 3] = 0.f;
+  }
+#pragma unroll 1
+  for (int k = 0; k < 10; ++k) {
+    const float4 *w = reinterpret_cast<const float4 *>(w1 + k * 64);
+    float xk = x[k], dxk = dx[k];
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      float4 wv = w[q];
+      a[4 * q] = fmaf(wv.x, xk, a[4 * q]);
+      a[4 * q + 1] = fmaf(wv.y, xk, a[4 * q + 1]);
+      a[4 * q + 2] = fmaf(wv.z, xk, a[4 * q + 2]);
+      a[4 * q + 3] = fmaf(wv.w, xk, a[4 * q + 3]);
+      da[4 * q] = fmaf(wv.x, dxk, da[4 * q]);
+      da[4 * q + 1] = fmaf(wv.y, dxk, da[4 * q + 1]);
+      da[4 * q + 2] = fmaf(wv.z, dxk, da[4 * q + 2]);
+      da[4 * q + 3] = fmaf(wv.w, dxk, da[4 * q + 3]);
     }
   }
 }
 
-__global__ void __launch_bounds__(128) radial_kernel(long long E, RadialParams R, const int *pair,
-                                                     EdgeArrays ea, RadialOut ro) {
+__global__ void __launch_bounds__(kRadialThreads) radial_kernel(long long E, RadialParams R, const int *pair,
+                                                                EdgeArrays ea, RadialOut ro) {
   extern __shared__ float sm[];
-  float *c_in = sm, *c_w1 = c_in + 640, *c_w2 = c_w1 + 4096, *d_in = c_w2 + 4096, *misc = d_in + 640;
-  float *c_b0 = misc, *c_b1 = misc + 64, *c_b2 = misc + 128, *d_b0 = misc + 192, *d_out = misc + 256;
-  float *c_g = misc + 320, *c_bt = c_g + 192, *d_g = c_bt + 192, *d_bt = d_g + 64;
-  float *stage = d_bt + 64; // [warp][2][64][4]
+  float *c_in = sm, *c_w1 = c_in + 640, *c_w2 = c_w1 + 4096, *d_in = c_w2 + 4096, *vecs = d_in + 640;
+  float *c_b0 = vecs, *c_b1 = vecs + 64, *c_b2 = vecs + 128, *d_b0 = vecs + 192, *d_out = vecs + 256;
+  float *c_g = vecs + 320, *c_bt = c_g + 192, *d_g = c_bt + 192, *d_bt = d_g + 64;
+  float *rows = vecs + 13 * 64;
   int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  for (int k = t; k < 640; k += 128) {
+  for (int k = t; k < 640; k += kRadialThreads) {
     c_in[k] = R.conv.input_t[k];
     d_in[k] = R.dens.input_t[k];
   }
-  for (int k = t; k < 4096; k += 128) {
+  for (int k = t; k < 4096; k += kRadialThreads) {
     c_w1[k] = R.conv.weight_t[1][k];
     c_w2[k] = R.conv.weight_t[2][k];
   }
-  for (int k = t; k < 64; k += 128) {
+  for (int k = t; k < 64; k += kRadialThreads) {
     c_b0[k] = R.conv.bias0[k];
     c_b1[k] = R.conv.bias[1][k];
     c_b2[k] = R.conv.bias[2][k];
@@ -183,111 +233,76 @@ __global__ void __launch_bounds__(128) radial_kernel(long long E, RadialParams R
   }
   __syncthreads();
   float d_ob = R.dens.out_b[0];
-  float4 *hs = reinterpret_cast<float4 *>(stage + warp * 512), *dhs = hs + 64;
-  long long groups = (E + 3) / 4;
-  for (long long grp = blockIdx.x * 4ll + warp; grp < groups; grp += gridDim.x * 4ll) {
-    long long e0 = grp * 4;
-    int zs[4], zr[4];
-    float x[4][10], dx[4][10], cutv[4][2];
+  float *my = rows + t * 2 * kRadialRow, *my_d = my + kRadialRow;
+  for (long long base = (long long)blockIdx.x * kRadialThreads; base < E; base += (long long)gridDim.x * kRadialThreads) {
+    long long e = base + t;
+    bool ok = e < E;
+    int p = ok ? pair[e] : 0, zs = p & 0xffff, zr = p >> 16;
+    float x[10], dx[10];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      bool ok = e0 + e < E;
-      int p = ok ? pair[e0 + e] : 0;
-      zs[e] = p & 0xffff;
-      zr[e] = p >> 16;
-      float2 cv = ok ? ea.cut[e0 + e] : make_float2(0.f, 0.f);
-      cutv[e][0] = cv.x;
-      cutv[e][1] = cv.y;
-#pragma unroll
-      for (int k = 0; k < 10; ++k) {
-        x[e][k] = ok ? ea.basis[(e0 + e) * 10 + k] : 0.f;
-        dx[e][k] = ok ? ea.dbasis[(e0 + e) * 10 + k] : 0.f;
-      }
+    for (int k = 0; k < 10; ++k) {
+      x[k] = ok ? ea.basis[e * 10 + k] : 0.f;
+      dx[k] = ok ? ea.dbasis[e * 10 + k] : 0.f;
     }
+    float2 cv = ok ? ea.cut[e] : make_float2(0.f, 0.f);
+    float a[64], da[64];
     // ---- conv radial network: 10 -> 64 -> 64 -> 64 ----
-    float a[4][2], da[4][2];
-#pragma unroll
-    for (int e = 0; e < 4; ++e)
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        int u = lane + 32 * q;
-        float s = c_b0[u] + R.conv.source[zs[e] * 64 + u] + R.conv.target[zr[e] * 64 + u], ds = 0.f;
-#pragma unroll
-        for (int k = 0; k < 10; ++k) {
-          float w = c_in[k * 64 + u];
-          s = fmaf(w, x[e][k], s);
-          ds = fmaf(w, dx[e][k], ds);
-        }
-        a[e][q] = s;
-        da[e][q] = ds;
-      }
-    ln_silu(a, da, c_g, c_bt, lane);
-#pragma unroll
+    radial_input(a, da, c_in, c_b0, R.conv.source, R.conv.target, zs, zr, x, dx);
+    row_ln_silu(a, da, my, my_d, c_g, c_bt);
+#pragma unroll 1
     for (int layer = 1; layer < 3; ++layer) {
       const float *W = layer == 1 ? c_w1 : c_w2, *bias = layer == 1 ? c_b1 : c_b2;
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        int u = lane + 32 * q;
-        hs[u] = make_float4(a[0][q], a[1][q], a[2][q], a[3][q]);
-        dhs[u] = make_float4(da[0][q], da[1][q], da[2][q], da[3][q]);
+      for (int u = 0; u < 64; ++u) {
+        a[u] = bias[u];
+        da[u] = 0.f;
       }
-      __syncwarp();
-      float b0 = bias[lane], b1 = bias[lane + 32];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        a[e][0] = b0, a[e][1] = b1;
-        da[e][0] = da[e][1] = 0.f;
-      }
-#pragma unroll 8
+#pragma unroll 1
       for (int k = 0; k < 64; ++k) {
-        float4 hv = hs[k], dv = dhs[k];
-        float w0 = W[k * 64 + lane], w1 = W[k * 64 + lane + 32];
-        float hv4[4] = {hv.x, hv.y, hv.z, hv.w}, dv4[4] = {dv.x, dv.y, dv.z, dv.w};
+        float hv = my[k], dv = my_d[k];
+        const float4 *w = reinterpret_cast<const float4 *>(W + k * 64);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          a[e][0] = fmaf(w0, hv4[e], a[e][0]);
-          a[e][1] = fmaf(w1, hv4[e], a[e][1]);
-          da[e][0] = fmaf(w0, dv4[e], da[e][0]);
-          da[e][1] = fmaf(w1, dv4[e], da[e][1]);
+        for (int q = 0; q < 16; ++q) {
+          float4 wv = w[q];
+          a[4 * q] = fmaf(wv.x, hv, a[4 * q]);
+          a[4 * q + 1] = fmaf(wv.y, hv, a[4 * q + 1]);
+          a[4 * q + 2] = fmaf(wv.z, hv, a[4 * q + 2]);
+          a[4 * q + 3] = fmaf(wv.w, hv, a[4 * q + 3]);
+          da[4 * q] = fmaf(wv.x, dv, da[4 * q]);
+          da[4 * q + 1] = fmaf(wv.y, dv, da[4 * q + 1]);
+          da[4 * q + 2] = fmaf(wv.z, dv, da[4 * q + 2]);
+          da[4 * q + 3] = fmaf(wv.w, dv, da[4 * q + 3]);
         }
       }
-      __syncwarp();
-      ln_silu(a, da, c_g + layer * 64, c_bt + layer * 64, lane);
+      row_ln_silu(a, da, my, my_d, c_g + layer * 64, c_bt + layer * 64);
     }
-#pragma unroll
-    for (int e = 0; e < 4; ++e)
-      if (e0 + e < E)
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          ro.h[(e0 + e) * 64 + lane + 32 * q] = a[e][q];
-          ro.dh[(e0 + e) * 64 + lane + 32 * q] = da[e][q];
-        }
+    // ---- coalesced write of h / dh: 32 consecutive edges per warp ----
+    __syncwarp();
+    long long wbase = base + warp * 32;
+    const float *wrows = rows + warp * 32 * 2 * kRadialRow;
+#pragma unroll 1
+    for (int r = 0; r < 32 && wbase + r < E; ++r) {
+      const float *src = wrows + r * 2 * kRadialRow;
+      size_t o = size_t(wbase + r) * 64;
+      ro.h[o + lane] = src[lane];
+      ro.h[o + 32 + lane] = src[32 + lane];
+      ro.dh[o + lane] = src[kRadialRow + lane];
+      ro.dh[o + 32 + lane] = src[kRadialRow + 32 + lane];
+    }
+    __syncwarp();
     // ---- density network: 10 -> 64, LayerNorm + SiLU, -> 1, tanh(a^2) x cutoff ----
-#pragma unroll
-    for (int e = 0; e < 4; ++e)
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        int u = lane + 32 * q;
-        float s = d_b0[u] + R.dens.source[zs[e] * 64 + u] + R.dens.target[zr[e] * 64 + u], ds = 0.f;
-#pragma unroll
-        for (int k = 0; k < 10; ++k) {
-          float w = d_in[k * 64 + u];
-          s = fmaf(w, x[e][k], s);
-          ds = fmaf(w, dx[e][k], ds);
-        }
-        a[e][q] = s;
-        da[e][q] = ds;
-      }
-    ln_silu(a, da, d_g, d_bt, lane);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float s = warp_allsum(d_out[lane] * a[e][0] + d_out[lane + 32] * a[e][1]) + d_ob;
-      float ds = warp_allsum(d_out[lane] * da[e][0] + d_out[lane + 32] * da[e][1]);
-      if (lane == 0 && e0 + e < E) {
-        float den = tanhf(s * s);
-        ro.density[e0 + e] =
-            make_float2(den * cutv[e][0], 2.f * s * ds * (1.f - den * den) * cutv[e][0] + den * cutv[e][1]);
-      }
+    radial_input(a, da, d_in, d_b0, R.dens.source, R.dens.target, zs, zr, x, dx);
+    row_ln_silu(a, da, my, my_d, d_g, d_bt);
+    float sv = d_ob, dsv = 0.f;
+#pragma unroll 4
+    for (int u = 0; u < 64; ++u) {
+      sv = fmaf(d_out[u], my[u], sv);
+      dsv = fmaf(d_out[u], my_d[u], dsv);
+    }
+    __syncwarp();
+    if (ok) {
+      float den = tanhf(sv * sv);
+      ro.density[e] = make_float2(den * cv.x, 2.f * sv * dsv * (1.f - den * den) * cv.x + den * cv.y);
     }
   }
 }
@@ -581,9 +596,9 @@ void launch_radial(cudaStream_t s, const DeviceGeometry &g, const Layer &l, cons
     return;
   size_t smem = kRadialSmemFloats * sizeof(float);
   lapis::check(cudaFuncSetAttribute(radial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  long long groups = (E + 3) / 4;
-  int blocks = int(std::min<long long>((groups + 3) / 4, 148 * 8));
-  lapis::launch(radial_kernel, blocks, 128, smem, s, E, RadialParams{l.radial, l.density}, pair, ea, ro);
+  long long tiles = (E + kRadialThreads - 1) / kRadialThreads;
+  int blocks = int(std::min<long long>(tiles, 148 * 2));
+  lapis::launch(radial_kernel, blocks, kRadialThreads, smem, s, E, RadialParams{l.radial, l.density}, pair, ea, ro);
 }
 
 void launch_message_forward(cudaStream_t s, int layer, const DeviceGeometry &g, const Layer &l, EdgeArrays ea,

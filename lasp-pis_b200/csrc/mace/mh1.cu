@@ -175,6 +175,8 @@ Result MH1::evaluate() {
       for (auto &q : chunks) {
         tc_gemm(s, int(q.e1 - q.e0), width, 64, 1, ro[k].h + q.e0 * 64, 0, l.radial.out_hi, l.radial.out_lo,
                 proj[k], width, 0, false, status);
+        if (chunks.size() == 1)
+          timer.mark("forward" + std::to_string(k) + ".projection");
         launch_message_forward_proj(s, k, c.geometry, l, ea, ro[k], q, proj[k], up[k], msg, rho[k]);
       }
     } else if (tensor_core_edges())
@@ -238,6 +240,8 @@ Result MH1::evaluate() {
         else
           tc_gemm(s, rows, width, 64, 2, ro[k].h + q.e0 * 64, (long long)E * 64, l.radial.out_hi,
                   l.radial.out_lo, R, width, (long long)chunk_cap * width, false, status);
+        if (chunks.size() == 1)
+          timer.mark("backward" + std::to_string(k) + ".projection");
         launch_message_backward_proj(s, k, c.geometry, l, ea, ro[k], q, R, dR, up[k], msggrad, rhograd, upgrad,
                                      edge_force, k == 0);
       }
