@@ -88,6 +88,7 @@ struct DeviceGeometry {
   const int *edge_sender = nullptr;    // [E]
   const int *edge_shift = nullptr;     // [E][3]
   const float4 *edge_vector = nullptr; // [E] (dx, dy, dz, r)
+  const float *edge_r2 = nullptr;      // [E] squared length compared against the cutoff
   const int *edge_reverse = nullptr;   // [E] index of the edge j <- i with the opposite shift
   long long edge_capacity = 0;
 };

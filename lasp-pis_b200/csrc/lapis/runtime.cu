@@ -193,7 +193,7 @@ struct Traverse {
 // bin order), so the edge order inside a receiver is deterministic.  Count pass when
 // out_sender == nullptr, fill pass otherwise.
 __global__ void neighbour_pass(Traverse g, int *counts, const int *row, int *out_sender, int *out_shift,
-                               float4 *out_vec) {
+                               float4 *out_vec, float *out_r2) {
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= g.n)
     return;
@@ -244,6 +244,8 @@ __global__ void neighbour_pass(Traverse g, int *counts, const int *row, int *out
             out_shift[3 * e + 1] = sy + wi1 - g.winding[3 * j + 1];
             out_shift[3 * e + 2] = sz + wi2 - g.winding[3 * j + 2];
             out_vec[e] = make_float4(dx, dy, dz, sqrtf(r2));
+            if (out_r2)
+              out_r2[e] = r2;
           }
           count += __popc(mask);
         }
@@ -509,7 +511,7 @@ void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
   tv.winding = sw;
   tv.stats = stats;
   if (n) {
-    lapis::launch(neighbour_pass, (n * 32 + 255) / 256, 256, 0, stream, tv, row_counts, nullptr, nullptr, nullptr, nullptr);
+    lapis::launch(neighbour_pass, (n * 32 + 255) / 256, 256, 0, stream, tv, row_counts, nullptr, nullptr, nullptr, nullptr, nullptr);
     lapis::launch(scan_exclusive, 1, 1024, 0, stream, row_counts, row, n, &stats->total_edges);
   }
   check(cudaGetLastError());
@@ -547,9 +549,10 @@ void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
   int *sender = array<int>("edges.sender", size_t(total));
   int *shift = array<int>("edges.shift", size_t(total) * 3);
   float4 *vec = array<float4>("edges.vector", size_t(total));
+  float *r2 = array<float>("edges.r2", size_t(total));
   int *rev = array<int>("edges.reverse", size_t(total));
   if (n && total) {
-    lapis::launch(neighbour_pass, (n * 32 + 255) / 256, 256, 0, stream, tv, nullptr, row, sender, shift, vec);
+    lapis::launch(neighbour_pass, (n * 32 + 255) / 256, 256, 0, stream, tv, nullptr, row, sender, shift, vec, r2);
     lapis::launch(reverse_edges, n, 128, 0, stream, row, sender, shift, rev, status);
   }
   check(cudaGetLastError());
@@ -570,6 +573,7 @@ void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
   geometry.edge_sender = sender;
   geometry.edge_shift = shift;
   geometry.edge_vector = vec;
+  geometry.edge_r2 = r2;
   geometry.edge_reverse = rev;
   geometry.edge_capacity = total;
 }
@@ -789,7 +793,8 @@ long long lapis_neighbor_list_static(int n, const float *xyz, const int *element
     if (n) {
       wrap_atoms<<<(n + 255) / 256, 256, 0, stream>>>(n, xyz, elements, wp, wxyz, wind, bin, grid, status);
       decide_backend<<<1, 1, 0, stream>>>(stats, 1, 0, 0.0);
-      neighbour_pass<<<(n * 32 + 255) / 256, 256, 0, stream>>>(tv, counts, nullptr, nullptr, nullptr, nullptr);
+      neighbour_pass<<<(n * 32 + 255) / 256, 256, 0, stream>>>(tv, counts, nullptr, nullptr, nullptr, nullptr,
+                                                               nullptr);
     }
     scan_exclusive<<<1, 1024, 0, stream>>>(counts, row, n, &stats->total_edges);
     check(cudaGetLastError());
@@ -808,7 +813,7 @@ long long lapis_neighbor_list_static(int n, const float *xyz, const int *element
       throw Error("Directed edge count exceeds int32 capacity");
     if (n && total && total <= capacity) {
       neighbour_pass<<<(n * 32 + 255) / 256, 256, 0, stream>>>(tv, nullptr, row, sender, shift,
-                                                               reinterpret_cast<float4 *>(vector));
+                                                               reinterpret_cast<float4 *>(vector), nullptr);
       check(cudaGetLastError());
       check(cudaStreamSynchronize(stream));
     }
