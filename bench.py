@@ -40,15 +40,21 @@ WORKLOADS = {"C1": "64-atom simple-cubic cell (a = 9 A)", "C2": "1,000-atom tric
 UNIT = "atoms*evals/s"
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+# DRAM read + write bytes per edge of the roofline kernel, from an ncu capture of the C2
+# workload (profiles/edge_backward1_C2.md: 1.0531 GB read + 8.83 MB written over 97,006
+# edges), scaled by the edge count.
+TRAFFIC_PER_EDGE = (1.053105e9 + 8.828416e6) / 97006
 
 
-def algorithmic_flops_backward1(edges: int) -> float:
-    """Algorithmic FP32 work of the layer-1 edge backward kernel per launch.
+def edge_backward1_bytes(edges: int, paths: int = 10) -> float:
+    """Algorithmic HBM bytes of the layer-1 edge tensor-product backward per launch.
 
-    Per directed edge: the r-tangent of the 64 -> 10 x 128 radial projection (2 x 64 x 1280)
-    and the tensor-product adjoints, 15 FLOP per (term, channel) x 86 terms x 128 channels.
+    Per directed edge: the radial projection row R and its r-tangent dR (2 x paths x 128 fp32),
+    Y and dY/dd (16 + 48 fp32), the edge geometry (d, r: 16 B), cutoff and density pairs
+    (8 + 8 B), the sender index (4 B) and the edge force written (16 B).  The sender's
+    up-projected features and the up-gradient atomics stay in L2 and are not counted.
     """
-    return edges * (2.0 * 64 * 1280 + 15.0 * 86 * 128)
+    return edges * (2.0 * paths * 128 * 4 + 64 + 192 + 16 + 8 + 8 + 4 + 16)
 
 
 class ClockSampler:
@@ -260,8 +266,8 @@ def main():
         pk, kind = peaks()
         edges = int(diag["edges"])
         k_ms = float(np.mean(stages.get("backward1.edges", [float("nan")])))
-        achieved = algorithmic_flops_backward1(edges) / (k_ms * 1e-3) / 1e12
-        peak = float(pk["bf16_tflops"])
+        achieved = edge_backward1_bytes(edges) / (k_ms * 1e-3) / 1e9
+        peak = float(pk["hbm_gbs"])
         line = {
             "metric": METRIC, "value": world * n * args.steps / (dev_ms * 1e-3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
@@ -273,12 +279,13 @@ def main():
                        "l2": "256 MiB buffer written between timed steps (outside the per-step event windows)"},
             "e2e": {"value": world * n * args.steps / (e2e_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": n * 16, "d2h_bytes_per_step": n * 16 + 84},
-            "roofline": {"kernel": "message_backward_kernel<1> (layer-1 edge backward, FP32 SIMT)",
-                         "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "peak_source": f"bf16_tflops ({kind}); the kernel runs on the "
-                                                                f"FP32 SIMT pipe", "traffic": None,
-                         "algorithmic_flops_per_launch": algorithmic_flops_backward1(edges),
-                         "kernel_ms": k_ms},
+            "roofline": {"kernel": "edge_proj_kernel<1, backward> (layer-1 edge tensor-product backward: "
+                                   "adjoints, r-tangent, per-edge force)",
+                         "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": f"hbm_gbs ({kind})",
+                         "traffic": TRAFFIC_PER_EDGE * edges if TRAFFIC_PER_EDGE else None,
+                         "algorithmic_bytes_per_launch": edge_backward1_bytes(edges), "kernel_ms": k_ms,
+                         "limiter": "FP32 issue (six operations per tensor-product term and channel), not HBM"},
             "stages_ms": {k: float(np.mean(v)) for k, v in stages.items()},
             "gpu_launches": int(diag["launches"]) * args.steps,
             "clocks": clocks.summary(),

@@ -18,15 +18,15 @@
 // Persistent: one CTA per SM walks the 128 x 128 output tiles (n fastest, so the CTAs that
 // run together share A tiles in L2) with a continuous pipeline across tiles.  TMEM holds
 // two slab buffers and two correction buffers (512 columns), so the MMAs of tile t+1 run
-// while tile t is drained and stored.  CTA = 8 warps (two per SM sub-partition, so the
-// drain warps may hold a full 128-column row of FP32 accumulators):
-//   warp 0      TMA producer (A, Bhi, Blo per 32-wide K slab, SWIZZLE_128B, 3-stage ring)
-//   warp 1      MMA issuer (one elected thread; UMMA 128 x 128 x 8)
-//   warps 2..5  drain TMEM (lane = output row) into FP32 registers and write the tile in
-//               two 64-column halves: 32 x 32 boxes staged 128B-swizzled in shared memory
-//               and written by TMA tensor stores (fp32 add-reductions when accumulating);
-//               rows past M are clipped by the tensor map
-//   warps 6..7  split A into hi/lo in shared memory
+// while tile t is drained and stored.  CTA = 12 warps:
+//   warp 0       TMA producer (A, Bhi, Blo per 32-wide K slab, SWIZZLE_128B, 3-stage ring)
+//   warp 1       MMA issuer (one elected thread; UMMA 128 x 128 x 8)
+//   warps 2..3   split A into hi/lo in shared memory
+//   warps 4..11  drain TMEM into FP32 registers: two warps per TMEM lane quadrant (lane =
+//                output row), each owning 64 of the 128 columns with two 32-column loads in
+//                flight; each writes its part of the tile as two 32 x 32 boxes staged
+//                128B-swizzled in shared memory and stored by TMA tensor stores (fp32
+//                add-reductions when accumulating); rows past M are clipped by the map
 // Every mbarrier wait is bounded: on time-out the CTA records an error code in *status,
 // stops issuing work, waits (bounded) for issued MMAs and frees its TMEM.
 #include "../lapis/launch.cuh"
@@ -44,11 +44,11 @@ constexpr int kBM = 128, kBN = 128, kBK = 32, kStages = 3;
 constexpr int kTileBytes = kBM * kBK * 4;        // 16 KiB (A, A_lo, Bhi, Blo tiles are equal)
 constexpr int kStageBytes = 4 * kTileBytes;      // A | A_lo | Bhi | Blo
 constexpr int kBoxBytes = 32 * 32 * 4;           // one 32 x 32 output box (4 KiB)
-constexpr int kStagingBytes = 4 * 2 * kBoxBytes; // half a tile: 4 drain warps x 2 boxes
+constexpr int kStagingBytes = 8 * kBoxBytes;     // one box per drain warp
 constexpr int kSmemBytes = 1024 /* align */ + kStages * kStageBytes + kStagingBytes + 128 /* barriers */;
 static_assert(kSmemBytes + 64 <= 232448, "shared memory budget");
 constexpr int kTmemCols = 4 * kBN; // hi*hi slab buffers 0/1, correction buffers 2/3 (512 columns)
-constexpr int kThreads = 256;
+constexpr int kThreads = 384, kDrainThreads = 256;
 constexpr int kStatusGemmTimeout = 7;
 
 // Instruction descriptor: D fp32, A/B tf32, both K-major, M = 128, N = 128.
@@ -95,9 +95,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull0 + 8 * b, 1);
-      mbar_init(tfree0 + 8 * b, 128);
+      mbar_init(tfree0 + 8 * b, kDrainThreads);
       mbar_init(cfull0 + 8 * b, 1);
-      mbar_init(cfree0 + 8 * b, 128);
+      mbar_init(cfree0 + 8 * b, kDrainThreads);
     }
     mbar_init(done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -168,9 +168,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(done);
       mma_done_issued = 1;
     }
-  } else if (warp >= 6) {
+  } else if (warp < 4) {
     // ---------------- A split: hi in place, lo beside it ----------------
-    int t = threadIdx.x - 192, g = 0;
+    int t = threadIdx.x - 64, g = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < tg.tiles && ok; tile += gridDim.x)
       for (int kt = 0; kt < ktiles; ++kt, ++g) {
@@ -194,43 +194,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(ready0 + 8 * s);
       }
   } else {
-    // ---------------- drain + store: lane = output row ----------------
-    int quarter = warp & 3;
-    uint32_t lane_addr = tmem + (uint32_t(quarter * 32) << 16);
-    unsigned char *boxes = staging + quarter * 2 * kBoxBytes; // this warp's two boxes
+    // ---------------- drain + store: lane = output row, 64 columns per warp ----------------
+    int quarter = warp & 3, col0 = 64 * ((warp - 4) >> 2);
+    uint32_t lane_addr = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(col0);
+    unsigned char *box = staging + (warp - 4) * kBoxBytes; // this warp's staging box
     bool ok = true;
     int g = 0, i = 0;
     for (int t = blockIdx.x; t < tg.tiles && ok; t += gridDim.x, ++i) {
       int n0, m0, z;
       tg.coords(t, n0, m0, z);
-      float acc[kBN];
+      float acc[64];
 #pragma unroll
-      for (int c = 0; c < kBN; ++c)
+      for (int c = 0; c < 64; ++c)
         acc[c] = 0.f;
-      auto drain = [&](uint32_t col, uint32_t full, int parity, uint32_t release) {
-        bool go = mbar_wait(full, parity, &abort_flag);
-        if (!__all_sync(0xffffffffu, go))
-          return false;
-        tc_fence_after();
-#pragma unroll
-        for (int c0 = 0; c0 < kBN; c0 += 32) {
-          float v[32];
-          tmem_ld32(lane_addr + col + uint32_t(c0), v);
-#pragma unroll
-          for (int k = 0; k < 32; ++k)
-            acc[c0 + k] += v[k];
-        }
-        tc_fence_before();
-        mbar_arrive(release);
-        return true;
-      };
-      for (int kt = 0; kt < ktiles && ok; ++kt, ++g) {
+      for (int kt = 0; kt < ktiles; ++kt, ++g) {
         int b = g & 1;
-        ok = drain(uint32_t(b * kBN), tfull0 + 8 * b, (g >> 1) & 1, tfree0 + 8 * b);
+        ok = mbar_wait(tfull0 + 8 * b, (g >> 1) & 1, &abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t r0[32], r1[32];
+        tmem_ld32_async(lane_addr + uint32_t(b * kBN), r0);
+        tmem_ld32_async(lane_addr + uint32_t(b * kBN + 32), r1);
+        tmem_wait_ld();
+        tmem_anchor(r0);
+        tmem_anchor(r1);
+        tc_fence_before();
+        mbar_arrive(tfree0 + 8 * b);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          acc[k] += __uint_as_float(r0[k]);
+          acc[32 + k] += __uint_as_float(r1[k]);
+        }
       }
       if (!ok)
         break;
-      // Correction buffer: added chunk by chunk while the tile is staged and stored.
+      // Correction buffer: added while the two boxes are staged and stored.
       int c = i & 1;
       ok = mbar_wait(cfull0 + 8 * c, (i >> 1) & 1, &abort_flag);
       if (!__all_sync(0xffffffffu, ok)) {
@@ -238,43 +239,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t corr = lane_addr + uint32_t((2 + c) * kBN);
+      uint32_t r0[32], r1[32];
+      tmem_ld32_async(lane_addr + uint32_t((2 + c) * kBN), r0);
+      tmem_ld32_async(lane_addr + uint32_t((2 + c) * kBN + 32), r1);
+      tmem_wait_ld();
+      tmem_anchor(r0);
+      tmem_anchor(r1);
+      tc_fence_before();
+      mbar_arrive(cfree0 + 8 * c);
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        // The previous stores must have read the boxes before they are rewritten.
+      for (int j = 0; j < 2; ++j) {
+        // The previous store must have read the box before it is rewritten.
         if (lane == 0)
           bulk_wait_read();
         __syncwarp();
+        // Row `lane` of the box: 16-byte chunk q at position q ^ (lane & 7) (SWIZZLE_128B).
+        unsigned char *row = box + lane * 128;
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          float v[32];
-          tmem_ld32(corr + uint32_t(64 * h + 32 * j), v);
-          // Row `lane` of box j: 16-byte chunk q at position q ^ (lane & 7) (SWIZZLE_128B).
-          unsigned char *row = boxes + j * kBoxBytes + lane * 128;
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float *a = acc + 64 * h + 32 * j + 4 * q;
-            *reinterpret_cast<float4 *>(row + ((q ^ (lane & 7)) << 4)) =
-                make_float4(a[0] + v[4 * q], a[1] + v[4 * q + 1], a[2] + v[4 * q + 2], a[3] + v[4 * q + 3]);
-          }
+        for (int q = 0; q < 8; ++q) {
+          const float *a = acc + 32 * j + 4 * q;
+          const uint32_t *r = (j ? r1 : r0) + 4 * q;
+          *reinterpret_cast<float4 *>(row + ((q ^ (lane & 7)) << 4)) =
+              make_float4(a[0] + __uint_as_float(r[0]), a[1] + __uint_as_float(r[1]),
+                          a[2] + __uint_as_float(r[2]), a[3] + __uint_as_float(r[3]));
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) {
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            unsigned src = smem_u32(boxes + j * kBoxBytes);
-            int x = n0 + 64 * h + 32 * j, y = m0 + 32 * quarter;
-            if (accumulate)
-              tma_add_3d(&tmC, src, x, y, z);
-            else
-              tma_store_3d(&tmC, src, x, y, z);
-          }
+          int x = n0 + col0 + 32 * j, y = m0 + 32 * quarter;
+          if (accumulate)
+            tma_add_3d(&tmC, smem_u32(box), x, y, z);
+          else
+            tma_store_3d(&tmC, smem_u32(box), x, y, z);
           bulk_commit();
         }
       }
-      tc_fence_before();
-      mbar_arrive(cfree0 + 8 * c);
     }
     if (lane == 0)
       bulk_wait();
