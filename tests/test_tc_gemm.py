@@ -10,7 +10,8 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-SHAPES = [(1000, 128, 128, 1), (300, 256, 2048, 3), (10000, 512, 512, 1), (130, 2048, 128, 2), (77, 128, 32, 7)]
+SHAPES = [(1000, 128, 128, 1), (300, 256, 2048, 3), (10000, 512, 512, 1), (130, 2048, 128, 2), (77, 128, 32, 7),
+          (5000, 1280, 64, 1), (3000, 512, 64, 2)]  # the last two: edge-projection shapes (K = 64)
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
