@@ -108,6 +108,7 @@ public:
   Diagnostics diagnostics;
   std::vector<KernelResources> resources;
   std::vector<int> original_elements;
+  std::vector<int> batch_offsets; // prepared batch: first atom of each cell, plus the total
   int *internal_to_original = nullptr, *original_to_internal = nullptr;
   // Device-resident inputs: when set, prepare() reads positions/elements from these
   // device pointers instead of copying host arrays (the timed device-only path).
@@ -133,6 +134,14 @@ public:
   // e0_by_z (device, indexed by atomic number) is given, each atom's baseline energy is
   // added to its energy and to the total, in float64 for the total.
   Result finish(float *energies, float *forces, float *node_virials, const float *e0_by_z = nullptr);
+  // Batch of independent periodic cells (B200 build addition, no reference counterpart):
+  // one combined graph, atoms concatenated in input order (internal order = input order),
+  // each cell wrapped with its own lattice and enumerated over its own atoms and images
+  // (all-images enumeration; the edge set equals the single-cell one), one host sync.
+  void prepare_batch(const std::vector<Structure> &cells, float cutoff, const Options &);
+  // Per-cell results of a prepared batch: energies/virials reduced per cell in float64.
+  std::vector<Result> finish_batch(float *energies, float *forces, float *node_virials,
+                                   const float *e0_by_z = nullptr);
   void synchronize();
   int status_code(); // device status word (0 ok, 1 zero distance, 2 unknown element)
 };
@@ -140,6 +149,8 @@ class Calculator {
   std::atomic_flag busy_ = ATOMIC_FLAG_INIT;
 
 protected:
+  // Batched evaluation hook: the default rejects batches (LJ and user calculators).
+  virtual std::vector<Result> evaluate_batch();
   Context context_;
   Options options_;
   float cutoff_;
@@ -149,6 +160,11 @@ public:
   Calculator(float cutoff, Options options = {}) : options_(options), cutoff_(cutoff) {}
   virtual ~Calculator() = default;
   Result calculate(const Structure &);
+  // Independent cells in one call (B200 build addition): same results as calculate() per
+  // cell up to float32 summation order; evaluated in sub-batches of at most
+  // kBatchAtoms atoms so the workspace stays bounded.  Single-flight like calculate().
+  static constexpr int kBatchAtoms = 65536;
+  std::vector<Result> calculate_batch(const std::vector<Structure> &cells);
   const Diagnostics &diagnostics() const { return context_.diagnostics; }
   const std::vector<KernelResources> &resources() const { return context_.resources; }
   Context &context() { return context_; }

@@ -78,6 +78,17 @@ MACE_EXPORT long long lapis_neighbor_edges(int n, const float *xyz, const float 
 MACE_EXPORT long long lapis_neighbor_list_static(int n, const float *xyz, const int *elements, const float *cell,
                                                  float cutoff, int *row, int *sender, int *shift, float *vector,
                                                  long long capacity, void *stream);
+/* Batch of independent periodic cells in one call (B200 build addition; the reference's
+ * callers loop over mace_calculate, mace/include/mace/c_api.h:13-14).  Cell c has sizes[c]
+ * atoms; xyz (sum(sizes) x 3, Angstrom) and Z (sum(sizes)) are the cells' arrays
+ * concatenated in order; cells is count x 9 (lattice vectors as rows).  Outputs are
+ * caller-owned: energies[count] (eV), per_atom[sum(sizes)], force[sum(sizes) x 3],
+ * virial[count x 9] (row major, -dE/d(strain)).  Per cell the results equal mace_calculate's
+ * up to float32 summation order.  Returns 0, or -1 with mace_last_error() set; an error does
+ * not poison the handle. */
+MACE_EXPORT int mace_calculate_batch(void *handle, int count, const int *sizes, const float *xyz, const int *Z,
+                                     const float *cells, double *energies, float *per_atom, float *force,
+                                     float *virial);
 #ifdef __cplusplus
 }
 #endif

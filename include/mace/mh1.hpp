@@ -7,7 +7,9 @@ namespace mace {
 class MACE_EXPORT MH1 final : public lapis::Calculator {
   struct Model;
   std::unique_ptr<Model> model_;
+  std::vector<lapis::Result> compute(bool batch); // the evaluation; one result or one per cell
   lapis::Result evaluate() override;
+  std::vector<lapis::Result> evaluate_batch() override;
 
 public:
   // PWMH1001 archive.  An empty head is required for archives (they carry one head).

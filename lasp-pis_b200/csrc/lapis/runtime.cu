@@ -314,6 +314,132 @@ __global__ void sum_partials(const double *partial, double *out) {
     out[q] = s;
   }
 }
+
+// ---------------- batches of independent cells ----------------
+struct BatchCell {
+  double inv[9], h[9];
+  float hf[9];
+  int images[3];
+  int first, count;
+};
+
+// Per-atom float64 wrap into its own cell: the same operations, order and rounding as
+// wrap_atoms, so each cell's wrapped float32 positions equal a single-cell call's.
+__global__ void wrap_batch(int n, const float *xyz, const int *z, const BatchCell *cells, const int *cell_of,
+                           float *wxyz, int *wind, int *status) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n)
+    return;
+  const BatchCell &p = cells[cell_of[i]];
+  int zi = z[i];
+  if (zi < 1 || zi > 118)
+    atomicCAS(status, 0, kStatusBadElement);
+  double f[3];
+  float q[3] = {xyz[3 * i], xyz[3 * i + 1], xyz[3 * i + 2]};
+  if (!isfinite(q[0]) || !isfinite(q[1]) || !isfinite(q[2])) {
+    atomicCAS(status, 0, kStatusNonfinite);
+    q[0] = q[1] = q[2] = 0;
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    double v = __dmul_rn(double(q[0]), p.inv[k]);
+    v = __dadd_rn(v, __dmul_rn(double(q[1]), p.inv[3 + k]));
+    v = __dadd_rn(v, __dmul_rn(double(q[2]), p.inv[6 + k]));
+    double w = floor(v);
+    if (fabs(w) > double(INT_MAX / 4)) {
+      atomicCAS(status, 0, kStatusWinding);
+      w = 0;
+    }
+    wind[3 * i + k] = int(w);
+    f[k] = __dsub_rn(v, w);
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    double x = __dmul_rn(f[0], p.h[k]);
+    x = __dadd_rn(x, __dmul_rn(f[1], p.h[3 + k]));
+    x = __dadd_rn(x, __dmul_rn(f[2], p.h[6 + k]));
+    wxyz[3 * i + k] = __double2float_rn(x);
+  }
+}
+
+// Warp per receiver: all images of its cell x the cell's atoms, with neighbour_pass's float32
+// displacement expression, inclusive cutoff and (i, i, 0) exclusion.  Count pass when
+// out_sender is null, fill pass otherwise; shifts are reported in the caller's frame.
+__global__ void neighbour_batch(int n, float cutoff2, const BatchCell *cells, const int *cell_of, const float *xyz,
+                                const int *winding, int *counts, const int *row, int *out_sender, int *out_shift,
+                                float4 *out_vec, float *out_r2) {
+  int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (i >= n)
+    return;
+  const BatchCell &c = cells[cell_of[i]];
+  float xi = xyz[3 * i], yi = xyz[3 * i + 1], zi = xyz[3 * i + 2];
+  int wi0 = winding[3 * i], wi1 = winding[3 * i + 1], wi2 = winding[3 * i + 2];
+  int count = 0, base_out = out_sender ? row[i] : 0, end = c.first + c.count;
+  for (int x = -c.images[0]; x <= c.images[0]; ++x)
+    for (int y = -c.images[1]; y <= c.images[1]; ++y)
+      for (int z = -c.images[2]; z <= c.images[2]; ++z)
+        for (int base = c.first; base < end; base += 32) {
+          int j = base + lane;
+          bool valid = j < end;
+          float dx = 0, dy = 0, dz = 0, r2 = 0;
+          if (valid) {
+            dx = xyz[3 * j] + x * c.hf[0] + y * c.hf[3] + z * c.hf[6] - xi;
+            dy = xyz[3 * j + 1] + x * c.hf[1] + y * c.hf[4] + z * c.hf[7] - yi;
+            dz = xyz[3 * j + 2] + x * c.hf[2] + y * c.hf[5] + z * c.hf[8] - zi;
+            r2 = dx * dx + dy * dy + dz * dz;
+            valid = r2 <= cutoff2 && !(i == j && x == 0 && y == 0 && z == 0);
+          }
+          unsigned mask = __ballot_sync(0xffffffffu, valid);
+          if (out_sender && valid) {
+            int e = base_out + count + __popc(mask & ((1u << lane) - 1));
+            out_sender[e] = j;
+            out_shift[3 * e] = x + wi0 - winding[3 * j];
+            out_shift[3 * e + 1] = y + wi1 - winding[3 * j + 1];
+            out_shift[3 * e + 2] = z + wi2 - winding[3 * j + 2];
+            out_vec[e] = make_float4(dx, dy, dz, sqrtf(r2));
+            out_r2[e] = r2;
+          }
+          count += __popc(mask);
+        }
+  if (!out_sender && lane == 0)
+    counts[i] = count;
+}
+
+__global__ void iota_kernel(int n, int *a, int *b) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n)
+    a[i] = b[i] = i;
+}
+
+// CTA per cell: fixed-order float64 sums of energy (+ e0) and the 9 virial components, and
+// per-atom energies (+ e0) and forces packed as [n energies | 3n forces].
+__global__ void batch_reduce(const BatchCell *cells, int n, const float *e, const float *f, const float *v,
+                             const float *e0, const int *z, float *out, double *sums) {
+  __shared__ double red[10][256];
+  const BatchCell &c = cells[blockIdx.x];
+  int t = threadIdx.x;
+  double acc[10] = {};
+  for (int i = c.first + t; i < c.first + c.count; i += blockDim.x) {
+    float base = e0 ? e0[z[i]] : 0.f, ev = e[i];
+    out[i] = ev + base;
+    acc[0] += double(ev) + double(base);
+    for (int q = 0; q < 3; ++q)
+      out[n + 3 * i + q] = f[3 * i + q];
+    for (int q = 0; q < 9; ++q)
+      acc[1 + q] += double(v[9 * i + q]);
+  }
+  for (int q = 0; q < 10; ++q)
+    red[q][t] = acc[q];
+  __syncthreads();
+  for (int step = 128; step; step >>= 1) {
+    if (t < step)
+      for (int q = 0; q < 10; ++q)
+        red[q][t] += red[q][t + step];
+    __syncthreads();
+  }
+  if (t < 10)
+    sums[blockIdx.x * 10 + t] = red[t][0];
+}
 } // namespace
 
 int &launch_counter() {
@@ -637,6 +763,255 @@ Result Context::finish(float *e, float *f, float *v, const float *e0_by_z) {
     r.virial[k] = float(hsums[1 + k]);
   }
   return r;
+}
+
+void Context::prepare_batch(const std::vector<Structure> &cells, float cutoff, const Options &opts) {
+  resources.clear();
+  launch_counter() = 0;
+  if (!std::isfinite(cutoff) || cutoff <= 0 || !std::isfinite(cutoff * cutoff))
+    throw Error("Invalid atom count or cutoff");
+  if (device_positions)
+    throw Error("Batched calls take host inputs");
+  int count = int(cells.size());
+  std::vector<BatchCell> host(count);
+  batch_offsets.assign(size_t(count) + 1, 0);
+  long long total_atoms = 0;
+  for (int c = 0; c < count; ++c) {
+    const Structure &s = cells[c];
+    if (s.size < 0 || s.size > INT_MAX / 16)
+      throw Error("Invalid atom count or cutoff");
+    if (!s.pbc[0] || !s.pbc[1] || !s.pbc[2])
+      throw Error("v1 requires three periodic axes");
+    if (s.size && (!s.positions || !s.elements))
+      throw Error("Null structure data");
+    double h[9];
+    for (int k = 0; k < 9; ++k) {
+      h[k] = s.cell[k];
+      if (!std::isfinite(h[k]))
+        throw Error("Nonfinite cell");
+    }
+    // Same validation, adjugate inverse and image counts as prepare().
+    double det = h[0] * (h[4] * h[8] - h[5] * h[7]) - h[1] * (h[3] * h[8] - h[5] * h[6]) +
+                 h[2] * (h[3] * h[7] - h[4] * h[6]);
+    double scale = 0;
+    for (double a : h)
+      scale = std::max(scale, std::abs(a));
+    if (!std::isfinite(det) || scale == 0 || std::abs(det) < 1e-10 * scale * scale * scale)
+      throw Error("Singular or ill-conditioned cell");
+    BatchCell &b = host[c];
+    double *inv = b.inv;
+    inv[0] = (h[4] * h[8] - h[5] * h[7]) / det;
+    inv[1] = (h[2] * h[7] - h[1] * h[8]) / det;
+    inv[2] = (h[1] * h[5] - h[2] * h[4]) / det;
+    inv[3] = (h[5] * h[6] - h[3] * h[8]) / det;
+    inv[4] = (h[0] * h[8] - h[2] * h[6]) / det;
+    inv[5] = (h[2] * h[3] - h[0] * h[5]) / det;
+    inv[6] = (h[3] * h[7] - h[4] * h[6]) / det;
+    inv[7] = (h[1] * h[6] - h[0] * h[7]) / det;
+    inv[8] = (h[0] * h[4] - h[1] * h[3]) / det;
+    bool grid_ok = true;
+    for (int k = 0; k < 9; ++k) {
+      b.h[k] = h[k];
+      b.hf[k] = s.cell[k];
+    }
+    for (int k = 0; k < 3; ++k) {
+      double height = 1 / std::sqrt(inv[k] * inv[k] + inv[3 + k] * inv[3 + k] + inv[6 + k] * inv[6 + k]);
+      grid_ok &= height / cutoff >= 1;
+      double im = std::ceil(cutoff / height);
+      if (im > 1000000)
+        throw Error("Excessive periodic image range");
+      b.images[k] = std::max(1, int(im));
+    }
+    if (double(2 * b.images[0] + 1) * (2 * b.images[1] + 1) * (2 * b.images[2] + 1) > INT_MAX)
+      throw Error("Periodic image tuples exceed v1 int32 capacity");
+    if (opts.backend == NeighborBackend::CellList && !grid_ok)
+      throw Error("CellList requires all reciprocal plane heights >= cutoff");
+    for (int i = 0; i < s.size; ++i) {
+      if (s.elements[i] < 1 || s.elements[i] > 118)
+        throw Error("Invalid atomic number");
+      for (int k = 0; k < 3; ++k)
+        if (!std::isfinite(s.positions[3 * i + k]))
+          throw Error("Nonfinite coordinate");
+    }
+    b.first = int(total_atoms);
+    b.count = s.size;
+    total_atoms += s.size;
+    if (total_atoms > INT_MAX / 16)
+      throw Error("Invalid atom count or cutoff");
+    batch_offsets[c + 1] = int(total_atoms);
+  }
+  int n = int(total_atoms);
+  // Pinned staging: xyz, Z and cell index in one upload; the cell parameters (doubles) go to
+  // their own 8-byte-aligned device array.
+  size_t bytes = size_t(n) * 20 + 256;
+  grow_pinned(pinned_, pinned_capacity_, bytes);
+  check(cudaEventRecord(start, stream));
+  auto *px = static_cast<char *>(pinned_);
+  original_elements.clear();
+  for (int c = 0; c < count; ++c) {
+    const Structure &s = cells[c];
+    int first = host[c].first;
+    if (s.size) {
+      std::memcpy(px + size_t(first) * 12, s.positions, size_t(s.size) * 12);
+      std::memcpy(px + size_t(n) * 12 + size_t(first) * 4, s.elements, size_t(s.size) * 4);
+      original_elements.insert(original_elements.end(), s.elements, s.elements + s.size);
+    }
+    int *cell_of = reinterpret_cast<int *>(px + size_t(n) * 16);
+    for (int i = 0; i < s.size; ++i)
+      cell_of[first + i] = c;
+  }
+  char *dev = static_cast<char *>(reserve("batch.input", size_t(n) * 20 + 16));
+  if (n)
+    check(cudaMemcpyAsync(dev, px, size_t(n) * 20, cudaMemcpyHostToDevice, stream));
+  const float *in_xyz = reinterpret_cast<const float *>(dev);
+  const int *in_z = reinterpret_cast<const int *>(dev + size_t(n) * 12);
+  const int *cell_of = reinterpret_cast<const int *>(dev + size_t(n) * 16);
+  auto *dcells = array<BatchCell>("batch.cells", std::max(count, 1));
+  if (count)
+    check(cudaMemcpyAsync(dcells, host.data(), size_t(count) * sizeof(BatchCell), cudaMemcpyHostToDevice, stream));
+  input_elements_ = in_z;
+  float *wxyz = array<float>("batch.xyz", size_t(n) * 3);
+  int *wind = array<int>("batch.winding", size_t(n) * 3);
+  int *row = array<int>("batch.row", size_t(n) + 1);
+  int *counts = array<int>("batch.counts", std::max(n, 1));
+  int *status = array<int>("geometry.status", 1);
+  long long *total = array<long long>("batch.total", 1);
+  int *i2o = array<int>("batch.i2o", std::max(n, 1)), *o2i = array<int>("batch.o2i", std::max(n, 1));
+  clear(status, sizeof(int));
+  clear(total, sizeof(long long));
+  float cutoff2 = cutoff * cutoff;
+  if (n) {
+    lapis::launch(wrap_batch, (n + 255) / 256, 256, 0, stream, n, in_xyz, in_z, dcells, cell_of, wxyz, wind, status);
+    lapis::launch(iota_kernel, (n + 255) / 256, 256, 0, stream, n, i2o, o2i);
+    lapis::launch(neighbour_batch, (n * 32 + 255) / 256, 256, 0, stream, n, cutoff2, dcells, cell_of, wxyz, wind,
+                  counts, nullptr, nullptr, nullptr, nullptr, nullptr);
+    lapis::launch(scan_exclusive, 1, 1024, 0, stream, counts, row, n, total);
+  } else {
+    clear(row, sizeof(int));
+  }
+  auto *hs = reinterpret_cast<long long *>(static_cast<char *>(pinned_) + bytes - 64);
+  auto *hstatus = reinterpret_cast<int *>(static_cast<char *>(pinned_) + bytes - 32);
+  check(cudaMemcpyAsync(hs, total, sizeof(long long), cudaMemcpyDeviceToHost, stream));
+  check(cudaMemcpyAsync(hstatus, status, 4, cudaMemcpyDeviceToHost, stream));
+  check(cudaStreamSynchronize(stream));
+  if (*hstatus == kStatusBadElement)
+    throw Error("Invalid atomic number");
+  if (*hstatus == kStatusNonfinite)
+    throw Error("Nonfinite coordinate");
+  if (*hstatus == kStatusWinding)
+    throw Error("Coordinate winding exceeds int32 range");
+  long long E = n ? *hs : 0;
+  if (E > INT_MAX)
+    throw Error("Directed edge count exceeds int32 capacity");
+  int *sender = array<int>("edges.sender", size_t(E));
+  int *shift = array<int>("edges.shift", size_t(E) * 3);
+  float4 *vec = array<float4>("edges.vector", size_t(E));
+  float *r2 = array<float>("edges.r2", size_t(E));
+  int *rev = array<int>("edges.reverse", size_t(E));
+  if (n && E) {
+    lapis::launch(neighbour_batch, (n * 32 + 255) / 256, 256, 0, stream, n, cutoff2, dcells, cell_of, wxyz, wind,
+                  nullptr, row, sender, shift, vec, r2);
+    lapis::launch(reverse_edges, n, 128, 0, stream, row, sender, shift, rev, status);
+  }
+  check(cudaGetLastError());
+  internal_to_original = i2o;
+  original_to_internal = o2i;
+  geometry = {};
+  geometry.n = n;
+  geometry.xyz = wxyz;
+  geometry.elements = in_z;
+  geometry.winding = wind;
+  geometry.status = status;
+  geometry.cutoff2 = cutoff2;
+  geometry.backend = NeighborBackend::BruteForce;
+  geometry.edge_offsets = row;
+  geometry.edge_sender = sender;
+  geometry.edge_shift = shift;
+  geometry.edge_vector = vec;
+  geometry.edge_r2 = r2;
+  geometry.edge_reverse = rev;
+  geometry.edge_capacity = E;
+  diagnostics.selected = NeighborBackend::BruteForce;
+  diagnostics.reason = "batch: all-images enumeration per cell";
+  diagnostics.edges = E;
+}
+
+std::vector<Result> Context::finish_batch(float *e, float *f, float *v, const float *e0_by_z) {
+  int n = geometry.n, count = int(batch_offsets.size()) - 1;
+  size_t out_floats = size_t(n) * 4;
+  float *packed = array<float>("output.ordered", std::max<size_t>(out_floats, 1));
+  double *sums = array<double>("output.batch_sums", size_t(std::max(count, 1)) * 10);
+  auto *dcells = array<BatchCell>("batch.cells", std::max(count, 1));
+  if (count)
+    lapis::launch(batch_reduce, count, 256, 0, stream, dcells, n, e, f, v, e0_by_z, input_elements_, packed, sums);
+  size_t bytes = out_floats * 4 + size_t(count) * 80 + 256;
+  grow_pinned(pinned_, pinned_capacity_, bytes);
+  auto *host = static_cast<char *>(pinned_);
+  auto *hstatus = reinterpret_cast<int *>(host);
+  auto *hsums = reinterpret_cast<double *>(host + 64);
+  auto *hout = reinterpret_cast<float *>(host + 64 + size_t(count) * 80);
+  check(cudaMemcpyAsync(hstatus, geometry.status, 4, cudaMemcpyDeviceToHost, stream));
+  if (count)
+    check(cudaMemcpyAsync(hsums, sums, size_t(count) * 80, cudaMemcpyDeviceToHost, stream));
+  if (out_floats)
+    check(cudaMemcpyAsync(hout, packed, out_floats * 4, cudaMemcpyDeviceToHost, stream));
+  check(cudaEventRecord(stop, stream));
+  check(cudaGetLastError());
+  check(cudaStreamSynchronize(stream));
+  if (*hstatus)
+    throw Error("Model detected invalid device state (code " + std::to_string(*hstatus) + ")");
+  check(cudaEventElapsedTime(&diagnostics.device_ms, start, stop));
+  std::vector<Result> results(count);
+  for (int c = 0; c < count; ++c) {
+    int first = batch_offsets[c], size = batch_offsets[c + 1] - first;
+    Result &r = results[c];
+    r.energies.assign(hout + first, hout + first + size);
+    r.forces.assign(hout + n + 3 * size_t(first), hout + n + 3 * size_t(first + size));
+    for (float x : r.energies)
+      if (!std::isfinite(x))
+        throw Error("Nonfinite model output");
+    for (float x : r.forces)
+      if (!std::isfinite(x))
+        throw Error("Nonfinite force");
+    r.energy = hsums[10 * c];
+    for (int k = 0; k < 9; ++k) {
+      if (!std::isfinite(hsums[10 * c + 1 + k]))
+        throw Error("Nonfinite virial");
+      r.virial[k] = float(hsums[10 * c + 1 + k]);
+    }
+  }
+  return results;
+}
+
+std::vector<Result> Calculator::evaluate_batch() { throw Error("This calculator does not support batches"); }
+
+std::vector<Result> Calculator::calculate_batch(const std::vector<Structure> &cells) {
+  if (busy_.test_and_set(std::memory_order_acquire))
+    throw Error("Calculator is single-flight: concurrent call rejected");
+  struct Guard {
+    std::atomic_flag &b;
+    ~Guard() { b.clear(std::memory_order_release); }
+  } guard{busy_};
+  std::vector<Result> out;
+  out.reserve(cells.size());
+  try {
+    // Consecutive sub-batches of at most kBatchAtoms atoms (a larger cell goes alone).
+    for (size_t c0 = 0; c0 < cells.size();) {
+      size_t c1 = c0;
+      long long atoms = 0;
+      while (c1 < cells.size() && (c1 == c0 || atoms + cells[c1].size <= kBatchAtoms))
+        atoms += std::max(cells[c1++].size, 0);
+      std::vector<Structure> part(cells.begin() + c0, cells.begin() + c1);
+      context_.prepare_batch(part, cutoff_, options_);
+      for (auto &r : evaluate_batch())
+        out.push_back(std::move(r));
+      c0 = c1;
+    }
+    return out;
+  } catch (...) {
+    cudaStreamSynchronize(context_.stream);
+    throw;
+  }
 }
 
 Result Calculator::calculate(const Structure &s) {

@@ -7,6 +7,7 @@
 #include <algorithm>
 #include <array>
 #include <cstring>
+#include <climits>
 #include <sstream>
 #include <vector>
 
@@ -172,6 +173,51 @@ int mace_calculate(void *h, int n, const float *xyz, const int *z, const float *
 int mace_calculate_device(void *h, int n, const float *xyz, const int *z, const float *cell, double *energy,
                           float *per_atom, float *force, float *virial) {
   return calculate(h, n, xyz, z, cell, energy, per_atom, force, virial, true);
+}
+
+int mace_calculate_batch(void *handle, int count, const int *sizes, const float *xyz, const int *z,
+                         const float *cells, double *energies, float *per_atom, float *force, float *virial) {
+  try {
+    error.clear();
+    if (!handle || count < 0 || (count && (!sizes || !cells || !energies || !virial)))
+      throw Error("Null calculator or result pointer");
+    long long total = 0;
+    for (int c = 0; c < count; ++c) {
+      if (sizes[c] < 0)
+        throw Error("Invalid atom count or cutoff");
+      total += sizes[c];
+    }
+    if (total > INT_MAX / 16)
+      throw Error("Invalid atom count or cutoff");
+    if (total && (!xyz || !z || !per_atom || !force))
+      throw Error("Null structure data");
+    auto *h = static_cast<Handle *>(handle);
+    DeviceScope scope(h->device);
+    std::vector<Structure> part(static_cast<size_t>(count));
+    long long first = 0;
+    for (int c = 0; c < count; ++c) {
+      Structure &s = part[c];
+      s.size = sizes[c];
+      s.positions = sizes[c] ? xyz + 3 * first : nullptr;
+      s.elements = sizes[c] ? z + first : nullptr;
+      std::copy(cells + 9 * size_t(c), cells + 9 * size_t(c) + 9, s.cell.begin());
+      first += sizes[c];
+    }
+    auto results = h->model->calculate_batch(part);
+    first = 0;
+    for (int c = 0; c < count; ++c) {
+      const auto &r = results[c];
+      energies[c] = r.energy;
+      std::copy(r.energies.begin(), r.energies.end(), per_atom + first);
+      std::copy(r.forces.begin(), r.forces.end(), force + 3 * first);
+      std::copy(r.virial.begin(), r.virial.end(), virial + 9 * size_t(c));
+      first += sizes[c];
+    }
+    return 0;
+  } catch (const std::exception &e) {
+    error = e.what();
+    return -1;
+  }
 }
 
 long long mace_last_edges(void *handle, int *out, long long capacity) {

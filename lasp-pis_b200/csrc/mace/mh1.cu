@@ -112,7 +112,10 @@ struct StageTimer {
 };
 } // namespace
 
-Result MH1::evaluate() {
+Result MH1::evaluate() { return compute(false)[0]; }
+std::vector<Result> MH1::evaluate_batch() { return compute(true); }
+
+std::vector<Result> MH1::compute(bool batch) {
   auto &c = context_;
   auto &m = model_->data;
   cudaStream_t s = c.stream;
@@ -260,9 +263,13 @@ Result MH1::evaluate() {
   check(cudaGetLastError());
   timer.mark("forces");
   timer.mark("finish-enqueue");
-  auto result = c.finish(energy, force, virial, m.e0_z);
+  std::vector<Result> results;
+  if (batch)
+    results = c.finish_batch(energy, force, virial, m.e0_z);
+  else
+    results.push_back(c.finish(energy, force, virial, m.e0_z));
   c.diagnostics.launches = launch_counter();
   timer.report(c.diagnostics);
-  return result;
+  return results;
 }
 } // namespace mace

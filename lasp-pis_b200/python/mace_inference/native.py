@@ -29,6 +29,8 @@ def load(path=None) -> ct.CDLL:
     lib.mace_calculate.restype = ct.c_int
     lib.mace_calculate_device.argtypes = [ct.c_void_p, ct.c_int] + [ct.c_void_p] * 7
     lib.mace_calculate_device.restype = ct.c_int
+    lib.mace_calculate_batch.argtypes = [ct.c_void_p, ct.c_int] + [ct.c_void_p] * 8
+    lib.mace_calculate_batch.restype = ct.c_int
     lib.mace_diagnostics.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_size_t]
     lib.mace_diagnostics.restype = ct.c_int
     lib.mace_profile.argtypes = [ct.c_void_p, ct.c_int]
@@ -91,6 +93,33 @@ class NativeMH1:
         xyz = np.ascontiguousarray(xyz, np.float32).reshape(-1, 3)
         z = np.ascontiguousarray(z, np.int32)
         return self._call(self.lib.mace_calculate, len(z), xyz.ctypes.data, z.ctypes.data, cell)
+
+    def calculate_batch(self, cells):
+        """Independent periodic cells in one call: ``cells`` is a sequence of (xyz, Z, cell).
+        Returns one result dict per cell (as calculate)."""
+        sizes = np.array([len(z) for _, z, _ in cells], np.int32)
+        total = int(sizes.sum())
+        xyz = np.ascontiguousarray(np.concatenate([np.asarray(x, np.float32).reshape(-1, 3) for x, _, _ in cells])
+                                   if total else np.zeros((0, 3), np.float32), np.float32)
+        z = np.ascontiguousarray(np.concatenate([np.asarray(q, np.int32) for _, q, _ in cells])
+                                 if total else np.zeros(0, np.int32), np.int32)
+        h = np.ascontiguousarray(np.stack([np.asarray(c, np.float32).reshape(3, 3) for _, _, c in cells])
+                                 if len(cells) else np.zeros((0, 3, 3), np.float32), np.float32)
+        count = len(cells)
+        energies = np.zeros(max(count, 1), np.float64)
+        per_atom = np.zeros(max(total, 1), np.float32)
+        forces = np.zeros((max(total, 1), 3), np.float32)
+        virials = np.zeros((max(count, 1), 3, 3), np.float32)
+        if self.lib.mace_calculate_batch(self.handle, count, sizes.ctypes.data, xyz.ctypes.data, z.ctypes.data,
+                                         h.ctypes.data, energies.ctypes.data, per_atom.ctypes.data,
+                                         forces.ctypes.data, virials.ctypes.data):
+            raise RuntimeError(_error(self.lib))
+        out, first = [], 0
+        for c, n in enumerate(sizes):
+            out.append({"energy": float(energies[c]), "energies": per_atom[first:first + n].copy(),
+                        "forces": forces[first:first + n].copy(), "virial": virials[c].copy()})
+            first += int(n)
+        return out
 
     def calculate_device(self, n, xyz_ptr, z_ptr, cell):
         """Device-resident inputs (raw device pointers on the handle's GPU)."""
