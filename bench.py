@@ -182,6 +182,115 @@ def reference_arm(args, archive, structure):
     print(json.dumps(line))
 
 
+C4_METRIC = "atoms*evals/s (E+F+virial), MH1-shape, C4 batch of 4,096 independent cells"
+
+
+def c4_reference(args, archive):
+    """The reference has no batched call: its callers loop over mace_calculate.  Time that
+    loop (reference CUDA build, C ABI, host buffers) over the first 512 C4 cells."""
+    import ctypes as ct
+    from lasp_b200 import structures
+    lib_path = ROOT / "oracle" / "_ref" / "libmace_ref.so"
+    if not lib_path.exists():
+        print(json.dumps({"impl": "reference", "unavailable": "reference CUDA build absent (oracle/_ref)"}))
+        return
+    cells = structures.load_c4(DATA)[:512]
+    lib = ct.CDLL(str(lib_path))
+    lib.mace_create_mh1.argtypes = [ct.c_char_p, ct.c_int]
+    lib.mace_create_mh1.restype = ct.c_void_p
+    lib.mace_last_error.restype = ct.c_char_p
+    lib.mace_calculate.argtypes = [ct.c_void_p, ct.c_int] + [ct.c_void_p] * 7
+    lib.mace_destroy.argtypes = [ct.c_void_p]
+    h = lib.mace_create_mh1(str(archive).encode(), 0)
+    e = np.zeros(1)
+    v = np.zeros((3, 3), np.float32)
+
+    def run():
+        for c in cells:
+            a = np.zeros(c.size, np.float32)
+            f = np.zeros((c.size, 3), np.float32)
+            assert lib.mace_calculate(h, c.size, c.positions.ctypes.data, c.numbers.ctypes.data,
+                                      c.cell.ctypes.data, e.ctypes.data, a.ctypes.data, f.ctypes.data,
+                                      v.ctypes.data) == 0, lib.mace_last_error()
+    for _ in range(args.warmup):
+        run()
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    total = time.perf_counter() - t
+    lib.mace_destroy(h)
+    atoms = sum(c.size for c in cells)
+    value = atoms * args.steps / total
+    print(json.dumps({"impl": "reference", "metric": C4_METRIC, "value": value, "unit": UNIT, "n_gpus": 1,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+                      "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                      "data": "synthetic",
+                      "config": {"workload": "C4: first 512 of the 4,096 cells (32-256 atoms each), sequential "
+                                             "mace_calculate calls -- the reference has no batched call",
+                                 "atoms": atoms},
+                      "cpu_baseline": {"value": value, "unit": UNIT, "cores": 1, "kind": "reference",
+                                       "sample": "512 C4 cells per step"},
+                      "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+
+
+def c4_ours(args, archive, rank, local, world):
+    """C4 through mace_calculate_batch: the 4,096 cells split across the ranks by LPT on
+    estimated work (strong scaling: the job is fixed), timed end to end on each rank (host
+    buffers, every H2D/D2H inside) and reported as the max over ranks."""
+    import torch
+    from lasp_b200 import structures
+    from mace_inference import NativeMH1
+    from mace_inference.batch import estimated_work, lpt_partition
+    cells = structures.load_c4(DATA)
+    items = [(c.positions, c.numbers, c.cell) for c in cells]
+    shards = lpt_partition([estimated_work(len(z), h) for _, z, h in items], world)
+    mine = [items[i] for i in shards[rank]]
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    model = NativeMH1(archive, backend=0, library=ROOT / "lasp-pis_b200" / "lib" / "libmace.so", device=local)
+    for _ in range(args.warmup):
+        model.calculate_batch(mine)
+    if world > 1:
+        torch.distributed.barrier()
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        model.calculate_batch(mine)
+    elapsed = time.perf_counter() - t
+    # Per-cell calls of the same engine on a sample, for the batching gain.
+    sample = items[:256]
+    t1 = time.perf_counter()
+    for x, z, h in sample:
+        model.calculate(x, z, h)
+    per_call = sum(len(z) for _, z, _ in sample) / (time.perf_counter() - t1)
+    launches = int(model.diagnostics["launches"])
+    if world > 1:
+        tt = torch.tensor([elapsed], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        elapsed = float(tt[0])
+    if rank == 0:
+        atoms = sum(len(z) for _, z, _ in items)
+        value = atoms * args.steps / elapsed
+        print(json.dumps({"metric": C4_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                          "warmup": args.warmup, "ms_per_step": 1e3 * elapsed / args.steps,
+                          "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                          "data": "synthetic",
+                          "config": {"workload": "C4: 4,096 cells, 32-256 atoms, Z 1-20, seed 104", "atoms": atoms,
+                                     "parallelism": f"LPT over {world} GPU(s), no data-path collective"},
+                          "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": atoms * 16 + 36 * len(items),
+                                  "d2h_bytes_per_step": atoms * 16 + 44 * len(items)},
+                          "per_cell_calls_atoms_per_s": per_call,
+                          "note": "value is end to end (mace_calculate_batch with host buffers); the batch API "
+                                  "takes host inputs only",
+                          "gpu_launches_last_sub_batch": launches}))
+    model.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -198,6 +307,13 @@ def main():
     from lasp_b200 import structures, synth
     archive = DATA / "mh1_synth.pwm"
     synth.write_archive(archive)
+    if args.config == "C4":
+        if args.impl == "reference":
+            if rank == 0:
+                c4_reference(args, archive)
+            return
+        c4_ours(args, archive, rank, local, world)
+        return
     structure = structures.load(args.config, DATA)
     if args.impl == "reference":
         if rank == 0:

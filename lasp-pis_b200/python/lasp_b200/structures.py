@@ -218,6 +218,33 @@ def load(name: str, cache_dir: str | Path) -> Structure:
     return s
 
 
+def _c4_arrays(index):
+    s = c4_cell(index)
+    return s.positions, s.numbers, s.cell
+
+
+def load_c4(cache_dir: str | Path, count: int = 4096, workers: int | None = None) -> list[Structure]:
+    """The C4 batch (cells 0..count-1 of c4_cell), generated in a spawn-context process pool
+    (CPU only) and cached as C4_<count>.npz."""
+    cache = Path(cache_dir) / f"C4_{count}.npz"
+    if cache.exists():
+        d = np.load(cache)
+        off = d["offsets"]
+        return [Structure(d["positions"][off[k]:off[k + 1]], d["numbers"][off[k]:off[k + 1]], d["cells"][k])
+                for k in range(count)]
+    import multiprocessing as mp
+    import os
+    with mp.get_context("spawn").Pool(workers or os.cpu_count() or 1) as pool:
+        parts = pool.map(_c4_arrays, range(count), chunksize=16)
+    cells = [Structure(p, z, c) for p, z, c in parts]
+    offsets = np.concatenate([[0], np.cumsum([c.size for c in cells])])
+    cache.parent.mkdir(parents=True, exist_ok=True)
+    np.savez(cache, positions=np.concatenate([c.positions for c in cells]),
+             numbers=np.concatenate([c.numbers for c in cells]), cells=np.stack([c.cell for c in cells]),
+             offsets=offsets)
+    return cells
+
+
 def density_sample(n_atoms: int, seed: int = 203) -> Structure:
     """A smaller cube cut from the C3 process (same density, lattice, jitter, species)."""
     rng = np.random.default_rng(seed)
