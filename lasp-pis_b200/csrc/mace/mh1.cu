@@ -96,6 +96,7 @@ struct StageTimer {
     check(cudaEventRecord(pool[names.size()], stream));
     names.push_back(name);
   }
+  // Intervals between consecutive marks, summed per name (chunked stages mark once per chunk).
   void report(Diagnostics &d) {
     d.stages.clear();
     if (!enabled || names.size() < 2)
@@ -104,10 +105,15 @@ struct StageTimer {
     for (size_t k = 1; k < names.size(); ++k) {
       float ms = 0;
       check(cudaEventElapsedTime(&ms, pool[k - 1], pool[k]));
-      d.stages.emplace_back(names[k], ms);
-      if (print)
-        std::fprintf(stderr, "MH1 %s: %.4f ms\n", names[k].c_str(), ms);
+      auto it = std::find_if(d.stages.begin(), d.stages.end(), [&](const auto &x) { return x.first == names[k]; });
+      if (it == d.stages.end())
+        d.stages.emplace_back(names[k], ms);
+      else
+        it->second += ms;
     }
+    if (print)
+      for (auto &x : d.stages)
+        std::fprintf(stderr, "MH1 %s: %.4f ms\n", x.first.c_str(), x.second);
   }
 };
 } // namespace
@@ -178,9 +184,9 @@ std::vector<Result> MH1::compute(bool batch) {
       for (auto &q : chunks) {
         tc_gemm(s, int(q.e1 - q.e0), width, 64, 1, ro[k].h + q.e0 * 64, 0, l.radial.out_hi, l.radial.out_lo,
                 proj[k], width, 0, false, status);
-        if (chunks.size() == 1)
-          timer.mark("forward" + std::to_string(k) + ".projection");
+        timer.mark("forward" + std::to_string(k) + ".projection");
         launch_message_forward_proj(s, k, c.geometry, l, ea, ro[k], q, proj[k], up[k], msg, rho[k]);
+        timer.mark("forward" + std::to_string(k) + ".messages");
       }
     } else if (tensor_core_edges())
       launch_message_forward_tc(s, k, c.geometry, l, ea, ro[k], up[k], msg, rho[k]);
@@ -243,10 +249,10 @@ std::vector<Result> MH1::compute(bool batch) {
         else
           tc_gemm(s, rows, width, 64, 2, ro[k].h + q.e0 * 64, (long long)E * 64, l.radial.out_hi,
                   l.radial.out_lo, R, width, (long long)chunk_cap * width, false, status);
-        if (chunks.size() == 1)
-          timer.mark("backward" + std::to_string(k) + ".projection");
+        timer.mark("backward" + std::to_string(k) + ".projection");
         launch_message_backward_proj(s, k, c.geometry, l, ea, ro[k], q, R, dR, up[k], msggrad, rhograd, upgrad,
                                      edge_force, k == 0);
+        timer.mark("backward" + std::to_string(k) + ".edges");
       }
     } else if (tensor_core_edges())
       launch_message_backward_tc(s, k, c.geometry, l, ea, ro[k], up[k], msggrad, rhograd, upgrad, edge_force, k == 0);
