@@ -129,15 +129,17 @@ __global__ void normalize_gate_kernel(int n, const float *raw, const float *res,
   }
 }
 
-// CTA per node: gate VJP into pre_grad, normalisation VJP into raw_grad and density_grad.
-__global__ void __launch_bounds__(128) gate_norm_backward_kernel(int n, const float *pre, const float *raw,
+// CTA per node, thread per channel: gate VJP into pre_grad, normalisation VJP into raw_grad
+// and density_grad (one fixed-order block reduction per node).
+__global__ void __launch_bounds__(512) gate_norm_backward_kernel(int n, const float *pre, const float *raw,
                                                                  const float *rho, const float *gg, float alpha,
                                                                  float beta, float cs, float cgt, float *pg,
                                                                  float *rg, float *rho_grad) {
-  __shared__ float red[4];
+  __shared__ float red[16];
   int i = blockIdx.x, t = threadIdx.x;
   float den = alpha + beta * rho[i], s = 0.f;
-  for (int c = t; c < 512; c += 128) {
+  {
+    int c = t;
     size_t k0 = size_t(i) * 2048 + c;
     float u = pre[k0], sg = sigm(u);
     float g0 = gg[size_t(i) * 512 + c] * cs * sg * (1.f + u * (1.f - sg));
@@ -168,8 +170,12 @@ __global__ void __launch_bounds__(128) gate_norm_backward_kernel(int n, const fl
   if ((t & 31) == 0)
     red[t >> 5] = s;
   __syncthreads();
-  if (t == 0)
-    rho_grad[i] = red[0] + red[1] + red[2] + red[3];
+  if (t == 0) {
+    float total = 0.f;
+    for (int w = 0; w < 16; ++w)
+      total += red[w];
+    rho_grad[i] = total;
+  }
 }
 
 // Symmetric contraction: y[out][c] = sum_t coef[t][c] x[a][c] x[b][c] x[c'][c] (degree <= 3).
@@ -475,7 +481,7 @@ void launch_gate_norm_backward(cudaStream_t s, int n, const float *pre, const fl
                                const float *gate_grad, float alpha, float beta, float scalar_scale, float gate_scale,
                                float *pre_grad, float *raw_grad, float *density_grad) {
   if (n)
-    lapis::launch(gate_norm_backward_kernel, n, 128, 0, s, n, pre, raw, density, gate_grad, alpha, beta, scalar_scale,
+    lapis::launch(gate_norm_backward_kernel, n, 512, 0, s, n, pre, raw, density, gate_grad, alpha, beta, scalar_scale,
                                                 gate_scale, pre_grad, raw_grad, density_grad);
 }
 size_t product_smem(int count, bool backward) {
