@@ -1,0 +1,51 @@
+// Spatial domain decomposition of one periodic structure across ranks (one process per GPU),
+// B200 build addition for large structures (no counterpart in the reference, whose
+// calculators evaluate a structure on one GPU).
+//
+// Every rank passes the same full structure.  After Context::prepare (the full CSR edge list),
+// localize() switches the context to this rank's part: the receivers it owns -- a contiguous
+// range of the bin-sorted internal order, i.e. a compact slab -- and, as senders, those plus
+// the ghost atoms their edges reach, numbered after them.  The evaluation then exchanges only
+// what crosses ranks, point to point over NCCL on the context's stream: layer features of
+// ghost senders (owners -> ghosts), their gradients and the ghost sender forces
+// (ghosts -> owners), and finally the per-atom outputs (an all-reduce of the owned rows),
+// so every rank returns the full result.  NCCL is loaded at run time (libnccl.so.2, the copy
+// already in the process when there is one).
+#pragma once
+#include "runtime.hpp"
+#include <memory>
+#include <string>
+
+namespace lapis {
+// A new NCCL unique id (128 bytes) for Domain's communicator; made by one rank, passed to all.
+std::string nccl_unique_id();
+
+class Domain {
+public:
+  Domain(int rank, int world, const void *unique_id);
+  ~Domain();
+  Domain(const Domain &) = delete;
+  Domain &operator=(const Domain &) = delete;
+  int rank() const;
+  int world() const;
+  // Owned receivers n_own = rows [0, n_own); senders n_local = owned then ghosts.
+  int n_own() const;
+  int n_local() const;
+  // After ctx.prepare on the full structure: ctx.geometry becomes the local graph.
+  void localize(Context &ctx);
+  // Back to the full geometry (for Context::finish).
+  void restore(Context &ctx);
+  // Rows [n_own, n_local) of x ([comps][stride][width] floats) from their owners.
+  void fetch_ghost_rows(Context &ctx, float *x, int comps, int stride, int width);
+  // Adds rows [n_own, n_local) of x into the owners' rows (ghosts -> owners).
+  void return_ghost_rows(Context &ctx, float *x, int comps, int stride, int width);
+  // Owned rows of e [n_own], f [n_own][3], v [n_own][9] into full-structure arrays (internal
+  // order), summed over ranks so every rank holds all atoms.  ef, ff, vf must be one contiguous
+  // buffer: ff = ef + n, vf = ef + 4 n (n = full atom count).
+  void gather_outputs(Context &ctx, const float *e, const float *f, const float *v, float *ef, float *ff, float *vf);
+
+private:
+  struct Impl;
+  std::unique_ptr<Impl> impl_;
+};
+} // namespace lapis

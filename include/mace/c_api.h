@@ -34,6 +34,17 @@ MACE_EXPORT int mace_diagnostics(void *handle, char *buffer, size_t capacity);
 /* Like mace_create_mh1 but binds the handle to CUDA device `device` (the reference binds
  * to whatever device is current at creation). */
 MACE_EXPORT void *mace_create_mh1_device(const char *archive, int backend, int device);
+/* Spatial domain decomposition of one structure across `world` ranks (one process per GPU;
+ * B200 build addition, no counterpart in the reference).  Every rank creates its handle with
+ * the same 128-byte NCCL id (from mace_nccl_unique_id on one rank) and then calls
+ * mace_calculate with the SAME full structure; each rank evaluates the receivers it owns,
+ * exchanges layer features, gradients and ghost forces over NCCL, and receives the full
+ * result.  Calls on the ranks' handles are collective: every rank must make the same calls
+ * in the same order. */
+MACE_EXPORT void *mace_create_mh1_domain(const char *archive, int backend, int device, int rank, int world,
+                                         const void *nccl_id);
+/* Writes a new 128-byte NCCL unique id for mace_create_mh1_domain; returns 0, or -1. */
+MACE_EXPORT int mace_nccl_unique_id(void *out128);
 /* mace_calculate with DEVICE-resident xyz/elements (device pointers on the handle's GPU);
  * results still land in the caller's host arrays.  Lets a caller that keeps structures in
  * HBM skip the host-to-device copy. */

@@ -1,5 +1,6 @@
 // mace::MH1 -- the C++ model API (same surface as mace/include/mace/mh1.hpp:6-19).
 #pragma once
+#include <lapis/domain.hpp>
 #include <lapis/runtime.hpp>
 #include <mace/export.h>
 #include <memory>
@@ -21,5 +22,8 @@ public:
   // MACE_PROFILE_MH1 environment variable, which additionally prints them to stderr).
   void set_profiling(bool enabled);
   lapis::Result calculate_file(const std::string &path, size_t frame = 0);
+  // Evaluate structures decomposed across ranks (B200 build addition): every rank passes the
+  // same full structure and gets the full result; null returns to single-GPU evaluation.
+  void set_domain(std::shared_ptr<lapis::Domain> domain);
 };
 } // namespace mace

@@ -151,6 +151,42 @@ void *mace_create_mh1_device(const char *path, int b, int device) {
   }
 }
 
+void *mace_create_mh1_domain(const char *path, int b, int device, int rank, int world, const void *nccl_id) {
+  try {
+    error.clear();
+    if (device < 0)
+      throw Error("Invalid device");
+    if (!nccl_id)
+      throw Error("Null NCCL id");
+    auto *h = static_cast<Handle *>(create(path, b, nullptr, device));
+    try {
+      DeviceScope scope(h->device);
+      h->model->set_domain(std::make_shared<lapis::Domain>(rank, world, nccl_id));
+    } catch (...) {
+      mace_destroy(h);
+      throw;
+    }
+    return h;
+  } catch (const std::exception &e) {
+    error = e.what();
+    return nullptr;
+  }
+}
+
+int mace_nccl_unique_id(void *out) {
+  try {
+    error.clear();
+    if (!out)
+      throw Error("Null output");
+    auto id = lapis::nccl_unique_id();
+    std::copy(id.begin(), id.end(), static_cast<char *>(out));
+    return 0;
+  } catch (const std::exception &e) {
+    error = e.what();
+    return -1;
+  }
+}
+
 void mace_destroy(void *handle) {
   auto *h = static_cast<Handle *>(handle);
   if (!h)

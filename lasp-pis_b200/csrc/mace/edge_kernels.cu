@@ -575,7 +575,60 @@ __global__ void force_gather_kernel(DeviceGeometry g, const float4 *ef, float *f
       virial[9 * i + k] += acc[3 + k];
   }
 }
+// Domain form of force_gather_kernel: reverse edges outside the local graph (index < 0) are
+// skipped -- their forces arrive from the ranks that own those receivers.
+__global__ void force_gather_domain_kernel(DeviceGeometry g, const float4 *ef, float *force, float *virial) {
+  int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (i >= g.n)
+    return;
+  float acc[12] = {};
+  for (int e = g.edge_offsets[i] + lane; e < g.edge_offsets[i + 1]; e += 32) {
+    float4 f = ef[e], d = g.edge_vector[e];
+    int r = g.edge_reverse[e];
+    float4 fr = r >= 0 ? ef[r] : make_float4(0.f, 0.f, 0.f, 0.f);
+    acc[0] += f.x - fr.x;
+    acc[1] += f.y - fr.y;
+    acc[2] += f.z - fr.z;
+    float dv[3] = {d.x, d.y, d.z}, fv[3] = {f.x, f.y, f.z};
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+#pragma unroll
+      for (int b = 0; b < 3; ++b)
+        acc[3 + 3 * a + b] -= dv[a] * fv[b];
+  }
+#pragma unroll
+  for (int q = 0; q < 12; ++q)
+    acc[q] = warp_allsum(acc[q]);
+  if (lane == 0) {
+    for (int k = 0; k < 3; ++k)
+      force[3 * i + k] += acc[k];
+    for (int k = 0; k < 9; ++k)
+      virial[9 * i + k] += acc[3 + k];
+  }
+}
+// The reaction of every local edge on a ghost sender, accumulated in the ghost's force row.
+__global__ void ghost_reaction_kernel(long long E, int n_own, const int *sender, const float4 *ef, float *force) {
+  long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (e >= E)
+    return;
+  int j = sender[e];
+  if (j >= n_own) {
+    float4 f = ef[e];
+    atomicAdd(force + 3 * j, -f.x);
+    atomicAdd(force + 3 * j + 1, -f.y);
+    atomicAdd(force + 3 * j + 2, -f.z);
+  }
+}
 } // namespace
+
+void launch_force_gather_domain(cudaStream_t s, const DeviceGeometry &g, const float4 *edge_force, float *force,
+                                float *virial) {
+  if (g.n && g.edge_capacity)
+    lapis::launch(force_gather_domain_kernel, (g.n * 32 + 255) / 256, 256, 0, s, g, edge_force, force, virial);
+  if (g.edge_capacity)
+    lapis::launch(ghost_reaction_kernel, int((g.edge_capacity + 255) / 256), 256, 0, s, g.edge_capacity, g.n,
+                  g.edge_sender, edge_force, force);
+}
 
 void launch_zbl(cudaStream_t s, const DeviceGeometry &g, const float *constants, const float *radii,
                 const float *coeff, float shift, float *energy, float *force, float *virial) {

@@ -54,6 +54,7 @@ template <int L, bool Bwd> struct Stage {
 
 struct ProjArgs {
   int n, r0, e_base;
+  int n_up; // row stride of up / up_grad (the sender count)
   const int *row, *sender;
   const float4 *vec;
   const float *R, *dR, *Y, *dY;
@@ -136,7 +137,7 @@ __global__ void __launch_bounds__(kThreads) edge_proj_kernel(ProjArgs a, TPValue
       if (lane < cnt) {
 #pragma unroll
         for (int q = 0; q < IN; ++q)
-          bulk_load(sb + S::U + (lane * IN + q) * 512, a.up + (size_t(q) * a.n + j) * 128, 512, full);
+          bulk_load(sb + S::U + (lane * IN + q) * 512, a.up + (size_t(q) * a.n_up + j) * 128, 512, full);
       }
       if (lane != 0)
         mbar_arrive(full);
@@ -230,7 +231,7 @@ __global__ void __launch_bounds__(kThreads) edge_proj_kernel(ProjArgs a, TPValue
           int j = meta[k].sender;
 #pragma unroll
           for (int q = 0; q < IN; ++q)
-            atomicAdd(a.up_grad + (size_t(q) * a.n + j) * 128 + c, ug[q]);
+            atomicAdd(a.up_grad + (size_t(q) * a.n_up + j) * 128 + c, ug[q]);
         }
         float dr = 0.f;
 #pragma unroll
@@ -313,9 +314,10 @@ void launch_proj(cudaStream_t s, int blocks, const ProjArgs &a, const TPValues &
 }
 
 ProjArgs proj_args(const DeviceGeometry &g, const Layer &l, EdgeArrays ea, RadialOut ro, const ProjectionChunk &k,
-                   const float *R, const float *up) {
+                   const float *R, const float *up, int n_up) {
   ProjArgs a{};
   a.n = g.n;
+  a.n_up = n_up ? n_up : g.n;
   a.r0 = k.r0;
   a.e_base = int(k.e0);
   a.row = g.edge_offsets;
@@ -335,11 +337,11 @@ ProjArgs proj_args(const DeviceGeometry &g, const Layer &l, EdgeArrays ea, Radia
 
 void launch_message_forward_proj(cudaStream_t s, int layer, const DeviceGeometry &g, const Layer &l, EdgeArrays ea,
                                  RadialOut ro, const ProjectionChunk &k, const float *R, const float *up,
-                                 float *message, float *density) {
+                                 float *message, float *density, int n_up) {
   int blocks = k.r1 - k.r0;
   if (blocks <= 0)
     return;
-  ProjArgs a = proj_args(g, l, ea, ro, k, R, up);
+  ProjArgs a = proj_args(g, l, ea, ro, k, R, up, n_up);
   a.msg = message;
   a.rho = density;
   if (layer == 0)
@@ -351,11 +353,12 @@ void launch_message_forward_proj(cudaStream_t s, int layer, const DeviceGeometry
 void launch_message_backward_proj(cudaStream_t s, int layer, const DeviceGeometry &g, const Layer &l,
                                   EdgeArrays ea, RadialOut ro, const ProjectionChunk &k, const float *R,
                                   const float *dR, const float *up, const float *message_grad,
-                                  const float *density_grad, float *up_grad, float4 *edge_force, bool accumulate) {
+                                  const float *density_grad, float *up_grad, float4 *edge_force, bool accumulate,
+                                  int n_up) {
   int blocks = k.r1 - k.r0;
   if (blocks <= 0)
     return;
-  ProjArgs a = proj_args(g, l, ea, ro, k, R, up);
+  ProjArgs a = proj_args(g, l, ea, ro, k, R, up, n_up);
   a.dR = dR;
   a.msg_grad = message_grad;
   a.rho_grad = density_grad;

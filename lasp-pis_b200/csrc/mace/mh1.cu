@@ -20,6 +20,7 @@ using namespace lapis;
 struct MH1::Model {
   ModelData data;
   bool profiling = false;
+  std::shared_ptr<lapis::Domain> domain;
   std::vector<cudaEvent_t> events;
   ~Model() {
     for (auto e : events)
@@ -38,6 +39,7 @@ MH1::MH1(const std::string &archive, Options o) : MH1(archive, o, {}) {}
 MH1::~MH1() = default;
 size_t MH1::parameter_bytes() const { return model_->data.bytes; }
 void MH1::set_profiling(bool enabled) { model_->profiling = enabled; }
+void MH1::set_domain(std::shared_ptr<lapis::Domain> domain) { model_->domain = std::move(domain); }
 
 long long projection_chunk_edges() {
   static const long long edges = [] {
@@ -125,24 +127,47 @@ std::vector<Result> MH1::compute(bool batch) {
   auto &c = context_;
   auto &m = model_->data;
   cudaStream_t s = c.stream;
-  int n = c.geometry.n;
-  size_t E = size_t(c.geometry.edge_capacity);
-  if (n > INT_MAX / 9728)
+  // Domain decomposition: the context switches to this rank's graph -- owned receivers
+  // (rows [0, n)) and, for the sender-indexed arrays, ghost rows [n, ns) after them.
+  lapis::Domain *dom = model_->domain.get();
+  if (dom && batch)
+    throw Error("Batched calls do not combine with domain decomposition");
+  int n_full = c.geometry.n;
+  if (n_full > INT_MAX / 9728)
     throw Error("MH1 node dimensions exceed v1 int32 capacity");
+  if (dom)
+    dom->localize(c);
+  struct Restore {
+    lapis::Domain *d;
+    Context &c;
+    ~Restore() {
+      if (d)
+        d->restore(c);
+    }
+  } restore_geometry{dom, c};
+  int n = c.geometry.n, ns = dom ? dom->n_local() : n;
+  size_t E = size_t(c.geometry.edge_capacity);
   StageTimer timer(s, model_->profiling, model_->events);
   auto node = [&](const std::string &name, size_t width) { return c.array<float>(name, size_t(n) * width); };
+  auto sender_node = [&](const std::string &name, size_t width) { return c.array<float>(name, size_t(ns) * width); };
   const float *cst = m.constants;
   int *status = c.geometry.status;
-  int *species = c.array<int>("mh.species", n);
-  float *energy = node("mh.e", 1), *force = node("mh.f", 3), *virial = node("mh.v", 9);
-  float *x0 = node("mh.embedding", 512);
-  launch_species(s, c.geometry, m.lookup, species);
-  launch_embed(s, n, species, m.embedding, x0);
+  int *species = c.array<int>("mh.species", ns);
+  float *energy = node("mh.e", 1), *force = sender_node("mh.f", 3), *virial = node("mh.v", 9);
+  float *x0 = sender_node("mh.embedding", 512);
+  DeviceGeometry senders = c.geometry;
+  senders.n = ns;
+  launch_species(s, senders, m.lookup, species);
+  launch_embed(s, ns, species, m.embedding, x0);
+  if (ns > n)
+    c.clear(force + size_t(3) * n, size_t(ns - n) * 3 * sizeof(float));
   launch_zbl(s, c.geometry, m.constants_dev, m.zbl_radii, m.zbl_c, cst[7], energy, force, virial);
   // Projection path: radial projections on the tensor cores into chunk buffers, tensor
   // products from those (default); otherwise the fused SIMT or tcgen05 edge kernels.
   bool projection = !tensor_core_edges() && tensor_core_linears() && m.layers[0].radial.out_hi &&
                     m.layers[1].radial.out_hi;
+  if (dom && !projection)
+    throw Error("Domain decomposition requires the tensor-core projection path");
   std::vector<ProjectionChunk> chunks;
   long long chunk_cap = 0;
   if (projection) {
@@ -165,7 +190,7 @@ std::vector<Result> MH1::compute(bool batch) {
   for (int k = 0; k < 2; ++k) {
     const Layer &l = m.layers[k];
     std::string p = "mh.l" + std::to_string(k);
-    up[k] = node(p + ".up", l.in_comp * 128);
+    up[k] = sender_node(p + ".up", l.in_comp * 128);
     rho[k] = node(p + ".rho", 1);
     raw[k] = node(p + ".raw", 9728);
     pre[k] = node(p + ".pre", 9728);
@@ -175,9 +200,17 @@ std::vector<Result> MH1::compute(bool batch) {
     ro[k] = RadialOut{hd, hd + E * 64, c.array<float2>(p + ".den", E)};
     int width = l.paths * 128;
     proj[k] = projection ? c.array<float>(p + ".proj", size_t(2 * chunk_cap) * width) : nullptr;
-    linear(s, n, l.up, input, up[k], false, false, status);
-    linear(s, n, l.res, up[k], res, false, false, status);
-    linear(s, n, l.skip, input, skip, false, false, status);
+    // Layer 0's sender features depend on the element only, so ghosts compute their own;
+    // layer 1's come from the ghosts' owners.
+    int in_rows = k ? n : ns;
+    if (k == 0)
+      linear(s, ns, l.up, input, up[k], false, false, status);
+    else
+      linear(s, n, l.up, input, up[k], false, false, status, n, ns);
+    if (dom && k == 1)
+      dom->fetch_ghost_rows(c, up[k], l.in_comp, ns, 128);
+    linear(s, n, l.res, up[k], res, false, false, status, ns);
+    linear(s, n, l.skip, input, skip, false, false, status, in_rows);
     launch_radial(s, c.geometry, l, pair, ea, ro[k]);
     timer.mark("forward" + std::to_string(k) + ".linears/radial");
     if (projection) {
@@ -185,7 +218,7 @@ std::vector<Result> MH1::compute(bool batch) {
         tc_gemm(s, int(q.e1 - q.e0), width, 64, 1, ro[k].h + q.e0 * 64, 0, l.radial.out_hi, l.radial.out_lo,
                 proj[k], width, 0, false, status);
         timer.mark("forward" + std::to_string(k) + ".projection");
-        launch_message_forward_proj(s, k, c.geometry, l, ea, ro[k], q, proj[k], up[k], msg, rho[k]);
+        launch_message_forward_proj(s, k, c.geometry, l, ea, ro[k], q, proj[k], up[k], msg, rho[k], ns);
         timer.mark("forward" + std::to_string(k) + ".messages");
       }
     } else if (tensor_core_edges())
@@ -217,7 +250,7 @@ std::vector<Result> MH1::compute(bool batch) {
   float *hgrad1 = node("mh.b.hgrad1", 512), *hgrad0 = node("mh.b.hgrad0", 2048);
   float *pgrad = node("mh.b.poly", 2048), *pingrad = node("mh.b.pin", 8192), *gategrad = gate;
   float *pregrad = res, *rawgrad = node("mh.b.raw", 9728), *rhograd = node("mh.b.rho", 1);
-  float *msggrad = msg, *upgrad = node("mh.b.up", 512);
+  float *msggrad = msg, *upgrad = sender_node("mh.b.up", 512);
   float4 *edge_force = c.array<float4>("mh.edge.force", E);
   launch_fill(s, n, one, cst[6]);
   linear(s, n, m.read1down, one, rgrad, true, false, status);
@@ -235,8 +268,14 @@ std::vector<Result> MH1::compute(bool batch) {
     launch_gate_norm_backward(s, n, pre[k], raw[k], rho[k], gategrad, l.alpha, l.beta, cst[11], cst[12], pregrad,
                               rawgrad, rhograd);
     linear(s, n, l.one, rawgrad, msggrad, true, false, status);
-    if (k == 1)
-      linear(s, n, l.res, pregrad, upgrad, true, false, status);
+    if (k == 1) {
+      if (dom) { // ghost rows collect the edge kernels' up-gradients for their owners
+        c.clear(upgrad, size_t(ns) * 512 * sizeof(float));
+        linear(s, n, l.res, pregrad, upgrad, true, true, status, n, ns);
+      } else {
+        linear(s, n, l.res, pregrad, upgrad, true, false, status);
+      }
+    }
     timer.mark("backward" + std::to_string(k) + ".node");
     if (projection) {
       int width = l.paths * 128;
@@ -251,7 +290,7 @@ std::vector<Result> MH1::compute(bool batch) {
                   l.radial.out_lo, R, width, (long long)chunk_cap * width, false, status);
         timer.mark("backward" + std::to_string(k) + ".projection");
         launch_message_backward_proj(s, k, c.geometry, l, ea, ro[k], q, R, dR, up[k], msggrad, rhograd, upgrad,
-                                     edge_force, k == 0);
+                                     edge_force, k == 0, ns);
         timer.mark("backward" + std::to_string(k) + ".edges");
       }
     } else if (tensor_core_edges())
@@ -260,14 +299,31 @@ std::vector<Result> MH1::compute(bool batch) {
       launch_message_backward(s, k, c.geometry, l, ea, ro[k], up[k], msggrad, rhograd, upgrad, edge_force, k == 0);
     timer.mark("backward" + std::to_string(k) + ".edges");
     if (k == 1) {
+      if (dom)
+        dom->return_ghost_rows(c, upgrad, l.in_comp, ns, 128);
       linear(s, n, l.skip, hgrad, hgrad0, true, false, status);
-      linear(s, n, l.up, upgrad, hgrad0, true, true, status);
+      linear(s, n, l.up, upgrad, hgrad0, true, true, status, ns, n);
       hgrad = hgrad0;
     }
   }
-  launch_force_gather(s, c.geometry, edge_force, force, virial);
+  if (dom) {
+    launch_force_gather_domain(s, c.geometry, edge_force, force, virial);
+    dom->return_ghost_rows(c, force, 1, ns, 3);
+  } else {
+    launch_force_gather(s, c.geometry, edge_force, force, virial);
+  }
   check(cudaGetLastError());
   timer.mark("forces");
+  if (dom) {
+    // Every rank's owned rows into full-structure arrays, summed over ranks.
+    float *out = c.array<float>("mh.domain.out", size_t(n_full) * 13);
+    dom->gather_outputs(c, energy, force, virial, out, out + n_full, out + size_t(4) * n_full);
+    dom->restore(c);
+    restore_geometry.d = nullptr;
+    energy = out;
+    force = out + n_full;
+    virial = out + size_t(4) * n_full;
+  }
   timer.mark("finish-enqueue");
   std::vector<Result> results;
   if (batch)

@@ -126,23 +126,30 @@ struct ProjectionChunk {
   int r0, r1;
   long long e0, e1;
 };
+// n_up: row stride of up / up_grad (senders; 0: the receiver count g.n).
 void launch_message_forward_proj(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &, EdgeArrays,
                                  RadialOut, const ProjectionChunk &, const float *R, const float *up,
-                                 float *message, float *density);
+                                 float *message, float *density, int n_up = 0);
 void launch_message_backward_proj(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &,
                                   EdgeArrays, RadialOut, const ProjectionChunk &, const float *R, const float *dR,
                                   const float *up, const float *message_grad, const float *density_grad,
-                                  float *up_grad, float4 *edge_force, bool accumulate);
+                                  float *up_grad, float4 *edge_force, bool accumulate, int n_up = 0);
 // Edges per projection chunk (bounds the R / dR buffers at 2 x 1280 floats per edge):
 // 2^20, or MACE_PROJECTION_CHUNK_EDGES when set to a positive value.
 long long projection_chunk_edges();
 void launch_force_gather(cudaStream_t, const lapis::DeviceGeometry &, const float4 *edge_force, float *force,
                          float *virial);
+// Domain-decomposed form: reverse edges outside the local graph (index < 0) are skipped and
+// every edge's reaction on a ghost sender (rows >= g.n of force) is accumulated for its owner.
+void launch_force_gather_domain(cudaStream_t, const lapis::DeviceGeometry &, const float4 *edge_force, float *force,
+                                float *virial);
 
 // Equivariant linear over n nodes: Y (+)= X W per path and component, or the transposed
 // product for the backward.  Paths with tensor-core-eligible shapes run on tc_gemm.
+// nx / ny: row stride of x's / y's component blocks (0: n), for arrays with rows beyond the n
+// computed ones (the ghost rows of a domain-decomposed evaluation).
 void linear(cudaStream_t, int n, const Linear &, const float *x, float *y, bool backward = false,
-            bool add = false, int *status = nullptr);
+            bool add = false, int *status = nullptr, int nx = 0, int ny = 0);
 // Tensor-core GEMM (tc_gemm.cu): C[z] (+)= A[z] B, B = Bhi + Blo given K-major [N][K].
 bool tc_gemm_supported(int N, int K);
 void tc_gemm(cudaStream_t, int M, int N, int K, int batch, const float *A, long long strideA, const float *Bhi,

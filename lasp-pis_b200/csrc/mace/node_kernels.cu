@@ -432,9 +432,14 @@ bool tensor_core_linears() {
   return on;
 }
 
-void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bool backward, bool add, int *status) {
+void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bool backward, bool add, int *status,
+            int nx, int ny) {
   if (!n)
     return;
+  if (!nx)
+    nx = n;
+  if (!ny)
+    ny = n;
   bool tc = tensor_core_linears() && status;
   // Direct stores (no zero fill, no read-modify-write) when every path runs on the tensor
   // cores and the paths' blocks tile the output.
@@ -442,31 +447,31 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
   for (const auto &t : l.tc)
     store = store && (backward ? t.bwd_hi : t.fwd_hi);
   if (!add && !store)
-    lapis::check(cudaMemsetAsync(y, 0, size_t(n) * (backward ? l.input : l.output) * 4, s));
+    lapis::check(cudaMemsetAsync(y, 0, size_t(ny) * (backward ? l.input : l.output) * 4, s));
   for (size_t q = 0; q < l.paths.size(); ++q) {
     const auto &p = l.paths[q];
     const float *w = l.weight + p.weight_offset;
     const TCWeights &t = l.tc[q];
     if (!backward) {
       if (tc && t.fwd_hi) {
-        tc_gemm(s, n, p.out_mul, p.in_mul, p.dim, x + size_t(p.in_offset) * n, (long long)n * p.in_mul, t.fwd_hi,
-                t.fwd_lo, y + size_t(p.out_offset) * n, p.out_mul, (long long)n * p.out_mul, !store, status);
+        tc_gemm(s, n, p.out_mul, p.in_mul, p.dim, x + size_t(p.in_offset) * nx, (long long)nx * p.in_mul, t.fwd_hi,
+                t.fwd_lo, y + size_t(p.out_offset) * ny, p.out_mul, (long long)ny * p.out_mul, !store, status);
         continue;
       }
       dim3 grid((p.out_mul + BN - 1) / BN, (n + BM - 1) / BM, p.dim);
-      lapis::launch(gemm_kernel<false>, grid, 256, 0, s, n, p.out_mul, p.in_mul, x + size_t(p.in_offset) * n,
-                    p.in_mul, (long long)n * p.in_mul, w, p.out_mul, y + size_t(p.out_offset) * n, p.out_mul,
-                    (long long)n * p.out_mul);
+      lapis::launch(gemm_kernel<false>, grid, 256, 0, s, n, p.out_mul, p.in_mul, x + size_t(p.in_offset) * nx,
+                    p.in_mul, (long long)nx * p.in_mul, w, p.out_mul, y + size_t(p.out_offset) * ny, p.out_mul,
+                    (long long)ny * p.out_mul);
     } else {
       if (tc && t.bwd_hi) {
-        tc_gemm(s, n, p.in_mul, p.out_mul, p.dim, x + size_t(p.out_offset) * n, (long long)n * p.out_mul,
-                t.bwd_hi, t.bwd_lo, y + size_t(p.in_offset) * n, p.in_mul, (long long)n * p.in_mul, !store, status);
+        tc_gemm(s, n, p.in_mul, p.out_mul, p.dim, x + size_t(p.out_offset) * nx, (long long)nx * p.out_mul,
+                t.bwd_hi, t.bwd_lo, y + size_t(p.in_offset) * ny, p.in_mul, (long long)ny * p.in_mul, !store, status);
         continue;
       }
       dim3 grid((p.in_mul + BN - 1) / BN, (n + BM - 1) / BM, p.dim);
-      lapis::launch(gemm_kernel<true>, grid, 256, 0, s, n, p.in_mul, p.out_mul, x + size_t(p.out_offset) * n,
-                    p.out_mul, (long long)n * p.out_mul, w, p.out_mul, y + size_t(p.in_offset) * n, p.in_mul,
-                    (long long)n * p.in_mul);
+      lapis::launch(gemm_kernel<true>, grid, 256, 0, s, n, p.in_mul, p.out_mul, x + size_t(p.out_offset) * nx,
+                    p.out_mul, (long long)nx * p.out_mul, w, p.out_mul, y + size_t(p.in_offset) * ny, p.in_mul,
+                    (long long)ny * p.in_mul);
     }
   }
 }

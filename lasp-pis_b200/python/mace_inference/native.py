@@ -29,6 +29,10 @@ def load(path=None) -> ct.CDLL:
     lib.mace_calculate.restype = ct.c_int
     lib.mace_calculate_device.argtypes = [ct.c_void_p, ct.c_int] + [ct.c_void_p] * 7
     lib.mace_calculate_device.restype = ct.c_int
+    lib.mace_create_mh1_domain.argtypes = [ct.c_char_p, ct.c_int, ct.c_int, ct.c_int, ct.c_int, ct.c_char_p]
+    lib.mace_create_mh1_domain.restype = ct.c_void_p
+    lib.mace_nccl_unique_id.argtypes = [ct.c_void_p]
+    lib.mace_nccl_unique_id.restype = ct.c_int
     lib.mace_calculate_batch.argtypes = [ct.c_void_p, ct.c_int] + [ct.c_void_p] * 8
     lib.mace_calculate_batch.restype = ct.c_int
     lib.mace_diagnostics.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_size_t]
@@ -63,13 +67,33 @@ def neighbor_edges(xyz, cell, cutoff=6.0, backend=0, grid_bytes=0, library=None)
     return out[:count]
 
 
-class NativeMH1:
-    """One MH1 handle: ``calculate(xyz, z, cell)`` -> energy, energies, forces, virial."""
+def nccl_unique_id(library=None) -> bytes:
+    """A new 128-byte NCCL id for ``NativeMH1(..., domain=(rank, world, id))`` (make it on one
+    rank and pass it to all)."""
+    lib = load(library)
+    buf = ct.create_string_buffer(128)
+    if lib.mace_nccl_unique_id(buf):
+        raise RuntimeError(_error(lib))
+    return buf.raw
 
-    def __init__(self, archive, backend=0, library=None, device=None, head=None):
+
+class NativeMH1:
+    """One MH1 handle: ``calculate(xyz, z, cell)`` -> energy, energies, forces, virial.
+
+    ``domain=(rank, world, nccl_id)`` decomposes each structure across ``world`` ranks (one
+    process per GPU, ``device`` required): every rank calls with the same full structure and
+    gets the full result; calls are collective."""
+
+    def __init__(self, archive, backend=0, library=None, device=None, head=None, domain=None):
         self.lib = load(library)
         b = {"auto": 0, "brute": 1, "cell": 2}.get(backend, backend)
-        if device is not None:
+        if domain is not None:
+            rank, world, nccl_id = domain
+            if device is None or len(nccl_id) != 128:
+                raise ValueError("domain decomposition needs a device and a 128-byte NCCL id")
+            self.handle = self.lib.mace_create_mh1_domain(str(archive).encode(), b, device, rank, world,
+                                                          ct.c_char_p(bytes(nccl_id)))
+        elif device is not None:
             self.handle = self.lib.mace_create_mh1_device(str(archive).encode(), b, device)
         elif head is not None:
             self.handle = self.lib.mace_create_mh1_head(str(archive).encode(), b, head.encode())
