@@ -7,10 +7,11 @@
 // kernels below consume it:
 //   forward   messages and density, as mace/src/mh1.cu:331-389 (w = cut * (R + b));
 //   backward  tensor-product adjoints, r-tangent and per-edge force, as mh1.cu:390-452.
-// The backward regroups the term sum so that each term costs six FP32 operations: per path
-// Q_p = sum_t cg G[out] u[in] Y[sh] (then dE/dr = sum_p Q_p dw_p), per harmonic
-// T_sh = sum_t cg G[out] u[in] w_p (then dE/dd = sum_sh T_sh dY_sh), and the sender
-// up-gradient sum_t cg G[out] Y[sh] w_p.  dY comes precomputed from the geometry kernel.
+// The backward regroups the term sum into per-path Q_p = sum_t cg G[out] u[in] Y[sh] (then
+// dE/dr = sum_p Q_p dw_p), per-harmonic T_sh = sum_t cg G[out] u[in] w_p (then
+// dE/dd = sum_sh T_sh dY_sh) and the sender up-gradient sum_t cg G[out] Y[sh] w_p, and
+// factors u[in] and w_p out of each (path, in) group of terms: three FP32 operations per term
+// plus three per group.  dY comes precomputed from the geometry kernel.
 //
 // CTA per receiver: warps 0..3 are the channels (thread = channel), warp 4 streams the
 // receiver's edges through a 2-stage shared-memory ring in tiles of T edges with bulk
@@ -35,7 +36,7 @@ using tc::mbar_wait;
 using tc::smem_u32;
 
 constexpr int kStatusEdgeTimeout = 8;
-constexpr int kStages = 2, kThreads = 160;
+constexpr int kThreads = 160;
 
 struct EdgeMeta {
   float4 vec; // d, r
@@ -46,6 +47,7 @@ struct EdgeMeta {
 template <int L, bool Bwd> struct Stage {
   static constexpr int P = Traits<L>::P, IN = Traits<L>::IN;
   static constexpr int T = 2;                         // edges per tile
+  static constexpr int NS = 2;
   static constexpr int ROW = P * 128 * 4;             // bytes of one R row
   static constexpr int R = 0, DR = R + T * ROW, U = DR + (Bwd ? T * ROW : 0), Y = U + T * IN * 512;
   static constexpr int DY = Y + T * 64, META = DY + (Bwd ? T * 192 : 0), BYTES = META + T * sizeof(EdgeMeta);
@@ -67,6 +69,38 @@ struct ProjArgs {
   int *status;
 };
 
+// Terms sharing (path, in) form a group; the backward factors u[in] and w[path] out of each
+// group.  The tables list every group contiguously (checked below).
+template <int L> constexpr bool same_group(int s, int t) {
+  return Traits<L>::term(s).path == Traits<L>::term(t).path && Traits<L>::term(s).in == Traits<L>::term(t).in;
+}
+template <int L> constexpr bool group_start(int t) { return t == 0 || !same_group<L>(t - 1, t); }
+template <int L> constexpr bool group_end(int t) { return t == Traits<L>::NT - 1 || !same_group<L>(t, t + 1); }
+template <int L> constexpr bool groups_contiguous() {
+  for (int s = 0; s < Traits<L>::NT; ++s)
+    for (int t = s + 1; t < Traits<L>::NT; ++t)
+      if (same_group<L>(s, t) && !same_group<L>(t - 1, t))
+        return false;
+  return true;
+}
+static_assert(groups_contiguous<0>() && groups_contiguous<1>(), "tensor-product groups must be contiguous");
+
+// Sums of (v0, v1, v2, v3) over the warp: lane 0 gets v0, lane 2 v1, lane 1 v2, lane 3 v3
+// (component 2 * (lane & 1) + ((lane >> 1) & 1)).  Halving exchanges, then a butterfly:
+// 6 shuffles instead of 20.
+__device__ __forceinline__ float warp_sum4(float v0, float v1, float v2, float v3, int lane) {
+  bool b0 = lane & 1, b1 = lane & 2;
+  float k0 = b0 ? v2 : v0, k1 = b0 ? v3 : v1;
+  k0 += __shfl_xor_sync(0xffffffffu, b0 ? v0 : v2, 1);
+  k1 += __shfl_xor_sync(0xffffffffu, b0 ? v1 : v3, 1);
+  float k = b1 ? k1 : k0;
+  k += __shfl_xor_sync(0xffffffffu, b1 ? k0 : k1, 2);
+  k += __shfl_xor_sync(0xffffffffu, k, 4);
+  k += __shfl_xor_sync(0xffffffffu, k, 8);
+  k += __shfl_xor_sync(0xffffffffu, k, 16);
+  return k;
+}
+
 // OR of `x` over the 128 channel threads (named barrier 1); also a barrier among them.
 __device__ __forceinline__ bool channels_any(bool x) {
   unsigned r;
@@ -84,7 +118,7 @@ template <int L, bool Bwd, bool Accumulate>
 __global__ void __launch_bounds__(kThreads) edge_proj_kernel(ProjArgs a, TPValues cg) {
   using S = Stage<L, Bwd>;
   using Tr = Traits<L>;
-  constexpr int P = Tr::P, NC = Tr::NC, IN = Tr::IN, T = S::T;
+  constexpr int P = Tr::P, NC = Tr::NC, IN = Tr::IN, T = S::T, kStages = S::NS;
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t bars[2 * kStages]; // full[s] | empty[s]
   __shared__ float red[2][4][T][4];
@@ -217,15 +251,26 @@ __global__ void __launch_bounds__(kThreads) edge_proj_kernel(ProjArgs a, TPValue
 #pragma unroll
         for (int q = 0; q < IN; ++q)
           ug[q] = 0.f;
+        // Per group (p, in) with a_t = cg_t G[out_t] and S = sum_t a_t Y[sh_t]:
+        //   Q_p += u[in] S,   ug[in] += w_p S,   T_sh += a_t (u[in] w_p)
+        // -- three operations per term plus three per group.
+        float S = 0.f, uw = 0.f;
         Unroll<0, Tr::NT>::run([&](auto tc_) {
           constexpr int tt = decltype(tc_)::value;
           constexpr TPTerm q = Tr::term(tt);
-          float x = cg.v[tt] * G[q.out];
-          float xu = x * u[q.in];
-          Q[q.path] = fmaf(xu, y[q.sh], Q[q.path]);
-          Tsh[q.sh] = fmaf(xu, w[q.path], Tsh[q.sh]);
-          if constexpr (L > 0)
-            ug[q.in] = fmaf(x, y[q.sh] * w[q.path], ug[q.in]);
+          float at = cg.v[tt] * G[q.out];
+          if constexpr (group_start<L>(tt)) {
+            uw = u[q.in] * w[q.path];
+            S = at * y[q.sh];
+          } else {
+            S = fmaf(at, y[q.sh], S);
+          }
+          Tsh[q.sh] = fmaf(at, uw, Tsh[q.sh]);
+          if constexpr (group_end<L>(tt)) {
+            Q[q.path] = fmaf(u[q.in], S, Q[q.path]);
+            if constexpr (L > 0)
+              ug[q.in] = fmaf(w[q.path], S, ug[q.in]);
+          }
         });
         if constexpr (L > 0) {
           int j = meta[k].sender;
@@ -250,14 +295,9 @@ __global__ void __launch_bounds__(kThreads) edge_proj_kernel(ProjArgs a, TPValue
             g = fmaf(Tsh[sh], gv[m], g);
           }
         }
-        dr = warp_allsum(dr);
-        gx = warp_allsum(gx);
-        gy = warp_allsum(gy);
-        gz = warp_allsum(gz);
-        if (lane == 0) {
-          float *rd = red[t & 1][warp][k];
-          rd[0] = dr, rd[1] = gx, rd[2] = gy, rd[3] = gz;
-        }
+        float sum = warp_sum4(dr, gx, gy, gz, lane);
+        if (lane < 4)
+          red[t & 1][warp][k][2 * (lane & 1) + (lane >> 1)] = sum;
       }
     }
     if constexpr (Bwd) {
@@ -306,7 +346,7 @@ __global__ void __launch_bounds__(kThreads) edge_proj_kernel(ProjArgs a, TPValue
 
 template <int L, bool Bwd, bool Accumulate>
 void launch_proj(cudaStream_t s, int blocks, const ProjArgs &a, const TPValues &cg) {
-  constexpr int smem = kStages * Stage<L, Bwd>::BYTES;
+  constexpr int smem = Stage<L, Bwd>::NS * Stage<L, Bwd>::BYTES;
   static_assert(Stage<L, Bwd>::BYTES % 128 == 0 || true, "");
   lapis::check(
       cudaFuncSetAttribute(edge_proj_kernel<L, Bwd, Accumulate>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
