@@ -106,19 +106,39 @@ __global__ void place_atoms(int n, const int *bin, const int *offsets, int *curs
     i2o[offsets[bin[i]] + atomicAdd(cursor + bin[i], 1)] = i;
 }
 
-// Within each bin, order atoms by input index: a deterministic internal order.
-__global__ void order_bins(int nb, const int *offsets, int *i2o) {
-  int b = blockIdx.x * blockDim.x + threadIdx.x;
+// Within each bin, order atoms by input index: a deterministic internal order.  Warp per bin:
+// the bin's (distinct) indices go to shared memory and each lane places its entries by rank.
+// Bins above kOrderMax atoms (not met with the cell-list bin sizes) use an insertion sort.
+constexpr int kOrderThreads = 256, kOrderMax = 128;
+__global__ void __launch_bounds__(kOrderThreads) order_bins(int nb, const int *offsets, int *i2o) {
+  __shared__ int vals[kOrderThreads / 32][kOrderMax];
+  int b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (b >= nb)
     return;
-  int begin = offsets[b], end = offsets[b + 1];
-  for (int k = begin + 1; k < end; ++k) {
-    int v = i2o[k], q = k - 1;
-    while (q >= begin && i2o[q] > v) {
-      i2o[q + 1] = i2o[q];
-      --q;
-    }
-    i2o[q + 1] = v;
+  int begin = offsets[b], end = offsets[b + 1], cnt = end - begin;
+  if (cnt <= 1)
+    return;
+  if (cnt > kOrderMax) {
+    if (lane == 0)
+      for (int k = begin + 1; k < end; ++k) {
+        int v = i2o[k], q = k - 1;
+        while (q >= begin && i2o[q] > v) {
+          i2o[q + 1] = i2o[q];
+          --q;
+        }
+        i2o[q + 1] = v;
+      }
+    return;
+  }
+  int *v = vals[threadIdx.x >> 5];
+  for (int k = lane; k < cnt; k += 32)
+    v[k] = i2o[begin + k];
+  __syncwarp();
+  for (int k = lane; k < cnt; k += 32) {
+    int x = v[k], rank = 0;
+    for (int q = 0; q < cnt; ++q)
+      rank += v[q] < x;
+    i2o[begin + rank] = x;
   }
 }
 
@@ -619,7 +639,8 @@ void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
   lapis::launch(scan_exclusive, 1, 1024, 0, stream, counts, offsets, nb, nullptr);
   if (n) {
     lapis::launch(place_atoms, blocks, 256, 0, stream, n, bin, offsets, cursor, internal_to_original);
-    lapis::launch(order_bins, (nb + 255) / 256, 256, 0, stream, nb, offsets, internal_to_original);
+    lapis::launch(order_bins, (nb * 32 + kOrderThreads - 1) / kOrderThreads, kOrderThreads, 0, stream, nb, offsets,
+                  internal_to_original);
     lapis::launch(gather_atoms, blocks, 256, 0, stream, n, internal_to_original, wxyz, in_z, bin, wind, sorted, sz, sb, sw,
                                              original_to_internal);
     lapis::launch(bin_stats, (nb + 255) / 256, 256, 0, stream, nb, dims[0], dims[1], dims[2], offsets, stats);

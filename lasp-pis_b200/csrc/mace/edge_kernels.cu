@@ -75,235 +75,319 @@ __global__ void zbl_kernel(DeviceGeometry g, const float *c, const float *radii,
 }
 
 // ---------------- per-edge geometry (warp per receiver, lane per edge) ----------------
-__global__ void geometry_kernel(DeviceGeometry g, const int *species, const float *c, const float *radii,
-                                const float *bessel, EdgeArrays out, int *pair) {
+// A warp's 32 edges are one contiguous block of every per-edge array, so each lane writes its
+// W values to its own padded shared-memory row (stride W + 1: conflict-free) and the warp
+// then stores the block with consecutive lanes on consecutive floats.
+constexpr int kGeometryThreads = 128, kGeometryRow = 49;
+
+template <int W>
+__device__ __forceinline__ void warp_rows_out(float *dst, const float (&v)[W], int cnt, int lane, float *buf) {
+  static_assert(W + 1 <= kGeometryRow, "row buffer too small");
+#pragma unroll
+  for (int k = 0; k < W; ++k)
+    buf[lane * (W + 1) + k] = v[k];
+  __syncwarp();
+  for (int f = lane; f < cnt * W; f += 32)
+    dst[f] = buf[f + f / W];
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(kGeometryThreads)
+    geometry_kernel(DeviceGeometry g, const int *species, const float *c, const float *radii, const float *bessel,
+                    EdgeArrays out, int *pair) {
+  __shared__ float rows[kGeometryThreads / 32][32 * kGeometryRow];
   int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (i >= g.n)
     return;
-  int zi = g.elements[i], si = species[i];
-  for (int e = g.edge_offsets[i] + lane; e < g.edge_offsets[i + 1]; e += 32) {
-    int j = g.edge_sender[e];
-    float4 d = g.edge_vector[e];
+  float *buf = rows[threadIdx.x >> 5];
+  int zi = g.elements[i], si = species[i], end = g.edge_offsets[i + 1];
+  for (int e0 = g.edge_offsets[i]; e0 < end; e0 += 32) {
+    int e = e0 + lane, cnt = min(32, end - e0);
+    bool valid = e < end;
+    float4 d = valid ? g.edge_vector[e] : make_float4(0.f, 0.f, 1.f, 1.f);
+    int j = valid ? g.edge_sender[e] : i;
     float r = d.w;
     if (r <= 0.f) {
       atomicCAS(g.status, 0, 1);
       r = 1e-10f;
     }
     int zj = g.elements[j];
-    pair[e] = species[j] | (si << 16);
     D1 dist{r, 1.f};
     D1 ratio = dist / cst(.5f * (radii[zj] + radii[zi]));
     D1 tr = cst(1.f) / (cst(1.f) + cst(c[3]) * dpow(ratio, c[4]) / (cst(1.f) + dpow(ratio, c[4] - c[5])));
     D1 cut = envelope(dist, c[0], c[2]);
-    out.cut[e] = make_float2(cut.v, cut.d);
+    if (valid) {
+      pair[e] = species[j] | (si << 16);
+      out.cut[e] = make_float2(cut.v, cut.d);
+    }
+    float bv[10], bd[10];
 #pragma unroll
     for (int k = 0; k < 10; ++k) {
       D1 b = cst(c[1]) * dsin(cst(bessel[k]) * tr) / tr;
-      out.basis[size_t(e) * 10 + k] = b.v;
-      out.dbasis[size_t(e) * 10 + k] = b.d;
+      bv[k] = b.v;
+      bd[k] = b.d;
     }
+    warp_rows_out<10>(out.basis + size_t(e0) * 10, bv, cnt, lane, buf);
+    warp_rows_out<10>(out.dbasis + size_t(e0) * 10, bd, cnt, lane, buf);
     float Y[16];
     if (out.dY) {
       float Gy[16][3];
       harmonics<true>(d.x, d.y, d.z, r, Y, Gy);
-#pragma unroll
-      for (int k = 0; k < 16; ++k)
-#pragma unroll
-        for (int q = 0; q < 3; ++q)
-          out.dY[size_t(e) * 48 + 3 * k + q] = Gy[k][q];
+      warp_rows_out<48>(out.dY + size_t(e0) * 48, reinterpret_cast<const float(&)[48]>(Gy), cnt, lane, buf);
     } else {
       harmonics<false>(d.x, d.y, d.z, r, Y, nullptr);
     }
-#pragma unroll
-    for (int k = 0; k < 16; ++k)
-      out.Y[size_t(e) * 16 + k] = Y[k];
+    warp_rows_out<16>(out.Y + size_t(e0) * 16, Y, cnt, lane, buf);
   }
 }
 
-// ---------------- radial MLP (thread per edge) ----------------
-// Each thread owns one edge.  A layer's 64 outputs and their r-tangents accumulate in
-// registers from warp-wide broadcast float4 weight reads, then go to the thread's own padded
-// shared-memory row (stride 65: conflict-free), where LayerNorm (in-thread sums) and SiLU
-// run as rolled loops -- keeping the kernel small enough for the instruction cache -- and
-// leave the next layer's input in place.  The final rows are written out coalesced.
+// ---------------- radial MLP (register-tiled: 4 edges x 8 outputs per lane) ----------------
+// The two 64 x 64 layers are small GEMMs over edges, fed from shared memory, which supplies one
+// 32-lane word per clock against 128 FMA lanes: a lane therefore owns a 4-edge x 8-output tile
+// (value and r-tangent, 64 accumulators), so every shared-memory word it loads feeds four FMAs.
+// Lane = 8 * edge group + output group: the lane's edges are the warp's slots 4 ge .. 4 ge + 3
+// and its outputs u = 8 go .. 8 go + 7.  LayerNorm sums combine the 8 lanes of an edge group
+// with three shuffles.  Weights and vectors are stored permuted ([k][go][12], 8 used) so the 8
+// output groups of a quarter warp read distinct banks.  Each warp keeps its 16 edges' layer
+// inputs in shared rows (value [0, 64), tangent [68, 132)) and their Bessel basis and
+// r-derivative; a CTA of 16 warps (128 registers a thread) takes tiles of 256 edges.
 struct RadialParams {
   Radial conv, dens;
 };
-constexpr int kRadialThreads = 128, kRadialRow = 65;
-// Shared layout (floats): conv input [10][64], W2 / W3 [64 in][64 out], density input
-// [10][64], 13 vectors of 64, then per-thread rows [128][2][65] (value, tangent).
-constexpr int kRadialSmemFloats = 640 + 2 * 4096 + 640 + 13 * 64 + kRadialThreads * 2 * kRadialRow;
+constexpr int kRadialThreads = 512, kRadialWarps = kRadialThreads / 32, kRadialEdgesPerWarp = 16;
+constexpr int kRadialEdges = kRadialWarps * kRadialEdgesPerWarp;
+constexpr int kRadialRow = 132, kRadialTan = 68, kRadialBasis = 20;
+constexpr int kRadialPerm = 96; // floats per permuted 64-vector (8 groups x 12)
+__host__ __device__ constexpr int radial_perm(int u) { return (u >> 3) * 12 + (u & 7); }
+// Shared layout (floats): conv input [10][96], density input [10][96], W2 / W3 [64][96],
+// 13 permuted vectors, then per warp: rows [16][132] and basis [16][20].
+constexpr int kRadialIn = 10 * kRadialPerm, kRadialW = 64 * kRadialPerm, kRadialVecs = 13 * kRadialPerm;
+constexpr int kRadialWarpFloats = kRadialEdgesPerWarp * (kRadialRow + kRadialBasis);
+constexpr int kRadialSmemFloats = 2 * kRadialIn + 2 * kRadialW + kRadialVecs + kRadialWarps * kRadialWarpFloats;
 
-// Store accumulators to the row, then LayerNorm (biased variance, eps 1e-5) + SiLU with the
-// forward tangent, in place.
-__device__ __forceinline__ void row_ln_silu(const float (&a)[64], const float (&da)[64], float *row, float *drow,
-                                            const float *gamma, const float *beta) {
-  float s0 = 0.f, s1 = 0.f, d0 = 0.f, d1 = 0.f;
+// Sum over the 8 lanes of an edge group.
+__device__ __forceinline__ float group_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  return v + __shfl_xor_sync(0xffffffffu, v, 4);
+}
+
+__device__ __forceinline__ void load8(const float *p, float (&v)[8]) {
+  float4 x = *reinterpret_cast<const float4 *>(p), y = *reinterpret_cast<const float4 *>(p + 4);
+  v[0] = x.x, v[1] = x.y, v[2] = x.z, v[3] = x.w, v[4] = y.x, v[5] = y.y, v[6] = y.z, v[7] = y.w;
+}
+
+// LayerNorm (biased variance, eps 1e-5) + SiLU with the forward tangent on the lane's 8
+// outputs of edge i (statistics over the edge group's 8 lanes).
+__device__ __forceinline__ void tile_ln_silu(float (&a)[8], float (&da)[8], const float *gamma, const float *beta) {
+  float s = 0.f, d = 0.f;
 #pragma unroll
-  for (int u = 0; u < 64; u += 2) {
-    row[u] = a[u], row[u + 1] = a[u + 1];
-    drow[u] = da[u], drow[u + 1] = da[u + 1];
-    s0 += a[u], s1 += a[u + 1];
-    d0 += da[u], d1 += da[u + 1];
+  for (int m = 0; m < 8; ++m)
+    s += a[m], d += da[m];
+  float mean = group_sum(s) * (1.f / 64), dmean = group_sum(d) * (1.f / 64);
+  float v = 0.f, c = 0.f;
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    a[m] -= mean;
+    da[m] -= dmean;
+    v = fmaf(a[m], a[m], v);
+    c = fmaf(a[m], da[m], c);
   }
-  float mean = (s0 + s1) * (1.f / 64), dmean = (d0 + d1) * (1.f / 64);
-  float v0 = 0.f, v1 = 0.f, c0 = 0.f, c1 = 0.f;
-#pragma unroll 4
-  for (int u = 0; u < 64; u += 2) {
-    float x0 = row[u] - mean, x1 = row[u + 1] - mean;
-    float t0 = drow[u] - dmean, t1 = drow[u + 1] - dmean;
-    v0 = fmaf(x0, x0, v0), v1 = fmaf(x1, x1, v1);
-    c0 = fmaf(x0, t0, c0), c1 = fmaf(x1, t1, c1);
-  }
-  float inv = rsqrtf((v0 + v1) * (1.f / 64) + 1e-5f);
-  float dinv = -inv * inv * inv * (c0 + c1) * (1.f / 64);
-#pragma unroll 2
-  for (int u = 0; u < 64; ++u) {
-    float xc = row[u] - mean, tc = drow[u] - dmean;
-    float x = xc * inv * gamma[u] + beta[u];
+  float inv = rsqrtf(group_sum(v) * (1.f / 64) + 1e-5f);
+  float dinv = -inv * inv * inv * group_sum(c) * (1.f / 64);
+  float g[8], bt[8];
+  load8(gamma, g);
+  load8(beta, bt);
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    float x = a[m] * inv * g[m] + bt[m];
     float sg = sigm(x);
-    float dx = (tc * inv + xc * dinv) * gamma[u];
-    row[u] = x * sg;
-    drow[u] = dx * sg * (1.f + x * (1.f - sg));
+    float dx = (da[m] * inv + a[m] * dinv) * g[m];
+    a[m] = x * sg;
+    da[m] = dx * sg * (1.f + x * (1.f - sg));
   }
 }
 
-// First layer: a = b0 + source[zs] + target[zr] + W1 x, da = W1 dx.
-__device__ __forceinline__ void radial_input(float (&a)[64], float (&da)[64], const float *w1, const float *b0,
-                                             const float *source, const float *target, int zs, int zr,
-                                             const float (&x)[10], const float (&dx)[10]) {
-  const float4 *src = reinterpret_cast<const float4 *>(source + zs * 64);
-  const float4 *tgt = reinterpret_cast<const float4 *>(target + zr * 64);
+// Input layer for the lane's 4 edges: a = b0 + source[zs] + target[zr] + W1 x, da = W1 dx.
+__device__ __forceinline__ void tile_input(float (&a)[4][8], float (&da)[4][8], const float *w1, const float *b0,
+                                           const float *source, const float *target, const int (&zs)[4],
+                                           const int (&zr)[4], int u0, const float *bas) {
+  float b[8];
+  load8(b0, b);
 #pragma unroll
-  for (int q = 0; q < 16; ++q) {
-    float4 sv = __ldg(src + q), tv = __ldg(tgt + q);
-    a[4 * q] = b0[4 * q] + sv.x + tv.x;
-    a[4 * q + 1] = b0[4 * q + 1] + sv.y + tv.y;
-    a[4 * q + 2] = b0[4 * q + 2] + sv.z + tv.z;
-    a[4 * q + 3] = b0[4 * q + 3] + sv.w + tv.w;
-    da[4 * q] = da[4 * q + 1] = da[4 * q + 2] = da[4 * q + 3] = 0.f;
+  for (int i = 0; i < 4; ++i) {
+    const float4 *sp = reinterpret_cast<const float4 *>(source + zs[i] * 64 + u0);
+    const float4 *tp = reinterpret_cast<const float4 *>(target + zr[i] * 64 + u0);
+    float4 s0 = __ldg(sp), s1 = __ldg(sp + 1), t0 = __ldg(tp), t1 = __ldg(tp + 1);
+    float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    float tv[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      a[i][m] = b[m] + sv[m] + tv[m];
+      da[i][m] = 0.f;
+    }
   }
-#pragma unroll 1
+#pragma unroll 2
   for (int k = 0; k < 10; ++k) {
-    const float4 *w = reinterpret_cast<const float4 *>(w1 + k * 64);
-    float xk = x[k], dxk = dx[k];
+    float w[8];
+    load8(w1 + k * kRadialPerm, w);
 #pragma unroll
-    for (int q = 0; q < 16; ++q) {
-      float4 wv = w[q];
-      a[4 * q] = fmaf(wv.x, xk, a[4 * q]);
-      a[4 * q + 1] = fmaf(wv.y, xk, a[4 * q + 1]);
-      a[4 * q + 2] = fmaf(wv.z, xk, a[4 * q + 2]);
-      a[4 * q + 3] = fmaf(wv.w, xk, a[4 * q + 3]);
-      da[4 * q] = fmaf(wv.x, dxk, da[4 * q]);
-      da[4 * q + 1] = fmaf(wv.y, dxk, da[4 * q + 1]);
-      da[4 * q + 2] = fmaf(wv.z, dxk, da[4 * q + 2]);
-      da[4 * q + 3] = fmaf(wv.w, dxk, da[4 * q + 3]);
+    for (int i = 0; i < 4; ++i) {
+      float xk = bas[i * kRadialBasis + k], dxk = bas[i * kRadialBasis + 10 + k];
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        a[i][m] = fmaf(w[m], xk, a[i][m]);
+        da[i][m] = fmaf(w[m], dxk, da[i][m]);
+      }
     }
   }
 }
 
-__global__ void __launch_bounds__(kRadialThreads) radial_kernel(long long E, RadialParams R, const int *pair,
+// The lane's outputs into its edges' rows (after every lane of the warp has read them).
+__device__ __forceinline__ void tile_store(float *rows, const float (&a)[4][8], const float (&da)[4][8], int u0) {
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float *r = rows + i * kRadialRow + u0;
+    *reinterpret_cast<float4 *>(r) = make_float4(a[i][0], a[i][1], a[i][2], a[i][3]);
+    *reinterpret_cast<float4 *>(r + 4) = make_float4(a[i][4], a[i][5], a[i][6], a[i][7]);
+    *reinterpret_cast<float4 *>(r + kRadialTan) = make_float4(da[i][0], da[i][1], da[i][2], da[i][3]);
+    *reinterpret_cast<float4 *>(r + kRadialTan + 4) = make_float4(da[i][4], da[i][5], da[i][6], da[i][7]);
+  }
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(kRadialThreads, 1) radial_kernel(long long E, RadialParams R, const int *pair,
                                                                 EdgeArrays ea, RadialOut ro) {
-  extern __shared__ float sm[];
-  float *c_in = sm, *c_w1 = c_in + 640, *c_w2 = c_w1 + 4096, *d_in = c_w2 + 4096, *vecs = d_in + 640;
-  float *c_b0 = vecs, *c_b1 = vecs + 64, *c_b2 = vecs + 128, *d_b0 = vecs + 192, *d_out = vecs + 256;
-  float *c_g = vecs + 320, *c_bt = c_g + 192, *d_g = c_bt + 192, *d_bt = d_g + 64;
-  float *rows = vecs + 13 * 64;
-  int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  extern __shared__ __align__(16) float sm[];
+  float *c_in = sm, *d_in = c_in + kRadialIn, *c_w = d_in + kRadialIn, *vecs = c_w + 2 * kRadialW;
+  float *c_b = vecs, *c_g = vecs + 3 * kRadialPerm, *c_bt = vecs + 6 * kRadialPerm;
+  float *d_b0 = vecs + 9 * kRadialPerm, *d_g = vecs + 10 * kRadialPerm, *d_bt = vecs + 11 * kRadialPerm;
+  float *d_out = vecs + 12 * kRadialPerm;
+  int t = threadIdx.x, lane = t & 31, warp = t >> 5, go = lane & 7, ge = lane >> 3;
+  float *wrows = vecs + kRadialVecs + warp * kRadialWarpFloats;
+  float *wbas = wrows + kRadialEdgesPerWarp * kRadialRow;
   for (int k = t; k < 640; k += kRadialThreads) {
-    c_in[k] = R.conv.input_t[k];
-    d_in[k] = R.dens.input_t[k];
+    int o = (k >> 6) * kRadialPerm + radial_perm(k & 63);
+    c_in[o] = R.conv.input_t[k];
+    d_in[o] = R.dens.input_t[k];
   }
   for (int k = t; k < 4096; k += kRadialThreads) {
-    c_w1[k] = R.conv.weight_t[1][k];
-    c_w2[k] = R.conv.weight_t[2][k];
+    int o = (k >> 6) * kRadialPerm + radial_perm(k & 63);
+    c_w[o] = R.conv.weight_t[1][k];
+    c_w[kRadialW + o] = R.conv.weight_t[2][k];
   }
   for (int k = t; k < 64; k += kRadialThreads) {
-    c_b0[k] = R.conv.bias0[k];
-    c_b1[k] = R.conv.bias[1][k];
-    c_b2[k] = R.conv.bias[2][k];
-    d_b0[k] = R.dens.bias0[k];
-    d_out[k] = R.dens.out_t[k];
+    int o = radial_perm(k);
+    c_b[o] = R.conv.bias0[k];
+    c_b[kRadialPerm + o] = R.conv.bias[1][k];
+    c_b[2 * kRadialPerm + o] = R.conv.bias[2][k];
     for (int l = 0; l < 3; ++l) {
-      c_g[l * 64 + k] = R.conv.gamma[l][k];
-      c_bt[l * 64 + k] = R.conv.beta[l][k];
+      c_g[l * kRadialPerm + o] = R.conv.gamma[l][k];
+      c_bt[l * kRadialPerm + o] = R.conv.beta[l][k];
     }
-    d_g[k] = R.dens.gamma[0][k];
-    d_bt[k] = R.dens.beta[0][k];
+    d_b0[o] = R.dens.bias0[k];
+    d_g[o] = R.dens.gamma[0][k];
+    d_bt[o] = R.dens.beta[0][k];
+    d_out[o] = R.dens.out_t[k];
   }
   __syncthreads();
-  float d_ob = R.dens.out_b[0];
-  float *my = rows + t * 2 * kRadialRow, *my_d = my + kRadialRow;
-  for (long long base = (long long)blockIdx.x * kRadialThreads; base < E; base += (long long)gridDim.x * kRadialThreads) {
-    long long e = base + t;
-    bool ok = e < E;
-    int p = ok ? pair[e] : 0, zs = p & 0xffff, zr = p >> 16;
-    float x[10], dx[10];
-#pragma unroll
-    for (int k = 0; k < 10; ++k) {
-      x[k] = ok ? ea.basis[e * 10 + k] : 0.f;
-      dx[k] = ok ? ea.dbasis[e * 10 + k] : 0.f;
+  const float d_ob = R.dens.out_b[0];
+  const int u0 = 8 * go, po = go * 12; // the lane's outputs and their block in a permuted vector
+  float *rows = wrows + 4 * ge * kRadialRow;
+  const float *bas = wbas + 4 * ge * kRadialBasis;
+  for (long long base = (long long)blockIdx.x * kRadialEdges; base < E; base += (long long)gridDim.x * kRadialEdges) {
+    long long wbase = base + warp * kRadialEdgesPerWarp;
+    int wcnt = E - wbase < kRadialEdgesPerWarp ? int(max(E - wbase, 0LL)) : kRadialEdgesPerWarp;
+    // ---- the warp's 16 edges: Bessel basis and r-derivative into shared memory ----
+    for (int f = lane; f < kRadialEdgesPerWarp * 10; f += 32) {
+      int j = f / 10, k = f - 10 * j;
+      bool ok = j < wcnt;
+      wbas[j * kRadialBasis + k] = ok ? ea.basis[size_t(wbase) * 10 + f] : 0.f;
+      wbas[j * kRadialBasis + 10 + k] = ok ? ea.dbasis[size_t(wbase) * 10 + f] : 0.f;
     }
-    float2 cv = ok ? ea.cut[e] : make_float2(0.f, 0.f);
-    float a[64], da[64];
+    int zs[4], zr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      int j = 4 * ge + i, p = j < wcnt ? pair[wbase + j] : 0;
+      zs[i] = p & 0xffff, zr[i] = p >> 16;
+    }
+    __syncwarp();
+    float a[4][8], da[4][8];
     // ---- conv radial network: 10 -> 64 -> 64 -> 64 ----
-    radial_input(a, da, c_in, c_b0, R.conv.source, R.conv.target, zs, zr, x, dx);
-    row_ln_silu(a, da, my, my_d, c_g, c_bt);
+    tile_input(a, da, c_in + po, c_b + po, R.conv.source, R.conv.target, zs, zr, u0, bas);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      tile_ln_silu(a[i], da[i], c_g + po, c_bt + po);
+    tile_store(rows, a, da, u0);
 #pragma unroll 1
     for (int layer = 1; layer < 3; ++layer) {
-      const float *W = layer == 1 ? c_w1 : c_w2, *bias = layer == 1 ? c_b1 : c_b2;
+      const float *W = c_w + (layer - 1) * kRadialW + po;
+      float b[8];
+      load8(c_b + layer * kRadialPerm + po, b);
 #pragma unroll
-      for (int u = 0; u < 64; ++u) {
-        a[u] = bias[u];
-        da[u] = 0.f;
-      }
-#pragma unroll 1
-      for (int k = 0; k < 64; ++k) {
-        float hv = my[k], dv = my_d[k];
-        const float4 *w = reinterpret_cast<const float4 *>(W + k * 64);
+      for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          float4 wv = w[q];
-          a[4 * q] = fmaf(wv.x, hv, a[4 * q]);
-          a[4 * q + 1] = fmaf(wv.y, hv, a[4 * q + 1]);
-          a[4 * q + 2] = fmaf(wv.z, hv, a[4 * q + 2]);
-          a[4 * q + 3] = fmaf(wv.w, hv, a[4 * q + 3]);
-          da[4 * q] = fmaf(wv.x, dv, da[4 * q]);
-          da[4 * q + 1] = fmaf(wv.y, dv, da[4 * q + 1]);
-          da[4 * q + 2] = fmaf(wv.z, dv, da[4 * q + 2]);
-          da[4 * q + 3] = fmaf(wv.w, dv, da[4 * q + 3]);
+        for (int m = 0; m < 8; ++m) {
+          a[i][m] = b[m];
+          da[i][m] = 0.f;
         }
+#pragma unroll 2
+      for (int k = 0; k < 64; ++k) {
+        float w[8], hv[4], dv[4];
+        load8(W + k * kRadialPerm, w);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          hv[i] = rows[i * kRadialRow + k];
+          dv[i] = rows[i * kRadialRow + kRadialTan + k];
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int m = 0; m < 8; ++m) {
+            a[i][m] = fmaf(w[m], hv[i], a[i][m]);
+            da[i][m] = fmaf(w[m], dv[i], da[i][m]);
+          }
       }
-      row_ln_silu(a, da, my, my_d, c_g + layer * 64, c_bt + layer * 64);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        tile_ln_silu(a[i], da[i], c_g + layer * kRadialPerm + po, c_bt + layer * kRadialPerm + po);
+      tile_store(rows, a, da, u0);
     }
-    // ---- coalesced write of h / dh: 32 consecutive edges per warp ----
-    __syncwarp();
-    long long wbase = base + warp * 32;
-    const float *wrows = rows + warp * 32 * 2 * kRadialRow;
-#pragma unroll 1
-    for (int r = 0; r < 32 && wbase + r < E; ++r) {
-      const float *src = wrows + r * 2 * kRadialRow;
-      size_t o = size_t(wbase + r) * 64;
-      ro.h[o + lane] = src[lane];
-      ro.h[o + 32 + lane] = src[32 + lane];
-      ro.dh[o + lane] = src[kRadialRow + lane];
-      ro.dh[o + 32 + lane] = src[kRadialRow + 32 + lane];
-    }
-    __syncwarp();
-    // ---- density network: 10 -> 64, LayerNorm + SiLU, -> 1, tanh(a^2) x cutoff ----
-    radial_input(a, da, d_in, d_b0, R.dens.source, R.dens.target, zs, zr, x, dx);
-    row_ln_silu(a, da, my, my_d, d_g, d_bt);
-    float sv = d_ob, dsv = 0.f;
+    // ---- coalesced write of h / dh: the warp's 16 consecutive edges ----
 #pragma unroll 4
-    for (int u = 0; u < 64; ++u) {
-      sv = fmaf(d_out[u], my[u], sv);
-      dsv = fmaf(d_out[u], my_d[u], dsv);
+    for (int f = lane; f < kRadialEdgesPerWarp * 64; f += 32) {
+      int r = f >> 6, c = f & 63;
+      if (r < wcnt) {
+        size_t o = size_t(wbase) * 64 + f;
+        ro.h[o] = wrows[r * kRadialRow + c];
+        ro.dh[o] = wrows[r * kRadialRow + kRadialTan + c];
+      }
     }
-    __syncwarp();
-    if (ok) {
-      float den = tanhf(sv * sv);
-      ro.density[e] = make_float2(den * cv.x, 2.f * sv * dsv * (1.f - den * den) * cv.x + den * cv.y);
+    // ---- density network: 10 -> 64, LayerNorm + SiLU, -> 1, tanh(a^2) x cutoff ----
+    tile_input(a, da, d_in + po, d_b0 + po, R.dens.source, R.dens.target, zs, zr, u0, bas);
+    float ow[8];
+    load8(d_out + po, ow);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      tile_ln_silu(a[i], da[i], d_g + po, d_bt + po);
+      float sv = 0.f, dsv = 0.f;
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        sv = fmaf(ow[m], a[i][m], sv);
+        dsv = fmaf(ow[m], da[i][m], dsv);
+      }
+      sv = group_sum(sv) + d_ob;
+      dsv = group_sum(dsv);
+      int j = 4 * ge + i;
+      if (go == 0 && j < wcnt) {
+        long long e = wbase + j;
+        float2 cv = ea.cut[e];
+        float den = tanhf(sv * sv);
+        ro.density[e] = make_float2(den * cv.x, 2.f * sv * dsv * (1.f - den * den) * cv.x + den * cv.y);
+      }
     }
+    __syncwarp(); // rows and basis are rewritten by the next tile
   }
 }
 
@@ -639,7 +723,8 @@ void launch_zbl(cudaStream_t s, const DeviceGeometry &g, const float *constants,
 void launch_edge_geometry(cudaStream_t s, const DeviceGeometry &g, const int *species, const float *constants,
                           const float *radii, const float *bessel, EdgeArrays ea, int *pair) {
   if (g.n)
-    lapis::launch(geometry_kernel, (g.n * 32 + 255) / 256, 256, 0, s, g, species, constants, radii, bessel, ea, pair);
+    lapis::launch(geometry_kernel, (g.n * 32 + kGeometryThreads - 1) / kGeometryThreads, kGeometryThreads, 0, s, g,
+                  species, constants, radii, bessel, ea, pair);
 }
 
 void launch_radial(cudaStream_t s, const DeviceGeometry &g, const Layer &l, const int *pair, EdgeArrays ea,
@@ -649,7 +734,7 @@ void launch_radial(cudaStream_t s, const DeviceGeometry &g, const Layer &l, cons
     return;
   size_t smem = kRadialSmemFloats * sizeof(float);
   lapis::check(cudaFuncSetAttribute(radial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  long long tiles = (E + kRadialThreads - 1) / kRadialThreads;
+  long long tiles = (E + kRadialEdges - 1) / kRadialEdges;
   int blocks = int(std::min<long long>(tiles, 148 * 2));
   lapis::launch(radial_kernel, blocks, kRadialThreads, smem, s, E, RadialParams{l.radial, l.density}, pair, ea, ro);
 }

@@ -14,7 +14,7 @@
 // plus three per group.  dY comes precomputed from the geometry kernel.
 //
 // CTA per receiver: warps 0..3 are the channels (thread = channel), warp 4 streams the
-// receiver's edges through a 2-stage shared-memory ring in tiles of T edges with bulk
+// receiver's edges through a 2- to 4-stage shared-memory ring in tiles of T edges with bulk
 // copies completing on an mbarrier -- the R (and dR) rows (contiguous, receiver-major),
 // the sender's up-projected features, Y (and dY) -- plus per-edge metadata, so the channel
 // warps read only shared memory.  Per-edge scalars are reduced over the 128 channels with
@@ -47,7 +47,9 @@ struct EdgeMeta {
 template <int L, bool Bwd> struct Stage {
   static constexpr int P = Traits<L>::P, IN = Traits<L>::IN;
   static constexpr int T = 2;                         // edges per tile
-  static constexpr int NS = 2;
+  // Ring depth: the layer-1 backward keeps 2 stages (50 KB) so that 3 CTAs fit an SM at its
+  // 128 registers; the lighter kernels take deeper rings within the same occupancy.
+  static constexpr int NS = Bwd ? (L ? 2 : 3) : 4;
   static constexpr int ROW = P * 128 * 4;             // bytes of one R row
   static constexpr int R = 0, DR = R + T * ROW, U = DR + (Bwd ? T * ROW : 0), Y = U + T * IN * 512;
   static constexpr int DY = Y + T * 64, META = DY + (Bwd ? T * 192 : 0), BYTES = META + T * sizeof(EdgeMeta);
@@ -115,7 +117,7 @@ __device__ __forceinline__ bool channels_any(bool x) {
 }
 
 template <int L, bool Bwd, bool Accumulate>
-__global__ void __launch_bounds__(kThreads) edge_proj_kernel(ProjArgs a, TPValues cg) {
+__global__ void __launch_bounds__(kThreads, L ? 3 : 6) edge_proj_kernel(ProjArgs a, TPValues cg) {
   using S = Stage<L, Bwd>;
   using Tr = Traits<L>;
   constexpr int P = Tr::P, NC = Tr::NC, IN = Tr::IN, T = S::T, kStages = S::NS;
@@ -138,43 +140,54 @@ __global__ void __launch_bounds__(kThreads) edge_proj_kernel(ProjArgs a, TPValue
 
   if (warp == 4) {
     // ---------------- producer ----------------
-    for (int t = 0; t < ntiles; ++t) {
-      int s = t % kStages;
-      bool ok = t < kStages || mbar_wait(empty0 + 8 * s, ((t / kStages) - 1) & 1, &abort_flag);
-      if (!__all_sync(0xffffffffu, ok))
-        break;
-      unsigned char *st = smem + s * S::BYTES;
-      unsigned sb = smem_u32(st), full = full0 + 8 * s;
-      int e0 = begin + t * T, cnt = min(T, end - e0), j = 0;
-      if (lane < cnt) {
-        int e = e0 + lane;
-        EdgeMeta m;
-        m.vec = a.vec[e];
-        m.cut = a.cut[e];
-        m.den = a.den[e];
-        m.sender = j = a.sender[e];
-        reinterpret_cast<EdgeMeta *>(st + S::META)[lane] = m;
+    // Edge metadata is read 32 edges (32 / T tiles) at a time, one edge per lane, so the
+    // global round trip is paid once per chunk rather than once per tile.
+    constexpr int kChunkTiles = 32 / T;
+    bool run = true;
+    for (int c0 = 0; c0 < ntiles && run; c0 += kChunkTiles) {
+      int me = begin + c0 * T + lane, j = 0;
+      EdgeMeta m{};
+      if (me < end) {
+        m.vec = a.vec[me];
+        m.cut = a.cut[me];
+        m.den = a.den[me];
+        m.sender = j = a.sender[me];
       }
-      __syncwarp();
-      if (lane == 0)
-        mbar_expect_tx(full, S::tx(cnt));
-      __syncwarp();
-      if (lane == 0) {
-        size_t r = size_t(e0 - a.e_base) * (P * 128);
-        bulk_load(sb + S::R, a.R + r, cnt * S::ROW, full);
-        if constexpr (Bwd)
-          bulk_load(sb + S::DR, a.dR + r, cnt * S::ROW, full);
-        bulk_load(sb + S::Y, a.Y + size_t(e0) * 16, cnt * 64, full);
-        if constexpr (Bwd)
-          bulk_load(sb + S::DY, a.dY + size_t(e0) * 48, cnt * 192, full);
-      }
-      if (lane < cnt) {
+      int tend = min(ntiles, c0 + kChunkTiles);
+      for (int t = c0; t < tend; ++t) {
+        int s = t % kStages;
+        bool ok = t < kStages || mbar_wait(empty0 + 8 * s, ((t / kStages) - 1) & 1, &abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) {
+          run = false;
+          break;
+        }
+        unsigned char *st = smem + s * S::BYTES;
+        unsigned sb = smem_u32(st), full = full0 + 8 * s;
+        int e0 = begin + t * T, cnt = min(T, end - e0), k = lane - (t - c0) * T;
+        bool mine = k >= 0 && k < cnt; // this lane holds the tile's edge k
+        if (mine)
+          reinterpret_cast<EdgeMeta *>(st + S::META)[k] = m;
+        __syncwarp();
+        if (lane == 0)
+          mbar_expect_tx(full, S::tx(cnt));
+        __syncwarp();
+        if (lane == 0) {
+          size_t r = size_t(e0 - a.e_base) * (P * 128);
+          bulk_load(sb + S::R, a.R + r, cnt * S::ROW, full);
+          if constexpr (Bwd)
+            bulk_load(sb + S::DR, a.dR + r, cnt * S::ROW, full);
+          bulk_load(sb + S::Y, a.Y + size_t(e0) * 16, cnt * 64, full);
+          if constexpr (Bwd)
+            bulk_load(sb + S::DY, a.dY + size_t(e0) * 48, cnt * 192, full);
+        }
+        if (mine) {
 #pragma unroll
-        for (int q = 0; q < IN; ++q)
-          bulk_load(sb + S::U + (lane * IN + q) * 512, a.up + (size_t(q) * a.n_up + j) * 128, 512, full);
+          for (int q = 0; q < IN; ++q)
+            bulk_load(sb + S::U + (k * IN + q) * 512, a.up + (size_t(q) * a.n_up + j) * 128, 512, full);
+        }
+        if (lane != 0)
+          mbar_arrive(full);
       }
-      if (lane != 0)
-        mbar_arrive(full);
     }
     return;
   }

@@ -183,8 +183,8 @@ std::vector<Result> MH1::compute(bool batch) {
   timer.mark("embedding/ZBL/geometry");
   RadialOut ro[2];
   float *proj[2] = {nullptr, nullptr}; // [R | dR] per layer, chunk_cap rows each
-  float *up[2], *rho[2], *raw[2], *pre[2], *pin[2], *hidden[2];
-  float *res = node("mh.t.res", 9728), *skip = node("mh.t.skip", 2048), *msg = node("mh.t.msg", 5120),
+  float *up[2], *rho[2], *raw[2], *res[2], *pin[2], *hidden[2];
+  float *skip = node("mh.t.skip", 2048), *msg = node("mh.t.msg", 5120),
         *gate = node("mh.t.gate", 8192), *poly = node("mh.t.poly", 2048), *node_e = node("mh.t.energy", 1);
   const float *input = x0;
   for (int k = 0; k < 2; ++k) {
@@ -193,7 +193,7 @@ std::vector<Result> MH1::compute(bool batch) {
     up[k] = sender_node(p + ".up", l.in_comp * 128);
     rho[k] = node(p + ".rho", 1);
     raw[k] = node(p + ".raw", 9728);
-    pre[k] = node(p + ".pre", 9728);
+    res[k] = node(p + ".res", 9728); // kept: the backward recomputes raw / den + res
     pin[k] = node(p + ".pin", 8192);
     hidden[k] = node(p + ".hidden", k ? 512 : 2048);
     float *hd = c.array<float>(p + ".hd", 2 * E * 64); // h then dh/dr, one GEMM batch apart
@@ -209,7 +209,7 @@ std::vector<Result> MH1::compute(bool batch) {
       linear(s, n, l.up, input, up[k], false, false, status, n, ns);
     if (dom && k == 1)
       dom->fetch_ghost_rows(c, up[k], l.in_comp, ns, 128);
-    linear(s, n, l.res, up[k], res, false, false, status, ns);
+    linear(s, n, l.res, up[k], res[k], false, false, status, ns);
     linear(s, n, l.skip, input, skip, false, false, status, in_rows);
     launch_radial(s, c.geometry, l, pair, ea, ro[k]);
     timer.mark("forward" + std::to_string(k) + ".linears/radial");
@@ -227,7 +227,7 @@ std::vector<Result> MH1::compute(bool batch) {
       launch_message_forward(s, k, c.geometry, l, ea, ro[k], up[k], msg, rho[k]);
     timer.mark("forward" + std::to_string(k) + ".messages");
     linear(s, n, l.one, msg, raw[k], false, false, status);
-    launch_normalize_gate(s, n, raw[k], res, rho[k], l.alpha, l.beta, cst[11], cst[12], pre[k], gate);
+    launch_normalize_gate(s, n, raw[k], res[k], rho[k], l.alpha, l.beta, cst[11], cst[12], gate);
     linear(s, n, l.two, gate, pin[k], false, false, status);
     launch_product(s, n, l, pin[k], poly);
     linear(s, n, l.plin, poly, hidden[k], false, false, status);
@@ -249,7 +249,7 @@ std::vector<Result> MH1::compute(bool batch) {
   float *one = node_e;
   float *hgrad1 = node("mh.b.hgrad1", 512), *hgrad0 = node("mh.b.hgrad0", 2048);
   float *pgrad = node("mh.b.poly", 2048), *pingrad = node("mh.b.pin", 8192), *gategrad = gate;
-  float *pregrad = res, *rawgrad = node("mh.b.raw", 9728), *rhograd = node("mh.b.rho", 1);
+  float *rawgrad = node("mh.b.raw", 9728), *rhograd = node("mh.b.rho", 1);
   float *msggrad = msg, *upgrad = sender_node("mh.b.up", 512);
   float4 *edge_force = c.array<float4>("mh.edge.force", E);
   launch_fill(s, n, one, cst[6]);
@@ -265,7 +265,8 @@ std::vector<Result> MH1::compute(bool batch) {
     linear(s, n, l.plin, hgrad, pgrad, true, false, status);
     launch_product_backward(s, n, l, pin[k], pgrad, pingrad);
     linear(s, n, l.two, pingrad, gategrad, true, false, status);
-    launch_gate_norm_backward(s, n, pre[k], raw[k], rho[k], gategrad, l.alpha, l.beta, cst[11], cst[12], pregrad,
+    float *pregrad = res[k]; // written in place over res[k]
+    launch_gate_norm_backward(s, n, res[k], raw[k], rho[k], gategrad, l.alpha, l.beta, cst[11], cst[12], pregrad,
                               rawgrad, rhograd);
     linear(s, n, l.one, rawgrad, msggrad, true, false, status);
     if (k == 1) {

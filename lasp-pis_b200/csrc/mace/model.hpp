@@ -158,10 +158,11 @@ void tc_gemm(cudaStream_t, int M, int N, int K, int batch, const float *A, long 
 void split_tf32(const float *w, size_t count, float *hi, float *lo);
 // Use the tensor-core path in linear() (default true; MACE_SIMT_LINEARS=1 disables).
 bool tensor_core_linears();
+// pre = raw / (alpha + beta density) + res is not stored: the backward recomputes it from raw
+// and res (the same FP32 expression, so the same values).  pre_grad may alias res.
 void launch_normalize_gate(cudaStream_t, int n, const float *raw, const float *res, const float *density,
-                           float alpha, float beta, float scalar_scale, float gate_scale, float *pre,
-                           float *gate);
-void launch_gate_norm_backward(cudaStream_t, int n, const float *pre, const float *raw, const float *density,
+                           float alpha, float beta, float scalar_scale, float gate_scale, float *gate);
+void launch_gate_norm_backward(cudaStream_t, int n, const float *res, const float *raw, const float *density,
                                const float *gate_grad, float alpha, float beta, float scalar_scale,
                                float gate_scale, float *pre_grad, float *raw_grad, float *density_grad);
 void launch_product(cudaStream_t, int n, const Layer &, const float *x, float *y);

@@ -81,6 +81,62 @@ __global__ void __launch_bounds__(256) gemm_kernel(int M, int N, int K, const fl
   }
 }
 
+// ---------------- skinny FP32 GEMM for N <= 16 (the readouts): C[z] += A[z] * B ----------------
+// Warp per row.  Lane = (k slice kk, column n) with NP = N rounded up to a power of two:
+// lane reads A[m][kk + (32 / NP) t] (coalesced) and B(k, n) from shared memory [K][NP]
+// (consecutive lanes on consecutive words), then the k slices are summed with shuffles.
+constexpr int kSkinnyMaxN = 16, kSkinnyMaxK = 1024, kSkinnyThreads = 256;
+
+template <int NP, bool TransB>
+__global__ void __launch_bounds__(kSkinnyThreads) skinny_kernel(int M, int N, int K, const float *__restrict__ A,
+                                                              int lda, long long sA, const float *__restrict__ B,
+                                                              int ldb, float *__restrict__ C, int ldc, long long sC) {
+  constexpr int KS = 32 / NP;
+  extern __shared__ float bs[]; // [K][NP], zero beyond N
+  A += blockIdx.y * sA;
+  C += blockIdx.y * sC;
+  for (int q = threadIdx.x; q < K * NP; q += blockDim.x) {
+    int k = q / NP, nn = q % NP;
+    bs[q] = nn < N ? (TransB ? B[size_t(nn) * ldb + k] : B[size_t(k) * ldb + nn]) : 0.f;
+  }
+  __syncthreads();
+  int lane = threadIdx.x & 31, n = lane % NP, kk = lane / NP;
+  int warps = gridDim.x * (kSkinnyThreads / 32);
+  for (int m = blockIdx.x * (kSkinnyThreads / 32) + (threadIdx.x >> 5); m < M; m += warps) {
+    const float *a = A + size_t(m) * lda;
+    float s0 = 0.f, s1 = 0.f;
+    int k = kk;
+    for (; k + KS < K; k += 2 * KS) {
+      s0 = fmaf(a[k], bs[k * NP + n], s0);
+      s1 = fmaf(a[k + KS], bs[(k + KS) * NP + n], s1);
+    }
+    if (k < K)
+      s0 = fmaf(a[k], bs[k * NP + n], s0);
+    float s = s0 + s1;
+#pragma unroll
+    for (int off = NP; off < 32; off <<= 1)
+      s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (kk == 0 && n < N)
+      C[size_t(m) * ldc + n] += s;
+  }
+}
+
+template <bool TransB>
+void launch_skinny(cudaStream_t s, int M, int N, int K, int batch, const float *A, int lda, long long sA,
+                   const float *B, int ldb, float *C, int ldc, long long sC) {
+  int np = N <= 1 ? 1 : N <= 2 ? 2 : N <= 4 ? 4 : N <= 8 ? 8 : 16;
+  auto kernel = np == 1   ? skinny_kernel<1, TransB>
+                : np == 2 ? skinny_kernel<2, TransB>
+                : np == 4 ? skinny_kernel<4, TransB>
+                : np == 8 ? skinny_kernel<8, TransB>
+                          : skinny_kernel<16, TransB>;
+  int smem = K * np * 4;
+  if (smem > 48 * 1024)
+    lapis::check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  dim3 grid(std::min((M + kSkinnyThreads / 32 - 1) / (kSkinnyThreads / 32), 296), batch);
+  lapis::launch(kernel, grid, kSkinnyThreads, smem, s, M, N, K, A, lda, sA, B, ldb, C, ldc, sC);
+}
+
 __global__ void species_kernel(lapis::DeviceGeometry g, const int *lookup, int *species) {
   int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= g.n)
@@ -102,8 +158,12 @@ __global__ void embed_kernel(int n, const int *species, const float *embedding, 
 }
 
 // One thread per (node, channel < 512): the 4 scalar groups and the 15 gated components.
+__device__ __forceinline__ float normalized(const float *raw, const float *res, size_t k, float den) {
+  return raw[k] / den + res[k];
+}
+
 __global__ void normalize_gate_kernel(int n, const float *raw, const float *res, const float *rho, float alpha,
-                                      float beta, float cs, float cg, float *pre, float *gate) {
+                                      float beta, float cs, float cg, float *gate) {
   int q = blockIdx.x * blockDim.x + threadIdx.x;
   if (q >= n * 512)
     return;
@@ -111,27 +171,23 @@ __global__ void normalize_gate_kernel(int n, const float *raw, const float *res,
   float den = alpha + beta * rho[i];
   float u[4];
 #pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    size_t k = size_t(i) * 2048 + g * 512 + c;
-    u[g] = raw[k] / den + res[k];
-    pre[k] = u[g];
-  }
+  for (int g = 0; g < 4; ++g)
+    u[g] = normalized(raw, res, size_t(i) * 2048 + g * 512 + c, den);
   gate[q] = cs * u[0] * sigm(u[0]);
 #pragma unroll
   for (int l = 1; l <= 3; ++l) {
     float gl = sigm(u[l]);
     for (int m = l * l; m < (l + 1) * (l + 1); ++m) {
-      size_t k = size_t(n) * 2048 + (size_t(m - 1) * n + i) * 512 + c;
-      float p = raw[k] / den + res[k];
-      pre[k] = p;
+      float p = normalized(raw, res, size_t(n) * 2048 + (size_t(m - 1) * n + i) * 512 + c, den);
       gate[(size_t(m) * n + i) * 512 + c] = p * cg * gl;
     }
   }
 }
 
 // CTA per node, thread per channel: gate VJP into pre_grad, normalisation VJP into raw_grad
-// and density_grad (one fixed-order block reduction per node).
-__global__ void __launch_bounds__(512) gate_norm_backward_kernel(int n, const float *pre, const float *raw,
+// and density_grad (one fixed-order block reduction per node).  pre is recomputed from raw and
+// res; pg may alias res (each element is read before the same thread writes it).
+__global__ void __launch_bounds__(512) gate_norm_backward_kernel(int n, const float *res, const float *raw,
                                                                  const float *rho, const float *gg, float alpha,
                                                                  float beta, float cs, float cgt, float *pg,
                                                                  float *rg, float *rho_grad) {
@@ -141,27 +197,27 @@ __global__ void __launch_bounds__(512) gate_norm_backward_kernel(int n, const fl
   {
     int c = t;
     size_t k0 = size_t(i) * 2048 + c;
-    float u = pre[k0], sg = sigm(u);
+    float u = normalized(raw, res, k0, den), sg = sigm(u);
     float g0 = gg[size_t(i) * 512 + c] * cs * sg * (1.f + u * (1.f - sg));
+    s -= g0 * raw[k0] * beta / (den * den);
     pg[k0] = g0;
     rg[k0] = g0 / den;
-    s -= g0 * raw[k0] * beta / (den * den);
 #pragma unroll
     for (int l = 1; l <= 3; ++l) {
       size_t gi = size_t(i) * 2048 + l * 512 + c;
-      float gl = sigm(pre[gi]), dg = 0.f;
+      float gl = sigm(normalized(raw, res, gi, den)), dg = 0.f;
       for (int m = l * l; m < (l + 1) * (l + 1); ++m) {
         size_t src = size_t(n) * 2048 + (size_t(m - 1) * n + i) * 512 + c;
         float go = gg[(size_t(m) * n + i) * 512 + c];
-        float v = go * cgt * gl;
+        float v = go * cgt * gl, r = raw[src];
+        dg += go * (r / den + res[src]) * cgt * gl * (1.f - gl);
+        s -= v * r * beta / (den * den);
         pg[src] = v;
         rg[src] = v / den;
-        s -= v * raw[src] * beta / (den * den);
-        dg += go * pre[src] * cgt * gl * (1.f - gl);
       }
+      s -= dg * raw[gi] * beta / (den * den);
       pg[gi] = dg;
       rg[gi] = dg / den;
-      s -= dg * raw[gi] * beta / (den * den);
     }
   }
 #pragma unroll
@@ -458,6 +514,12 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
                 t.fwd_lo, y + size_t(p.out_offset) * ny, p.out_mul, (long long)ny * p.out_mul, !store, status);
         continue;
       }
+      if (p.out_mul <= kSkinnyMaxN && p.in_mul <= kSkinnyMaxK) {
+        launch_skinny<false>(s, n, p.out_mul, p.in_mul, p.dim, x + size_t(p.in_offset) * nx, p.in_mul,
+                             (long long)nx * p.in_mul, w, p.out_mul, y + size_t(p.out_offset) * ny, p.out_mul,
+                             (long long)ny * p.out_mul);
+        continue;
+      }
       dim3 grid((p.out_mul + BN - 1) / BN, (n + BM - 1) / BM, p.dim);
       lapis::launch(gemm_kernel<false>, grid, 256, 0, s, n, p.out_mul, p.in_mul, x + size_t(p.in_offset) * nx,
                     p.in_mul, (long long)nx * p.in_mul, w, p.out_mul, y + size_t(p.out_offset) * ny, p.out_mul,
@@ -466,6 +528,12 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
       if (tc && t.bwd_hi) {
         tc_gemm(s, n, p.in_mul, p.out_mul, p.dim, x + size_t(p.out_offset) * nx, (long long)nx * p.out_mul,
                 t.bwd_hi, t.bwd_lo, y + size_t(p.in_offset) * ny, p.in_mul, (long long)ny * p.in_mul, !store, status);
+        continue;
+      }
+      if (p.in_mul <= kSkinnyMaxN && p.out_mul <= kSkinnyMaxK) {
+        launch_skinny<true>(s, n, p.in_mul, p.out_mul, p.dim, x + size_t(p.out_offset) * nx, p.out_mul,
+                            (long long)nx * p.out_mul, w, p.out_mul, y + size_t(p.in_offset) * ny, p.in_mul,
+                            (long long)ny * p.in_mul);
         continue;
       }
       dim3 grid((p.in_mul + BN - 1) / BN, (n + BM - 1) / BM, p.dim);
@@ -477,16 +545,16 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
 }
 
 void launch_normalize_gate(cudaStream_t s, int n, const float *raw, const float *res, const float *density,
-                           float alpha, float beta, float scalar_scale, float gate_scale, float *pre, float *gate) {
+                           float alpha, float beta, float scalar_scale, float gate_scale, float *gate) {
   if (n)
     lapis::launch(normalize_gate_kernel, blocks_for(size_t(n) * 512, 256), 256, 0, s, n, raw, res, density, alpha, beta,
-                                                                           scalar_scale, gate_scale, pre, gate);
+                  scalar_scale, gate_scale, gate);
 }
-void launch_gate_norm_backward(cudaStream_t s, int n, const float *pre, const float *raw, const float *density,
+void launch_gate_norm_backward(cudaStream_t s, int n, const float *res, const float *raw, const float *density,
                                const float *gate_grad, float alpha, float beta, float scalar_scale, float gate_scale,
                                float *pre_grad, float *raw_grad, float *density_grad) {
   if (n)
-    lapis::launch(gate_norm_backward_kernel, n, 512, 0, s, n, pre, raw, density, gate_grad, alpha, beta, scalar_scale,
+    lapis::launch(gate_norm_backward_kernel, n, 512, 0, s, n, res, raw, density, gate_grad, alpha, beta, scalar_scale,
                                                 gate_scale, pre_grad, raw_grad, density_grad);
 }
 size_t product_smem(int count, bool backward) {
