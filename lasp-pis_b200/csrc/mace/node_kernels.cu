@@ -157,81 +157,130 @@ __global__ void embed_kernel(int n, const int *species, const float *embedding, 
   x[q] = embedding[species[i] * 512 + c];
 }
 
-// One thread per (node, channel < 512): the 4 scalar groups and the 15 gated components.
-__device__ __forceinline__ float normalized(const float *raw, const float *res, size_t k, float den) {
-  return raw[k] / den + res[k];
+// One thread per (node, 4 channels of 512): the 4 scalar groups and the 15 gated components,
+// float4 accesses; every element follows the same FP32 expressions as a scalar pass.
+__device__ __forceinline__ void ld4(const float *p, size_t k, float (&v)[4]) {
+  float4 x = *reinterpret_cast<const float4 *>(p + k);
+  v[0] = x.x, v[1] = x.y, v[2] = x.z, v[3] = x.w;
+}
+__device__ __forceinline__ void st4(float *p, size_t k, const float (&v)[4]) {
+  *reinterpret_cast<float4 *>(p + k) = make_float4(v[0], v[1], v[2], v[3]);
+}
+// pre = raw / den + res for the 4 channels at k.
+__device__ __forceinline__ void normalized4(const float *raw, const float *res, size_t k, float den, float (&u)[4]) {
+  float r[4], q[4];
+  ld4(raw, k, r);
+  ld4(res, k, q);
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    u[j] = r[j] / den + q[j];
 }
 
 __global__ void normalize_gate_kernel(int n, const float *raw, const float *res, const float *rho, float alpha,
                                       float beta, float cs, float cg, float *gate) {
   int q = blockIdx.x * blockDim.x + threadIdx.x;
-  if (q >= n * 512)
+  if (q >= n * 128)
     return;
-  int i = q / 512, c = q % 512;
+  int i = q >> 7, c = (q & 127) * 4;
   float den = alpha + beta * rho[i];
-  float u[4];
+  float u[4][4], o[4];
 #pragma unroll
   for (int g = 0; g < 4; ++g)
-    u[g] = normalized(raw, res, size_t(i) * 2048 + g * 512 + c, den);
-  gate[q] = cs * u[0] * sigm(u[0]);
+    normalized4(raw, res, size_t(i) * 2048 + g * 512 + c, den, u[g]);
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    o[j] = cs * u[0][j] * sigm(u[0][j]);
+  st4(gate, size_t(i) * 512 + c, o);
 #pragma unroll
   for (int l = 1; l <= 3; ++l) {
-    float gl = sigm(u[l]);
+    float gl[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      gl[j] = sigm(u[l][j]);
+#pragma unroll
     for (int m = l * l; m < (l + 1) * (l + 1); ++m) {
-      float p = normalized(raw, res, size_t(n) * 2048 + (size_t(m - 1) * n + i) * 512 + c, den);
-      gate[(size_t(m) * n + i) * 512 + c] = p * cg * gl;
+      float p[4];
+      normalized4(raw, res, size_t(n) * 2048 + (size_t(m - 1) * n + i) * 512 + c, den, p);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        o[j] = p[j] * cg * gl[j];
+      st4(gate, (size_t(m) * n + i) * 512 + c, o);
     }
   }
 }
 
-// CTA per node, thread per channel: gate VJP into pre_grad, normalisation VJP into raw_grad
-// and density_grad (one fixed-order block reduction per node).  pre is recomputed from raw and
-// res; pg may alias res (each element is read before the same thread writes it).
-__global__ void __launch_bounds__(512) gate_norm_backward_kernel(int n, const float *res, const float *raw,
+// Four nodes per CTA, thread per 4 channels: gate VJP into pre_grad, normalisation VJP into
+// raw_grad and density_grad (one fixed-order reduction per node).  pre is recomputed from raw
+// and res; pg may alias res (each element is read before the same thread writes it).
+__global__ void __launch_bounds__(512, 2) gate_norm_backward_kernel(int n, const float *res, const float *raw,
                                                                  const float *rho, const float *gg, float alpha,
                                                                  float beta, float cs, float cgt, float *pg,
                                                                  float *rg, float *rho_grad) {
-  __shared__ float red[16];
-  int i = blockIdx.x, t = threadIdx.x;
-  float den = alpha + beta * rho[i], s = 0.f;
-  {
-    int c = t;
+  __shared__ float red[4][4];
+  int t = threadIdx.x, slot = t >> 7, c = (t & 127) * 4, i = blockIdx.x * 4 + slot;
+  float s = 0.f;
+  if (i < n) {
+    float den = alpha + beta * rho[i];
     size_t k0 = size_t(i) * 2048 + c;
-    float u = normalized(raw, res, k0, den), sg = sigm(u);
-    float g0 = gg[size_t(i) * 512 + c] * cs * sg * (1.f + u * (1.f - sg));
-    s -= g0 * raw[k0] * beta / (den * den);
-    pg[k0] = g0;
-    rg[k0] = g0 / den;
+    float r[4], u[4], g[4], o[4], ro[4];
+    ld4(raw, k0, r);
+    normalized4(raw, res, k0, den, u);
+    ld4(gg, size_t(i) * 512 + c, g);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float sg = sigm(u[j]);
+      float g0 = g[j] * cs * sg * (1.f + u[j] * (1.f - sg));
+      s -= g0 * r[j] * beta / (den * den);
+      o[j] = g0;
+      ro[j] = g0 / den;
+    }
+    st4(pg, k0, o);
+    st4(rg, k0, ro);
 #pragma unroll
     for (int l = 1; l <= 3; ++l) {
       size_t gi = size_t(i) * 2048 + l * 512 + c;
-      float gl = sigm(normalized(raw, res, gi, den)), dg = 0.f;
+      float gl[4], dg[4] = {0.f, 0.f, 0.f, 0.f}, rgi[4];
+      normalized4(raw, res, gi, den, gl);
+      ld4(raw, gi, rgi);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        gl[j] = sigm(gl[j]);
+#pragma unroll
       for (int m = l * l; m < (l + 1) * (l + 1); ++m) {
         size_t src = size_t(n) * 2048 + (size_t(m - 1) * n + i) * 512 + c;
-        float go = gg[(size_t(m) * n + i) * 512 + c];
-        float v = go * cgt * gl, r = raw[src];
-        dg += go * (r / den + res[src]) * cgt * gl * (1.f - gl);
-        s -= v * r * beta / (den * den);
-        pg[src] = v;
-        rg[src] = v / den;
+        float go[4], rs[4], qs[4];
+        ld4(gg, (size_t(m) * n + i) * 512 + c, go);
+        ld4(raw, src, rs);
+        ld4(res, src, qs);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float v = go[j] * cgt * gl[j];
+          dg[j] += go[j] * (rs[j] / den + qs[j]) * cgt * gl[j] * (1.f - gl[j]);
+          s -= v * rs[j] * beta / (den * den);
+          o[j] = v;
+          ro[j] = v / den;
+        }
+        st4(pg, src, o);
+        st4(rg, src, ro);
       }
-      s -= dg * raw[gi] * beta / (den * den);
-      pg[gi] = dg;
-      rg[gi] = dg / den;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        s -= dg[j] * rgi[j] * beta / (den * den);
+        o[j] = dg[j];
+        ro[j] = dg[j] / den;
+      }
+      st4(pg, gi, o);
+      st4(rg, gi, ro);
     }
   }
 #pragma unroll
   for (int step = 16; step; step >>= 1)
     s += __shfl_xor_sync(0xffffffffu, s, step);
   if ((t & 31) == 0)
-    red[t >> 5] = s;
+    red[slot][(t >> 5) & 3] = s;
   __syncthreads();
-  if (t == 0) {
-    float total = 0.f;
-    for (int w = 0; w < 16; ++w)
-      total += red[w];
-    rho_grad[i] = total;
-  }
+  if ((t & 127) == 0 && i < n)
+    rho_grad[i] = (red[slot][0] + red[slot][1]) + (red[slot][2] + red[slot][3]);
 }
 
 // Symmetric contraction: y[out][c] = sum_t coef[t][c] x[a][c] x[b][c] x[c'][c] (degree <= 3).
@@ -547,15 +596,15 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
 void launch_normalize_gate(cudaStream_t s, int n, const float *raw, const float *res, const float *density,
                            float alpha, float beta, float scalar_scale, float gate_scale, float *gate) {
   if (n)
-    lapis::launch(normalize_gate_kernel, blocks_for(size_t(n) * 512, 256), 256, 0, s, n, raw, res, density, alpha, beta,
+    lapis::launch(normalize_gate_kernel, blocks_for(size_t(n) * 128, 256), 256, 0, s, n, raw, res, density, alpha, beta,
                   scalar_scale, gate_scale, gate);
 }
 void launch_gate_norm_backward(cudaStream_t s, int n, const float *res, const float *raw, const float *density,
                                const float *gate_grad, float alpha, float beta, float scalar_scale, float gate_scale,
                                float *pre_grad, float *raw_grad, float *density_grad) {
   if (n)
-    lapis::launch(gate_norm_backward_kernel, n, 512, 0, s, n, res, raw, density, gate_grad, alpha, beta, scalar_scale,
-                                                gate_scale, pre_grad, raw_grad, density_grad);
+    lapis::launch(gate_norm_backward_kernel, (n + 3) / 4, 512, 0, s, n, res, raw, density, gate_grad, alpha, beta,
+                  scalar_scale, gate_scale, pre_grad, raw_grad, density_grad);
 }
 size_t product_smem(int count, bool backward) {
   return (size_t(count) * 32 + ((count + 3) & ~3)) * 4 + size_t(kProdWarps) * (backward ? 2 : 1) * kProdV * 32 * 4;
