@@ -154,6 +154,18 @@ void linear(cudaStream_t, int n, const Linear &, const float *x, float *y, bool 
 bool tc_gemm_supported(int N, int K);
 void tc_gemm(cudaStream_t, int M, int N, int K, int batch, const float *A, long long strideA, const float *Bhi,
              const float *Blo, float *C, int ldc, long long strideC, bool accumulate, int *status);
+// A group of independent tensor-core GEMMs in one persistent launch (per 16 problems).
+struct GemmSpec {
+  int M, N, K, batch;
+  const float *A;
+  long long strideA;
+  const float *Bhi, *Blo;
+  float *C;
+  int ldc;
+  long long strideC;
+  bool accumulate;
+};
+void tc_gemm_group(cudaStream_t, const GemmSpec *specs, int count, int *status);
 // Host split of a weight matrix into tf32-rounded hi and the fp32 remainder lo.
 void split_tf32(const float *w, size_t count, float *hi, float *lo);
 // Use the tensor-core path in linear() (default true; MACE_SIMT_LINEARS=1 disables).

@@ -82,59 +82,84 @@ __global__ void __launch_bounds__(256) gemm_kernel(int M, int N, int K, const fl
 }
 
 // ---------------- skinny FP32 GEMM for N <= 16 (the readouts): C[z] += A[z] * B ----------------
-// Warp per row.  Lane = (k slice kk, column n) with NP = N rounded up to a power of two:
-// lane reads A[m][kk + (32 / NP) t] (coalesced) and B(k, n) from shared memory [K][NP]
-// (consecutive lanes on consecutive words), then the k slices are summed with shuffles.
+// Warp per row.  The row of A is read in coalesced float4 chunks of 128 (lane = 4 columns),
+// B sits in shared memory transposed and zero-padded ([NP][KP], NP = N rounded up to a power
+// of two), so each lane forms NP partial dot products; a halving exchange then leaves lane l
+// with the row total of column l (NP - 1 + 5 - log2(NP) shuffles).  Needs K, lda multiples of
+// 4 and a 16-byte aligned A.
 constexpr int kSkinnyMaxN = 16, kSkinnyMaxK = 1024, kSkinnyThreads = 256;
+
+template <int NP>
+__device__ __forceinline__ float lane_totals(float (&p)[NP], int lane) {
+#pragma unroll
+  for (int h = NP / 2; h >= 1; h /= 2) {
+    bool up = lane & h;
+#pragma unroll
+    for (int i = 0; i < h; ++i) {
+      float send = up ? p[i] : p[i + h];
+      p[i] = (up ? p[i + h] : p[i]) + __shfl_xor_sync(0xffffffffu, send, h);
+    }
+  }
+  float v = p[0];
+#pragma unroll
+  for (int off = NP; off < 32; off <<= 1)
+    v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v; // column lane & (NP - 1)
+}
 
 template <int NP, bool TransB>
 __global__ void __launch_bounds__(kSkinnyThreads) skinny_kernel(int M, int N, int K, const float *__restrict__ A,
                                                               int lda, long long sA, const float *__restrict__ B,
                                                               int ldb, float *__restrict__ C, int ldc, long long sC) {
-  constexpr int KS = 32 / NP;
-  extern __shared__ float bs[]; // [K][NP], zero beyond N
+  extern __shared__ __align__(16) float bs[]; // [NP][KP], zero beyond N and K
+  int KP = (K + 127) & ~127;
   A += blockIdx.y * sA;
   C += blockIdx.y * sC;
-  for (int q = threadIdx.x; q < K * NP; q += blockDim.x) {
-    int k = q / NP, nn = q % NP;
-    bs[q] = nn < N ? (TransB ? B[size_t(nn) * ldb + k] : B[size_t(k) * ldb + nn]) : 0.f;
+  for (int q = threadIdx.x; q < NP * KP; q += blockDim.x) {
+    int nn = q / KP, k = q - nn * KP;
+    bs[q] = nn < N && k < K ? (TransB ? B[size_t(nn) * ldb + k] : B[size_t(k) * ldb + nn]) : 0.f;
   }
   __syncthreads();
-  int lane = threadIdx.x & 31, n = lane % NP, kk = lane / NP;
+  int lane = threadIdx.x & 31;
   int warps = gridDim.x * (kSkinnyThreads / 32);
   for (int m = blockIdx.x * (kSkinnyThreads / 32) + (threadIdx.x >> 5); m < M; m += warps) {
     const float *a = A + size_t(m) * lda;
-    float s0 = 0.f, s1 = 0.f;
-    int k = kk;
-    for (; k + KS < K; k += 2 * KS) {
-      s0 = fmaf(a[k], bs[k * NP + n], s0);
-      s1 = fmaf(a[k + KS], bs[(k + KS) * NP + n], s1);
-    }
-    if (k < K)
-      s0 = fmaf(a[k], bs[k * NP + n], s0);
-    float s = s0 + s1;
+    float p[NP];
 #pragma unroll
-    for (int off = NP; off < 32; off <<= 1)
-      s += __shfl_xor_sync(0xffffffffu, s, off);
-    if (kk == 0 && n < N)
-      C[size_t(m) * ldc + n] += s;
+    for (int n = 0; n < NP; ++n)
+      p[n] = 0.f;
+    for (int k = 4 * lane; k < KP; k += 128) {
+      float4 av = k < K ? *reinterpret_cast<const float4 *>(a + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int n = 0; n < NP; ++n) {
+        float4 bv = *reinterpret_cast<const float4 *>(bs + n * KP + k);
+        p[n] = fmaf(av.x, bv.x, fmaf(av.y, bv.y, fmaf(av.z, bv.z, fmaf(av.w, bv.w, p[n]))));
+      }
+    }
+    float v = lane_totals<NP>(p, lane);
+    if (lane < NP && lane < N)
+      C[size_t(m) * ldc + lane] += v;
   }
 }
 
+// False when the shape or alignment does not suit skinny_kernel.
 template <bool TransB>
-void launch_skinny(cudaStream_t s, int M, int N, int K, int batch, const float *A, int lda, long long sA,
+bool launch_skinny(cudaStream_t s, int M, int N, int K, int batch, const float *A, int lda, long long sA,
                    const float *B, int ldb, float *C, int ldc, long long sC) {
+  if (N > kSkinnyMaxN || K > kSkinnyMaxK || K % 4 || lda % 4 || sA % 4 || reinterpret_cast<uintptr_t>(A) % 16)
+    return false;
   int np = N <= 1 ? 1 : N <= 2 ? 2 : N <= 4 ? 4 : N <= 8 ? 8 : 16;
   auto kernel = np == 1   ? skinny_kernel<1, TransB>
                 : np == 2 ? skinny_kernel<2, TransB>
                 : np == 4 ? skinny_kernel<4, TransB>
                 : np == 8 ? skinny_kernel<8, TransB>
                           : skinny_kernel<16, TransB>;
-  int smem = K * np * 4;
+  int smem = np * ((K + 127) & ~127) * 4;
   if (smem > 48 * 1024)
     lapis::check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   dim3 grid(std::min((M + kSkinnyThreads / 32 - 1) / (kSkinnyThreads / 32), 296), batch);
   lapis::launch(kernel, grid, kSkinnyThreads, smem, s, M, N, K, A, lda, sA, B, ldb, C, ldc, sC);
+  return true;
 }
 
 __global__ void species_kernel(lapis::DeviceGeometry g, const int *lookup, int *species) {
@@ -553,38 +578,58 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
     store = store && (backward ? t.bwd_hi : t.fwd_hi);
   if (!add && !store)
     lapis::check(cudaMemsetAsync(y, 0, size_t(ny) * (backward ? l.input : l.output) * 4, s));
+  // Tensor-core paths go out as grouped launches of consecutive paths whose output blocks are
+  // disjoint: paths that add into the same block stay in separate launches, in path order, so
+  // every element sums its contributions in the same order on every call.
+  std::vector<GemmSpec> group;
+  std::vector<std::pair<int, int>> ranges; // output blocks of the current group (component units)
+  for (size_t q = 0; q < l.paths.size() && tc; ++q) {
+    const auto &p = l.paths[q];
+    const TCWeights &t = l.tc[q];
+    if (!(backward ? t.bwd_hi : t.fwd_hi))
+      continue;
+    int o0 = backward ? p.in_offset : p.out_offset, o1 = o0 + (backward ? p.in_mul : p.out_mul) * p.dim;
+    for (auto &r : ranges)
+      if (o0 < r.second && r.first < o1) {
+        tc_gemm_group(s, group.data(), int(group.size()), status);
+        group.clear();
+        ranges.clear();
+        break;
+      }
+    ranges.push_back({o0, o1});
+    if (!backward)
+      group.push_back(GemmSpec{n, p.out_mul, p.in_mul, p.dim, x + size_t(p.in_offset) * nx, (long long)nx * p.in_mul,
+                               t.fwd_hi, t.fwd_lo, y + size_t(p.out_offset) * ny, p.out_mul,
+                               (long long)ny * p.out_mul, !store});
+    else
+      group.push_back(GemmSpec{n, p.in_mul, p.out_mul, p.dim, x + size_t(p.out_offset) * nx, (long long)nx * p.out_mul,
+                               t.bwd_hi, t.bwd_lo, y + size_t(p.in_offset) * ny, p.in_mul, (long long)ny * p.in_mul,
+                               !store});
+  }
+  if (!group.empty())
+    tc_gemm_group(s, group.data(), int(group.size()), status);
   for (size_t q = 0; q < l.paths.size(); ++q) {
     const auto &p = l.paths[q];
     const float *w = l.weight + p.weight_offset;
     const TCWeights &t = l.tc[q];
     if (!backward) {
-      if (tc && t.fwd_hi) {
-        tc_gemm(s, n, p.out_mul, p.in_mul, p.dim, x + size_t(p.in_offset) * nx, (long long)nx * p.in_mul, t.fwd_hi,
-                t.fwd_lo, y + size_t(p.out_offset) * ny, p.out_mul, (long long)ny * p.out_mul, !store, status);
+      if (tc && t.fwd_hi)
         continue;
-      }
-      if (p.out_mul <= kSkinnyMaxN && p.in_mul <= kSkinnyMaxK) {
-        launch_skinny<false>(s, n, p.out_mul, p.in_mul, p.dim, x + size_t(p.in_offset) * nx, p.in_mul,
-                             (long long)nx * p.in_mul, w, p.out_mul, y + size_t(p.out_offset) * ny, p.out_mul,
-                             (long long)ny * p.out_mul);
+      if (launch_skinny<false>(s, n, p.out_mul, p.in_mul, p.dim, x + size_t(p.in_offset) * nx, p.in_mul,
+                               (long long)nx * p.in_mul, w, p.out_mul, y + size_t(p.out_offset) * ny, p.out_mul,
+                               (long long)ny * p.out_mul))
         continue;
-      }
       dim3 grid((p.out_mul + BN - 1) / BN, (n + BM - 1) / BM, p.dim);
       lapis::launch(gemm_kernel<false>, grid, 256, 0, s, n, p.out_mul, p.in_mul, x + size_t(p.in_offset) * nx,
                     p.in_mul, (long long)nx * p.in_mul, w, p.out_mul, y + size_t(p.out_offset) * ny, p.out_mul,
                     (long long)ny * p.out_mul);
     } else {
-      if (tc && t.bwd_hi) {
-        tc_gemm(s, n, p.in_mul, p.out_mul, p.dim, x + size_t(p.out_offset) * nx, (long long)nx * p.out_mul,
-                t.bwd_hi, t.bwd_lo, y + size_t(p.in_offset) * ny, p.in_mul, (long long)ny * p.in_mul, !store, status);
+      if (tc && t.bwd_hi)
         continue;
-      }
-      if (p.in_mul <= kSkinnyMaxN && p.out_mul <= kSkinnyMaxK) {
-        launch_skinny<true>(s, n, p.in_mul, p.out_mul, p.dim, x + size_t(p.out_offset) * nx, p.out_mul,
-                            (long long)nx * p.out_mul, w, p.out_mul, y + size_t(p.in_offset) * ny, p.in_mul,
-                            (long long)ny * p.in_mul);
+      if (launch_skinny<true>(s, n, p.in_mul, p.out_mul, p.dim, x + size_t(p.out_offset) * nx, p.out_mul,
+                              (long long)nx * p.out_mul, w, p.out_mul, y + size_t(p.in_offset) * ny, p.in_mul,
+                              (long long)ny * p.in_mul))
         continue;
-      }
       dim3 grid((p.in_mul + BN - 1) / BN, (n + BM - 1) / BM, p.dim);
       lapis::launch(gemm_kernel<true>, grid, 256, 0, s, n, p.in_mul, p.out_mul, x + size_t(p.out_offset) * nx,
                     p.out_mul, (long long)nx * p.out_mul, w, p.out_mul, y + size_t(p.in_offset) * ny, p.in_mul,
@@ -698,8 +743,20 @@ extern "C" int mace_debug_gemm(int M, int N, int K, int batch, const float *A, c
       lapis::check(cudaMemcpy(hi, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
       lapis::check(cudaMemcpy(lo, l.data(), l.size() * 4, cudaMemcpyHostToDevice));
       lapis::check(cudaMemset(status, 0, 4));
-      tc_gemm(cudaStream_t(0), M, N, K, batch, A, (long long)M * K, hi, lo, C, N, (long long)M * N, accumulate != 0,
-              status);
+      if (mode == 1) {
+        tc_gemm(cudaStream_t(0), M, N, K, batch, A, (long long)M * K, hi, lo, C, N, (long long)M * N,
+                accumulate != 0, status);
+      } else { // grouped: one problem per batch plane, columns split as [128, N - 128]
+        std::vector<GemmSpec> group;
+        for (int z = 0; z < batch; ++z)
+          for (int n0 = 0; n0 < N; n0 += (n0 ? N : 128)) {
+            int nc = n0 ? N - n0 : std::min(N, 128);
+            group.push_back(GemmSpec{M, nc, K, 1, A + size_t(z) * M * K, (long long)M * K, hi + size_t(n0) * K,
+                                     lo + size_t(n0) * K, C + size_t(z) * M * N + n0, N, (long long)M * N,
+                                     accumulate != 0});
+          }
+        tc_gemm_group(cudaStream_t(0), group.data(), int(group.size()), status);
+      }
     }
     lapis::check(cudaGetLastError());
     lapis::check(cudaDeviceSynchronize());

@@ -50,6 +50,7 @@ static_assert(kSmemBytes + 64 <= 232448, "shared memory budget");
 constexpr int kTmemCols = 4 * kBN; // hi*hi slab buffers 0/1, correction buffers 2/3 (512 columns)
 constexpr int kThreads = 384, kDrainThreads = 256;
 constexpr int kStatusGemmTimeout = 7;
+constexpr int kMaxGemmProblems = 16;
 
 // Instruction descriptor: D fp32, A/B tf32, both K-major, M = 128, N = 128.
 constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(kBN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
@@ -68,10 +69,26 @@ struct TileGrid {
   }
 };
 
+// One launch runs a group of independent GEMMs (the paths of an equivariant linear) over
+// their concatenated tile space, so short problems share one pipeline ramp and tail.
+struct GemmProblem {
+  CUtensorMap a, bhi, blo, c;
+  TileGrid tg;
+  int ktiles, accumulate, tile0; // first tile of this problem in the group
+};
+struct GemmGroup {
+  GemmProblem p[kMaxGemmProblems];
+  int count, tiles;
+  // Problem of group tile t, advancing q (tiles are visited in increasing order).
+  __device__ __forceinline__ const GemmProblem &find(int t, int &q) const {
+    while (q + 1 < count && t >= p[q + 1].tile0)
+      ++q;
+    return p[q];
+  }
+};
+
 __global__ void __launch_bounds__(kThreads, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBhi,
-                   const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmC, TileGrid tg,
-                   int K, int accumulate, int *status) {
+    tc_gemm_kernel(const __grid_constant__ GemmGroup gg, int *status) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char *staging = smem + kStages * kStageBytes;
@@ -81,7 +98,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ volatile int abort_flag;
   __shared__ int mma_done_issued; // whether the final commit to `done` was issued
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int ktiles = K / kBK;
   unsigned full0 = smem_u32(bars), ready0 = full0 + 8 * kStages, empty0 = ready0 + 8 * kStages,
            tfull0 = empty0 + 8 * kStages, tfree0 = tfull0 + 16, cfull0 = tfree0 + 16, cfree0 = cfull0 + 16,
            done = cfree0 + 16;
@@ -116,20 +132,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      int g = 0;
+      int g = 0, q = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < tg.tiles && ok; t += gridDim.x) {
+      for (int t = blockIdx.x; t < gg.tiles && ok; t += gridDim.x) {
+        const GemmProblem &pr = gg.find(t, q);
         int n0, m0, z;
-        tg.coords(t, n0, m0, z);
-        for (int kt = 0; kt < ktiles; ++kt, ++g) {
+        pr.tg.coords(t - pr.tile0, n0, m0, z);
+        for (int kt = 0; kt < pr.ktiles; ++kt, ++g) {
           int s = g % kStages;
           if (g >= kStages && !(ok = mbar_wait(empty0 + 8 * s, ((g / kStages) - 1) & 1, &abort_flag)))
             break;
           unsigned base = smem_u32(smem + s * kStageBytes);
           mbar_expect_tx(full0 + 8 * s, 3 * kTileBytes);
-          tma_load_3d(base, &tmA, kt * kBK, m0, z, full0 + 8 * s);
-          tma_load_2d(base + 2 * kTileBytes, &tmBhi, kt * kBK, n0, full0 + 8 * s);
-          tma_load_2d(base + 3 * kTileBytes, &tmBlo, kt * kBK, n0, full0 + 8 * s);
+          tma_load_3d(base, &pr.a, kt * kBK, m0, z, full0 + 8 * s);
+          tma_load_2d(base + 2 * kTileBytes, &pr.bhi, kt * kBK, n0, full0 + 8 * s);
+          tma_load_2d(base + 3 * kTileBytes, &pr.blo, kt * kBK, n0, full0 + 8 * s);
         }
       }
     }
@@ -137,9 +154,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       bool ok = true;
-      int g = 0, i = 0;
-      for (int t = blockIdx.x; t < tg.tiles && ok; t += gridDim.x, ++i) {
-        int c = i & 1;
+      int g = 0, i = 0, q = 0;
+      for (int t = blockIdx.x; t < gg.tiles && ok; t += gridDim.x, ++i) {
+        int ktiles = gg.find(t, q).ktiles, c = i & 1;
         if (i >= 2 && !(ok = mbar_wait(cfree0 + 8 * c, ((i >> 1) - 1) & 1, &abort_flag)))
           break;
         uint32_t corr = tmem + uint32_t((2 + c) * kBN);
@@ -170,10 +187,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < 4) {
     // ---------------- A split: hi in place, lo beside it ----------------
-    int t = threadIdx.x - 64, g = 0;
+    int t = threadIdx.x - 64, g = 0, q = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < tg.tiles && ok; tile += gridDim.x)
-      for (int kt = 0; kt < ktiles; ++kt, ++g) {
+    for (int tile = blockIdx.x; tile < gg.tiles && ok; tile += gridDim.x)
+      for (int kt = 0, ktiles = gg.find(tile, q).ktiles; kt < ktiles; ++kt, ++g) {
         int s = g % kStages;
         ok = mbar_wait(full0 + 8 * s, (g / kStages) & 1, &abort_flag);
         if (!__all_sync(0xffffffffu, ok)) {
@@ -199,10 +216,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t lane_addr = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(col0);
     unsigned char *box = staging + (warp - 4) * kBoxBytes; // this warp's staging box
     bool ok = true;
-    int g = 0, i = 0;
-    for (int t = blockIdx.x; t < tg.tiles && ok; t += gridDim.x, ++i) {
-      int n0, m0, z;
-      tg.coords(t, n0, m0, z);
+    int g = 0, i = 0, q = 0;
+    for (int t = blockIdx.x; t < gg.tiles && ok; t += gridDim.x, ++i) {
+      const GemmProblem &pr = gg.find(t, q);
+      int n0, m0, z, ktiles = pr.ktiles;
+      pr.tg.coords(t - pr.tile0, n0, m0, z);
       float acc[64];
 #pragma unroll
       for (int c = 0; c < 64; ++c)
@@ -267,10 +285,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) {
           int x = n0 + col0 + 32 * j, y = m0 + 32 * quarter;
-          if (accumulate)
-            tma_add_3d(&tmC, smem_u32(box), x, y, z);
+          if (pr.accumulate)
+            tma_add_3d(&pr.c, smem_u32(box), x, y, z);
           else
-            tma_store_3d(&tmC, smem_u32(box), x, y, z);
+            tma_store_3d(&pr.c, smem_u32(box), x, y, z);
           bulk_commit();
         }
       }
@@ -353,20 +371,15 @@ CUtensorMap tc_map_2d(const float *base, int cols, long long rows, int box_cols,
 
 bool tc_gemm_supported(int N, int K) { return N % kBN == 0 && K % kBK == 0 && K >= kBK; }
 
-// C[z] (+)= A[z] * B  with B = Bhi + Blo given K-major ([N][K]); batch z = 0..batch-1.
-void tc_gemm(cudaStream_t s, int M, int N, int K, int batch, const float *A, long long strideA, const float *Bhi,
-             const float *Blo, float *C, int ldc, long long strideC, bool accumulate, int *status) {
-  if (!M || !batch)
-    return;
-  if (!tc_gemm_supported(N, K))
+namespace {
+void check_problem(const GemmSpec &g) {
+  if (!tc_gemm_supported(g.N, g.K))
     throw lapis::Error("tensor-core GEMM shape unsupported");
-  if ((reinterpret_cast<uintptr_t>(C) & 15) || ldc % 4 || (batch > 1 && strideC % 4))
+  if ((reinterpret_cast<uintptr_t>(g.C) & 15) || g.ldc % 4 || (g.batch > 1 && g.strideC % 4))
     throw lapis::Error("tensor-core GEMM output is not 16-byte aligned");
-  // A as [batch][M][K] (always a rank-3 map: the kernel issues 3D loads); B as [N][K].
-  CUtensorMap ma = make_map(A, K, M, 3, batch, batch > 1 ? strideA : (long long)M * K);
-  CUtensorMap mh = make_map(Bhi, K, N, 2, 1, 0), ml = make_map(Blo, K, N, 2, 1, 0);
-  // C as [batch][M][ldc], written in 32 x 32 boxes over its first N columns.
-  CUtensorMap mc = make_map(C, N, M, 3, batch, batch > 1 ? strideC : (long long)M * ldc, ldc, 32);
+}
+
+void launch_group(cudaStream_t s, const GemmSpec *specs, int count, int *status) {
   static thread_local int configured_device = -1, sms = 148;
   int device = 0;
   lapis::check(cudaGetDevice(&device));
@@ -375,12 +388,51 @@ void tc_gemm(cudaStream_t s, int M, int N, int K, int batch, const float *A, lon
     lapis::check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
     configured_device = device;
   }
-  TileGrid tg{N / kBN, (M + kBM - 1) / kBM, 0};
-  long long tiles = (long long)tg.nN * tg.nM * batch;
-  if (tiles > INT_MAX)
-    throw lapis::Error("tensor-core GEMM has too many tiles");
-  tg.tiles = int(tiles);
+  GemmGroup gg{};
+  long long tiles = 0;
+  int n = 0;
+  for (int k = 0; k < count; ++k) {
+    const GemmSpec &g = specs[k];
+    if (!g.M || !g.batch)
+      continue;
+    GemmProblem &p = gg.p[n++];
+    // A as [batch][M][K] (always a rank-3 map: the kernel issues 3D loads); B as [N][K].
+    p.a = make_map(g.A, g.K, g.M, 3, g.batch, g.batch > 1 ? g.strideA : (long long)g.M * g.K);
+    p.bhi = make_map(g.Bhi, g.K, g.N, 2, 1, 0);
+    p.blo = make_map(g.Blo, g.K, g.N, 2, 1, 0);
+    // C as [batch][M][ldc], written in 32 x 32 boxes over its first N columns.
+    p.c = make_map(g.C, g.N, g.M, 3, g.batch, g.batch > 1 ? g.strideC : (long long)g.M * g.ldc, g.ldc, 32);
+    p.tg = TileGrid{g.N / kBN, (g.M + kBM - 1) / kBM, 0};
+    long long pt = (long long)p.tg.nN * p.tg.nM * g.batch;
+    p.tg.tiles = int(std::min<long long>(pt, INT_MAX));
+    p.ktiles = g.K / kBK;
+    p.accumulate = g.accumulate;
+    p.tile0 = int(std::min<long long>(tiles, INT_MAX));
+    tiles += pt;
+    if (tiles > INT_MAX)
+      throw lapis::Error("tensor-core GEMM has too many tiles");
+  }
+  if (!n)
+    return;
+  gg.count = n;
+  gg.tiles = int(tiles);
   int grid = int(std::min<long long>(tiles, sms));
-  lapis::launch(tc_gemm_kernel, grid, kThreads, kSmemBytes, s, ma, mh, ml, mc, tg, K, int(accumulate), status);
+  lapis::launch(tc_gemm_kernel, grid, kThreads, kSmemBytes, s, gg, status);
+}
+} // namespace
+
+// C[z] (+)= A[z] * B  with B = Bhi + Blo given K-major ([N][K]); batch z = 0..batch-1.
+void tc_gemm(cudaStream_t s, int M, int N, int K, int batch, const float *A, long long strideA, const float *Bhi,
+             const float *Blo, float *C, int ldc, long long strideC, bool accumulate, int *status) {
+  GemmSpec g{M, N, K, batch, A, strideA, Bhi, Blo, C, ldc, strideC, accumulate};
+  tc_gemm_group(s, &g, 1, status);
+}
+
+void tc_gemm_group(cudaStream_t s, const GemmSpec *specs, int count, int *status) {
+  for (int k = 0; k < count; ++k)
+    if (specs[k].M && specs[k].batch)
+      check_problem(specs[k]);
+  for (int k = 0; k < count; k += kMaxGemmProblems)
+    launch_group(s, specs + k, std::min(count - k, kMaxGemmProblems), status);
 }
 } // namespace mace

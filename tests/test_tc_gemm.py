@@ -11,11 +11,12 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 SHAPES = [(1000, 128, 128, 1), (300, 256, 2048, 3), (10000, 512, 512, 1), (130, 2048, 128, 2), (77, 128, 32, 7),
-          (5000, 1280, 64, 1), (3000, 512, 64, 2)]  # the last two: edge-projection shapes (K = 64)
+          (5000, 1280, 64, 1), (3000, 512, 64, 2),  # edge-projection shapes (K = 64)
+          (200, 384, 96, 9)]  # grouped mode: 18 problems, two launches
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
-@pytest.mark.parametrize("mode", [0, 1], ids=["simt", "tcgen05"])
+@pytest.mark.parametrize("mode", [0, 1, 2], ids=["simt", "tcgen05", "tcgen05-grouped"])
 def test_gemm_matches_fp64(library, shape, mode):
     import torch
     lib = ct.CDLL(str(library))
