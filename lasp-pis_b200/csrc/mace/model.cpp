@@ -213,24 +213,6 @@ void ModelData::load(const std::string &path) {
       }
       l.tc.push_back(t);
     }
-    // Do the paths' output (forward) / input (backward) blocks tile the whole vector once?
-    auto tiles = [&](bool fwd) {
-      std::vector<std::pair<int64_t, int64_t>> iv;
-      for (const auto &p : l.paths) {
-        int64_t o = fwd ? p.out_offset : p.in_offset, m = fwd ? p.out_mul : p.in_mul;
-        iv.emplace_back(o, o + m * p.dim);
-      }
-      std::sort(iv.begin(), iv.end());
-      int64_t at = 0;
-      for (auto &v : iv) {
-        if (v.first != at)
-          return false;
-        at = v.second;
-      }
-      return at == (fwd ? output : input);
-    };
-    l.fwd_tiles = tiles(true);
-    l.bwd_tiles = tiles(false);
     return l;
   };
   auto get_radial = [&](const std::string &key, int depth, int outputs) {

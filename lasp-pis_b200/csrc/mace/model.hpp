@@ -27,9 +27,6 @@ struct Linear {
   std::vector<LinearPath> paths;
   std::vector<TCWeights> tc;     // per path
   const float *weight = nullptr; // device, [in_mul][out_mul] per path
-  // The paths' output blocks (forward) / input blocks (backward) are disjoint and cover the
-  // whole output, so a non-accumulating call can store each path's result directly.
-  bool fwd_tiles = false, bwd_tiles = false;
 };
 // Radial MLP weights, transposed at load for coalesced per-unit access.
 struct Radial {
@@ -154,7 +151,9 @@ void linear(cudaStream_t, int n, const Linear &, const float *x, float *y, bool 
 bool tc_gemm_supported(int N, int K);
 void tc_gemm(cudaStream_t, int M, int N, int K, int batch, const float *A, long long strideA, const float *Bhi,
              const float *Blo, float *C, int ldc, long long strideC, bool accumulate, int *status);
-// A group of independent tensor-core GEMMs in one persistent launch (per 16 problems).
+// A group of independent tensor-core GEMMs in one persistent launch (per 16 problems).  A
+// spec with `join` set is a further K segment of the previous spec's problem (same C, M, N,
+// batch and mode; its own A, K and B): C (+)= sum over the segments of A_s B_s.
 struct GemmSpec {
   int M, N, K, batch;
   const float *A;
@@ -164,6 +163,7 @@ struct GemmSpec {
   int ldc;
   long long strideC;
   bool accumulate;
+  bool join = false;
 };
 void tc_gemm_group(cudaStream_t, const GemmSpec *specs, int count, int *status);
 // Host split of a weight matrix into tf32-rounded hi and the fp32 remainder lo.

@@ -571,50 +571,77 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
   if (!ny)
     ny = n;
   bool tc = tensor_core_linears() && status;
-  // Direct stores (no zero fill, no read-modify-write) when every path runs on the tensor
-  // cores and the paths' blocks tile the output.
-  bool store = !add && tc && (backward ? l.bwd_tiles : l.fwd_tiles);
-  for (const auto &t : l.tc)
-    store = store && (backward ? t.bwd_hi : t.fwd_hi);
-  if (!add && !store)
-    lapis::check(cudaMemsetAsync(y, 0, size_t(ny) * (backward ? l.input : l.output) * 4, s));
-  // Tensor-core paths go out as grouped launches of consecutive paths whose output blocks are
-  // disjoint: paths that add into the same block stay in separate launches, in path order, so
-  // every element sums its contributions in the same order on every call.
-  std::vector<GemmSpec> group;
-  std::vector<std::pair<int, int>> ranges; // output blocks of the current group (component units)
-  for (size_t q = 0; q < l.paths.size() && tc; ++q) {
+  // Tensor-core paths: paths writing the same output block become one GEMM whose K range
+  // concatenates their inputs (segments in path order); the resulting problems go out as
+  // grouped launches.  When every path runs on the tensor cores and the blocks tile the
+  // output, the GEMMs store directly (no zero fill, no read-modify-write).
+  struct Problem {
+    int o0, o1;
+    std::vector<GemmSpec> segs;
+  };
+  std::vector<Problem> problems;
+  bool all_tc = tc, overlap = false;
+  for (size_t q = 0; q < l.paths.size(); ++q) {
     const auto &p = l.paths[q];
     const TCWeights &t = l.tc[q];
-    if (!(backward ? t.bwd_hi : t.fwd_hi))
+    if (!tc || !(backward ? t.bwd_hi : t.fwd_hi)) {
+      all_tc = false;
       continue;
+    }
     int o0 = backward ? p.in_offset : p.out_offset, o1 = o0 + (backward ? p.in_mul : p.out_mul) * p.dim;
+    GemmSpec g = !backward ? GemmSpec{n, p.out_mul, p.in_mul, p.dim, x + size_t(p.in_offset) * nx,
+                                      (long long)nx * p.in_mul, t.fwd_hi, t.fwd_lo, y + size_t(p.out_offset) * ny,
+                                      p.out_mul, (long long)ny * p.out_mul, true}
+                           : GemmSpec{n, p.in_mul, p.out_mul, p.dim, x + size_t(p.out_offset) * nx,
+                                      (long long)nx * p.out_mul, t.bwd_hi, t.bwd_lo, y + size_t(p.in_offset) * ny,
+                                      p.in_mul, (long long)ny * p.in_mul, true};
+    Problem *same = nullptr;
+    for (auto &pr : problems) {
+      if (pr.o0 == o0 && pr.o1 == o1 && pr.segs[0].N == g.N && pr.segs[0].batch == g.batch)
+        same = &pr;
+      else if (o0 < pr.o1 && pr.o0 < o1)
+        overlap = true;
+    }
+    if (same)
+      same->segs.push_back(g);
+    else
+      problems.push_back(Problem{o0, o1, {g}});
+  }
+  long long covered = 0;
+  for (auto &pr : problems)
+    covered += pr.o1 - pr.o0;
+  bool store = !add && all_tc && !overlap && covered == (backward ? l.input : l.output);
+  if (!add && !store)
+    lapis::check(cudaMemsetAsync(y, 0, size_t(ny) * (backward ? l.input : l.output) * 4, s));
+  // Problems whose blocks partly overlap stay in separate launches, in path order.
+  std::vector<GemmSpec> group;
+  std::vector<std::pair<int, int>> ranges;
+  for (auto &pr : problems) {
     for (auto &r : ranges)
-      if (o0 < r.second && r.first < o1) {
+      if (pr.o0 < r.second && r.first < pr.o1) {
         tc_gemm_group(s, group.data(), int(group.size()), status);
         group.clear();
         ranges.clear();
         break;
       }
-    ranges.push_back({o0, o1});
-    if (!backward)
-      group.push_back(GemmSpec{n, p.out_mul, p.in_mul, p.dim, x + size_t(p.in_offset) * nx, (long long)nx * p.in_mul,
-                               t.fwd_hi, t.fwd_lo, y + size_t(p.out_offset) * ny, p.out_mul,
-                               (long long)ny * p.out_mul, !store});
-    else
-      group.push_back(GemmSpec{n, p.in_mul, p.out_mul, p.dim, x + size_t(p.out_offset) * nx, (long long)nx * p.out_mul,
-                               t.bwd_hi, t.bwd_lo, y + size_t(p.in_offset) * ny, p.in_mul, (long long)ny * p.in_mul,
-                               !store});
+    ranges.push_back({pr.o0, pr.o1});
+    for (size_t k = 0; k < pr.segs.size(); ++k) {
+      GemmSpec g = pr.segs[k];
+      g.accumulate = !store;
+      g.join = k > 0;
+      group.push_back(g);
+    }
   }
   if (!group.empty())
     tc_gemm_group(s, group.data(), int(group.size()), status);
+  // The remaining paths on the FP32 SIMT kernels (accumulating).
   for (size_t q = 0; q < l.paths.size(); ++q) {
     const auto &p = l.paths[q];
     const float *w = l.weight + p.weight_offset;
     const TCWeights &t = l.tc[q];
+    if (tc && (backward ? t.bwd_hi : t.fwd_hi))
+      continue;
     if (!backward) {
-      if (tc && t.fwd_hi)
-        continue;
       if (launch_skinny<false>(s, n, p.out_mul, p.in_mul, p.dim, x + size_t(p.in_offset) * nx, p.in_mul,
                                (long long)nx * p.in_mul, w, p.out_mul, y + size_t(p.out_offset) * ny, p.out_mul,
                                (long long)ny * p.out_mul))
@@ -624,8 +651,6 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
                     p.in_mul, (long long)nx * p.in_mul, w, p.out_mul, y + size_t(p.out_offset) * ny, p.out_mul,
                     (long long)ny * p.out_mul);
     } else {
-      if (tc && t.bwd_hi)
-        continue;
       if (launch_skinny<true>(s, n, p.in_mul, p.out_mul, p.dim, x + size_t(p.out_offset) * nx, p.out_mul,
                               (long long)nx * p.out_mul, w, p.out_mul, y + size_t(p.in_offset) * ny, p.in_mul,
                               (long long)ny * p.in_mul))
@@ -746,6 +771,50 @@ extern "C" int mace_debug_gemm(int M, int N, int K, int batch, const float *A, c
       if (mode == 1) {
         tc_gemm(cudaStream_t(0), M, N, K, batch, A, (long long)M * K, hi, lo, C, N, (long long)M * N,
                 accumulate != 0, status);
+      } else if (mode == 3) { // K split into two segments with their own contiguous A and B
+        int k0 = (K / 64) * 32, k1 = K - k0;
+        if (!k0)
+          throw lapis::Error("mode 3 needs K >= 64");
+        std::vector<float> hs[2], ls[2];
+        for (int q = 0; q < 2; ++q) {
+          int kb = q ? k0 : 0, kc = q ? k1 : k0;
+          hs[q].resize(size_t(N) * kc);
+          ls[q].resize(size_t(N) * kc);
+          for (int n = 0; n < N; ++n)
+            for (int k = 0; k < kc; ++k) {
+              hs[q][size_t(n) * kc + k] = h[size_t(n) * K + kb + k];
+              ls[q][size_t(n) * kc + k] = l[size_t(n) * K + kb + k];
+            }
+        }
+        float *seg[2][3] = {};
+        try {
+          for (int q = 0; q < 2; ++q) {
+            int kb = q ? k0 : 0, kc = q ? k1 : k0;
+            lapis::check(cudaMalloc(&seg[q][0], size_t(batch) * M * kc * 4 + 16));
+            lapis::check(cudaMalloc(&seg[q][1], hs[q].size() * 4));
+            lapis::check(cudaMalloc(&seg[q][2], ls[q].size() * 4));
+            lapis::check(cudaMemcpy2D(seg[q][0], size_t(kc) * 4, A + kb, size_t(K) * 4, size_t(kc) * 4,
+                                      size_t(batch) * M, cudaMemcpyDeviceToDevice));
+            lapis::check(cudaMemcpy(seg[q][1], hs[q].data(), hs[q].size() * 4, cudaMemcpyHostToDevice));
+            lapis::check(cudaMemcpy(seg[q][2], ls[q].data(), ls[q].size() * 4, cudaMemcpyHostToDevice));
+          }
+          GemmSpec g[2];
+          for (int q = 0; q < 2; ++q) {
+            int kc = q ? k1 : k0;
+            g[q] = GemmSpec{M, N, kc, batch, seg[q][0], (long long)M * kc, seg[q][1], seg[q][2], C, N, (long long)M * N,
+                            accumulate != 0, q == 1};
+          }
+          tc_gemm_group(cudaStream_t(0), g, 2, status);
+          lapis::check(cudaDeviceSynchronize());
+        } catch (...) {
+          for (auto &q : seg)
+            for (auto *ptr : q)
+              cudaFree(ptr);
+          throw;
+        }
+        for (auto &q : seg)
+          for (auto *ptr : q)
+            cudaFree(ptr);
       } else { // grouped: one problem per batch plane, columns split as [128, N - 128]
         std::vector<GemmSpec> group;
         for (int z = 0; z < batch; ++z)

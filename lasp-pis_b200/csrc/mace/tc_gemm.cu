@@ -50,7 +50,7 @@ static_assert(kSmemBytes + 64 <= 232448, "shared memory budget");
 constexpr int kTmemCols = 4 * kBN; // hi*hi slab buffers 0/1, correction buffers 2/3 (512 columns)
 constexpr int kThreads = 384, kDrainThreads = 256;
 constexpr int kStatusGemmTimeout = 7;
-constexpr int kMaxGemmProblems = 16;
+constexpr int kMaxGemmProblems = 16, kMaxGemmSegments = 16;
 
 // Instruction descriptor: D fp32, A/B tf32, both K-major, M = 128, N = 128.
 constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(kBN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
@@ -70,14 +70,22 @@ struct TileGrid {
 };
 
 // One launch runs a group of independent GEMMs (the paths of an equivariant linear) over
-// their concatenated tile space, so short problems share one pipeline ramp and tail.
+// their concatenated tile space, so short problems share one pipeline ramp and tail.  A
+// problem's K range may be a concatenation of segments, each with its own A and B (paths
+// that add into the same output block): C = sum_s A_s B_s accumulates inside the tile.
+struct GemmSegment {
+  CUtensorMap a, bhi, blo;
+  int ktiles;
+};
 struct GemmProblem {
-  CUtensorMap a, bhi, blo, c;
+  CUtensorMap a, bhi, blo, c; // first K segment and the output
   TileGrid tg;
-  int ktiles, accumulate, tile0; // first tile of this problem in the group
+  int ktiles, kt0, accumulate, tile0; // total K tiles, the first segment's; first tile in the group
+  int seg0, nseg;                     // further K segments
 };
 struct GemmGroup {
   GemmProblem p[kMaxGemmProblems];
+  GemmSegment seg[kMaxGemmSegments];
   int count, tiles;
   // Problem of group tile t, advancing q (tiles are visited in increasing order).
   __device__ __forceinline__ const GemmProblem &find(int t, int &q) const {
@@ -138,7 +146,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const GemmProblem &pr = gg.find(t, q);
         int n0, m0, z;
         pr.tg.coords(t - pr.tile0, n0, m0, z);
-        for (int kt = 0; kt < pr.ktiles; ++kt, ++g) {
+        for (int kt = 0; kt < pr.kt0; ++kt, ++g) {
           int s = g % kStages;
           if (g >= kStages && !(ok = mbar_wait(empty0 + 8 * s, ((g / kStages) - 1) & 1, &abort_flag)))
             break;
@@ -147,6 +155,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(base, &pr.a, kt * kBK, m0, z, full0 + 8 * s);
           tma_load_2d(base + 2 * kTileBytes, &pr.bhi, kt * kBK, n0, full0 + 8 * s);
           tma_load_2d(base + 3 * kTileBytes, &pr.blo, kt * kBK, n0, full0 + 8 * s);
+        }
+        for (int sg = pr.seg0; sg < pr.seg0 + pr.nseg && ok; ++sg) {
+          const GemmSegment &seg = gg.seg[sg];
+          for (int kt = 0; kt < seg.ktiles; ++kt, ++g) {
+            int s = g % kStages;
+            if (g >= kStages && !(ok = mbar_wait(empty0 + 8 * s, ((g / kStages) - 1) & 1, &abort_flag)))
+              break;
+            unsigned base = smem_u32(smem + s * kStageBytes);
+            mbar_expect_tx(full0 + 8 * s, 3 * kTileBytes);
+            tma_load_3d(base, &seg.a, kt * kBK, m0, z, full0 + 8 * s);
+            tma_load_2d(base + 2 * kTileBytes, &seg.bhi, kt * kBK, n0, full0 + 8 * s);
+            tma_load_2d(base + 3 * kTileBytes, &seg.blo, kt * kBK, n0, full0 + 8 * s);
+          }
         }
       }
     }
@@ -390,27 +411,39 @@ void launch_group(cudaStream_t s, const GemmSpec *specs, int count, int *status)
   }
   GemmGroup gg{};
   long long tiles = 0;
-  int n = 0;
+  int n = 0, ns = 0;
   for (int k = 0; k < count; ++k) {
     const GemmSpec &g = specs[k];
     if (!g.M || !g.batch)
       continue;
-    GemmProblem &p = gg.p[n++];
+    if (!g.join) {
+      GemmProblem &p = gg.p[n++];
+      // C as [batch][M][ldc], written in 32 x 32 boxes over its first N columns.
+      p.c = make_map(g.C, g.N, g.M, 3, g.batch, g.batch > 1 ? g.strideC : (long long)g.M * g.ldc, g.ldc, 32);
+      p.tg = TileGrid{g.N / kBN, (g.M + kBM - 1) / kBM, 0};
+      long long pt = (long long)p.tg.nN * p.tg.nM * g.batch;
+      p.tg.tiles = int(std::min<long long>(pt, INT_MAX));
+      p.accumulate = g.accumulate;
+      p.tile0 = int(std::min<long long>(tiles, INT_MAX));
+      p.seg0 = ns;
+      tiles += pt;
+      if (tiles > INT_MAX)
+        throw lapis::Error("tensor-core GEMM has too many tiles");
+    }
+    GemmProblem &p = gg.p[n - 1];
     // A as [batch][M][K] (always a rank-3 map: the kernel issues 3D loads); B as [N][K].
-    p.a = make_map(g.A, g.K, g.M, 3, g.batch, g.batch > 1 ? g.strideA : (long long)g.M * g.K);
-    p.bhi = make_map(g.Bhi, g.K, g.N, 2, 1, 0);
-    p.blo = make_map(g.Blo, g.K, g.N, 2, 1, 0);
-    // C as [batch][M][ldc], written in 32 x 32 boxes over its first N columns.
-    p.c = make_map(g.C, g.N, g.M, 3, g.batch, g.batch > 1 ? g.strideC : (long long)g.M * g.ldc, g.ldc, 32);
-    p.tg = TileGrid{g.N / kBN, (g.M + kBM - 1) / kBM, 0};
-    long long pt = (long long)p.tg.nN * p.tg.nM * g.batch;
-    p.tg.tiles = int(std::min<long long>(pt, INT_MAX));
-    p.ktiles = g.K / kBK;
-    p.accumulate = g.accumulate;
-    p.tile0 = int(std::min<long long>(tiles, INT_MAX));
-    tiles += pt;
-    if (tiles > INT_MAX)
-      throw lapis::Error("tensor-core GEMM has too many tiles");
+    CUtensorMap a = make_map(g.A, g.K, g.M, 3, g.batch, g.batch > 1 ? g.strideA : (long long)g.M * g.K);
+    CUtensorMap bhi = make_map(g.Bhi, g.K, g.N, 2, 1, 0), blo = make_map(g.Blo, g.K, g.N, 2, 1, 0);
+    if (!g.join) {
+      p.a = a, p.bhi = bhi, p.blo = blo;
+      p.kt0 = g.K / kBK;
+    } else {
+      GemmSegment &sg = gg.seg[ns++];
+      sg.a = a, sg.bhi = bhi, sg.blo = blo;
+      sg.ktiles = g.K / kBK;
+      p.nseg += 1;
+    }
+    p.ktiles += g.K / kBK;
   }
   if (!n)
     return;
@@ -429,10 +462,34 @@ void tc_gemm(cudaStream_t s, int M, int N, int K, int batch, const float *A, lon
 }
 
 void tc_gemm_group(cudaStream_t s, const GemmSpec *specs, int count, int *status) {
-  for (int k = 0; k < count; ++k)
-    if (specs[k].M && specs[k].batch)
-      check_problem(specs[k]);
-  for (int k = 0; k < count; k += kMaxGemmProblems)
-    launch_group(s, specs + k, std::min(count - k, kMaxGemmProblems), status);
+  for (int k = 0; k < count; ++k) {
+    const GemmSpec &g = specs[k];
+    if (!g.M || !g.batch)
+      continue;
+    check_problem(g);
+    if (g.join && (k == 0 || specs[k - 1].M != g.M || specs[k - 1].N != g.N || specs[k - 1].batch != g.batch ||
+                   specs[k - 1].C != g.C || specs[k - 1].ldc != g.ldc || specs[k - 1].strideC != g.strideC ||
+                   specs[k - 1].accumulate != g.accumulate))
+      throw lapis::Error("tensor-core GEMM segment does not match its problem");
+  }
+  // Launches of at most kMaxGemmProblems problems and kMaxGemmSegments further segments; a
+  // problem's segments stay in one launch.
+  for (int k = 0; k < count;) {
+    int end = k, problems = 0, segments = 0;
+    while (end < count) {
+      int e = end + 1;
+      while (e < count && specs[e].join)
+        ++e;
+      if (e - end - 1 > kMaxGemmSegments)
+        throw lapis::Error("tensor-core GEMM problem has too many segments");
+      if (problems + 1 > kMaxGemmProblems || segments + (e - end - 1) > kMaxGemmSegments)
+        break;
+      ++problems;
+      segments += e - end - 1;
+      end = e;
+    }
+    launch_group(s, specs + k, end - k, status);
+    k = end;
+  }
 }
 } // namespace mace

@@ -16,9 +16,11 @@ SHAPES = [(1000, 128, 128, 1), (300, 256, 2048, 3), (10000, 512, 512, 1), (130, 
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
-@pytest.mark.parametrize("mode", [0, 1, 2], ids=["simt", "tcgen05", "tcgen05-grouped"])
+@pytest.mark.parametrize("mode", [0, 1, 2, 3], ids=["simt", "tcgen05", "tcgen05-grouped", "tcgen05-ksegments"])
 def test_gemm_matches_fp64(library, shape, mode):
     import torch
+    if mode == 3 and shape[2] < 64:
+        pytest.skip("K segments need K >= 64")
     lib = ct.CDLL(str(library))
     lib.mace_debug_gemm.argtypes = [ct.c_int] * 4 + [ct.c_void_p] * 3 + [ct.c_int, ct.c_int]
     lib.mace_last_error.restype = ct.c_char_p
