@@ -414,7 +414,7 @@ def main():
                          "frac": achieved / peak, "peak_source": f"hbm_gbs ({kind})",
                          "traffic": TRAFFIC_PER_EDGE * edges if TRAFFIC_PER_EDGE else None,
                          "algorithmic_bytes_per_launch": edge_backward1_bytes(edges), "kernel_ms": k_ms,
-                         "limiter": "FP32 issue (six operations per tensor-product term and channel), not HBM"},
+                         "limiter": "FP32 issue (three operations per tensor-product term and channel, three per (path, input) group), not HBM"},
             "stages_ms": {k: float(np.mean(v)) for k, v in stages.items()},
             "gpu_launches": int(diag["launches"]) * args.steps,
             "clocks": clocks.summary(),

@@ -117,7 +117,7 @@ __device__ __forceinline__ bool channels_any(bool x) {
 }
 
 template <int L, bool Bwd, bool Accumulate>
-__global__ void __launch_bounds__(kThreads, L ? 3 : 6) edge_proj_kernel(ProjArgs a, TPValues cg) {
+__global__ void __launch_bounds__(kThreads, L ? 3 : 7) edge_proj_kernel(ProjArgs a, TPValues cg) {
   using S = Stage<L, Bwd>;
   using Tr = Traits<L>;
   constexpr int P = Tr::P, NC = Tr::NC, IN = Tr::IN, T = S::T, kStages = S::NS;
@@ -140,14 +140,15 @@ __global__ void __launch_bounds__(kThreads, L ? 3 : 6) edge_proj_kernel(ProjArgs
 
   if (warp == 4) {
     // ---------------- producer ----------------
-    // Edge metadata is read 32 edges (32 / T tiles) at a time, one edge per lane, so the
-    // global round trip is paid once per chunk rather than once per tile.
-    constexpr int kChunkTiles = 32 / T;
+    // The forward reads edge metadata 32 edges (32 / T tiles) at a time, one edge per lane, so
+    // the global round trip is paid once per chunk; the backward, whose tiles take longer,
+    // reads it per tile.
+    constexpr int kChunkTiles = Bwd ? 1 : 32 / T;
     bool run = true;
     for (int c0 = 0; c0 < ntiles && run; c0 += kChunkTiles) {
       int me = begin + c0 * T + lane, j = 0;
       EdgeMeta m{};
-      if (me < end) {
+      if (lane < kChunkTiles * T && me < end) {
         m.vec = a.vec[me];
         m.cut = a.cut[me];
         m.den = a.den[me];
