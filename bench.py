@@ -41,9 +41,9 @@ UNIT = "atoms*evals/s"
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 # DRAM read + write bytes per edge of the roofline kernel, from an ncu capture of the C2
-# workload (profiles/edge_backward1_C2.md: 1.0531 GB read + 8.83 MB written over 97,006
+# workload (profiles/edge_backward1_C2.md: 1.0523 GB read + 9.95 MB written over 97,006
 # edges), scaled by the edge count.
-TRAFFIC_PER_EDGE = (1.053105e9 + 8.828416e6) / 97006
+TRAFFIC_PER_EDGE = (1.052328e9 + 9.952512e6) / 97006
 
 
 def edge_backward1_bytes(edges: int, paths: int = 10) -> float:

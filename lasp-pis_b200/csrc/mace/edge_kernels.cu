@@ -145,8 +145,9 @@ __global__ void __launch_bounds__(kGeometryThreads)
 // The two 64 x 64 layers are small GEMMs over edges, fed from shared memory, which supplies one
 // 32-lane word per clock against 128 FMA lanes: a lane therefore owns a 4-edge x 8-output tile
 // (value and r-tangent, 64 accumulators), so every shared-memory word it loads feeds four FMAs.
-// Lane = 8 * edge group + output group: the lane's edges are the warp's slots 4 ge .. 4 ge + 3
-// and its outputs u = 8 go .. 8 go + 7.  LayerNorm sums combine the 8 lanes of an edge group
+// Lane = 8 * edge group + output group: the lane's edges are the warp's slots ge + 4 i (i < 4;
+// interleaved so the four groups' rows fall on distinct banks) and its outputs
+// u = 8 go .. 8 go + 7.  LayerNorm sums combine the 8 lanes of an edge group
 // with three shuffles.  Weights and vectors are stored permuted ([k][go][12], 8 used) so the 8
 // output groups of a quarter warp read distinct banks.  Each warp keeps its 16 edges' layer
 // inputs in shared rows (value [0, 64), tangent [68, 132)) and their Bessel basis and
@@ -211,7 +212,7 @@ __device__ __forceinline__ void tile_ln_silu(float (&a)[8], float (&da)[8], cons
 // Input layer for the lane's 4 edges: a = b0 + source[zs] + target[zr] + W1 x, da = W1 dx.
 __device__ __forceinline__ void tile_input(float (&a)[4][8], float (&da)[4][8], const float *w1, const float *b0,
                                            const float *source, const float *target, const int (&zs)[4],
-                                           const int (&zr)[4], int u0, const float *bas) {
+                                           const int (&zr)[4], int u0, const float *bas) { // bas: edge i at 4 i rows
   float b[8];
   load8(b0, b);
 #pragma unroll
@@ -233,7 +234,7 @@ __device__ __forceinline__ void tile_input(float (&a)[4][8], float (&da)[4][8], 
     load8(w1 + k * kRadialPerm, w);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      float xk = bas[i * kRadialBasis + k], dxk = bas[i * kRadialBasis + 10 + k];
+      float xk = bas[4 * i * kRadialBasis + k], dxk = bas[4 * i * kRadialBasis + 10 + k];
 #pragma unroll
       for (int m = 0; m < 8; ++m) {
         a[i][m] = fmaf(w[m], xk, a[i][m]);
@@ -243,12 +244,13 @@ __device__ __forceinline__ void tile_input(float (&a)[4][8], float (&da)[4][8], 
   }
 }
 
-// The lane's outputs into its edges' rows (after every lane of the warp has read them).
+// The lane's outputs into its edges' rows (edge i at 4 i rows; after every lane of the warp has
+// read them).
 __device__ __forceinline__ void tile_store(float *rows, const float (&a)[4][8], const float (&da)[4][8], int u0) {
   __syncwarp();
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    float *r = rows + i * kRadialRow + u0;
+    float *r = rows + 4 * i * kRadialRow + u0;
     *reinterpret_cast<float4 *>(r) = make_float4(a[i][0], a[i][1], a[i][2], a[i][3]);
     *reinterpret_cast<float4 *>(r + 4) = make_float4(a[i][4], a[i][5], a[i][6], a[i][7]);
     *reinterpret_cast<float4 *>(r + kRadialTan) = make_float4(da[i][0], da[i][1], da[i][2], da[i][3]);
@@ -294,8 +296,8 @@ __global__ void __launch_bounds__(kRadialThreads, 1) radial_kernel(long long E, 
   __syncthreads();
   const float d_ob = R.dens.out_b[0];
   const int u0 = 8 * go, po = go * 12; // the lane's outputs and their block in a permuted vector
-  float *rows = wrows + 4 * ge * kRadialRow;
-  const float *bas = wbas + 4 * ge * kRadialBasis;
+  float *rows = wrows + ge * kRadialRow;
+  const float *bas = wbas + ge * kRadialBasis;
   for (long long base = (long long)blockIdx.x * kRadialEdges; base < E; base += (long long)gridDim.x * kRadialEdges) {
     long long wbase = base + warp * kRadialEdgesPerWarp;
     int wcnt = E - wbase < kRadialEdgesPerWarp ? int(max(E - wbase, 0LL)) : kRadialEdgesPerWarp;
@@ -309,7 +311,7 @@ __global__ void __launch_bounds__(kRadialThreads, 1) radial_kernel(long long E, 
     int zs[4], zr[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      int j = 4 * ge + i, p = j < wcnt ? pair[wbase + j] : 0;
+      int j = ge + 4 * i, p = j < wcnt ? pair[wbase + j] : 0;
       zs[i] = p & 0xffff, zr[i] = p >> 16;
     }
     __syncwarp();
@@ -338,8 +340,8 @@ __global__ void __launch_bounds__(kRadialThreads, 1) radial_kernel(long long E, 
         load8(W + k * kRadialPerm, w);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          hv[i] = rows[i * kRadialRow + k];
-          dv[i] = rows[i * kRadialRow + kRadialTan + k];
+          hv[i] = rows[4 * i * kRadialRow + k];
+          dv[i] = rows[4 * i * kRadialRow + kRadialTan + k];
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i)
@@ -379,7 +381,7 @@ __global__ void __launch_bounds__(kRadialThreads, 1) radial_kernel(long long E, 
       }
       sv = group_sum(sv) + d_ob;
       dsv = group_sum(dsv);
-      int j = 4 * ge + i;
+      int j = ge + 4 * i;
       if (go == 0 && j < wcnt) {
         long long e = wbase + j;
         float2 cv = ea.cut[e];

@@ -310,14 +310,23 @@ void ModelData::load(const std::string &path) {
       std::vector<int> abc;
       std::vector<float> sorted;
       int starts[4];
+      // Per output, terms sorted by (a, b, c) with missing factors as 16 (stable), so the terms
+      // sharing a and (a, b) are contiguous.
       for (int o = 0; o < 4; ++o) {
         starts[o] = int(abc.size());
+        std::vector<std::pair<int, size_t>> block; // (a | b << 8 | c << 16, term)
         for (size_t t = 0; t < poly.size(); ++t)
           if (poly[t].output == o) {
             const auto &q = poly[t];
-            abc.push_back(q.a | (q.degree >= 2 ? q.b : 16) << 8 | (q.degree >= 3 ? q.c : 16) << 16);
-            sorted.insert(sorted.end(), coef.begin() + t * 512, coef.begin() + (t + 1) * 512);
+            block.push_back({q.a | (q.degree >= 2 ? q.b : 16) << 8 | (q.degree >= 3 ? q.c : 16) << 16, t});
           }
+        auto key = [](int v) { return (v & 255) << 16 | ((v >> 8) & 255) << 8 | v >> 16; }; // (a, b, c)
+        std::stable_sort(block.begin(), block.end(),
+                         [&](const auto &x, const auto &y) { return key(x.first) < key(y.first); });
+        for (auto &[packed, t] : block) {
+          abc.push_back(packed);
+          sorted.insert(sorted.end(), coef.begin() + t * 512, coef.begin() + (t + 1) * 512);
+        }
       }
       l.poly_out_start = make_int4(starts[0], starts[1], starts[2], starts[3]);
       // Compiled kernels when the sorted terms are exactly this layer's compiled table.

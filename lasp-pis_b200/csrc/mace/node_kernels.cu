@@ -435,8 +435,46 @@ template <int N> struct PUnroll<N, N> {
   template <class F> __device__ __forceinline__ static void run(F &&) {}
 };
 constexpr int kPolyPair = 2; // nodes per thread
-
 constexpr int kPolyWarps = 4;
+
+// Nested evaluation over the (a, b, c)-sorted terms of one output:
+//     y = sum_a v_a T_a,   T_a = sum_b v_b S_ab,   S_ab = sum_c cf_abc v_c
+// -- one FP32 operation per term plus one per (a, b) group and per a group -- and its VJP
+// with the output gradient G:
+//     g_c += cf_abc (G v_a v_b),   g_b += (G v_a) S_ab,   g_a += G T_a.
+// Missing factors are the constant slot 16 (v = 1; its gradient is discarded).
+template <int L> constexpr bool poly_same_a(int s, int t) { return PolyTable<L>::term(s).a == PolyTable<L>::term(t).a; }
+template <int L> constexpr bool poly_same_ab(int s, int t) {
+  return poly_same_a<L>(s, t) && PolyTable<L>::term(s).b == PolyTable<L>::term(t).b;
+}
+// First term of the a group / (a, b) group that term k of output o belongs to.
+template <int L> constexpr int a_head(int o, int k) {
+  while (k > PolyTable<L>::start(o) && poly_same_a<L>(k - 1, k))
+    --k;
+  return k;
+}
+template <int L> constexpr int ab_head(int o, int k) {
+  while (k > PolyTable<L>::start(o) && poly_same_ab<L>(k - 1, k))
+    --k;
+  return k;
+}
+template <int L> constexpr bool a_end(int o, int k) {
+  return k + 1 == PolyTable<L>::start(o + 1) || !poly_same_a<L>(k, k + 1);
+}
+template <int L> constexpr bool ab_end(int o, int k) {
+  return k + 1 == PolyTable<L>::start(o + 1) || !poly_same_ab<L>(k, k + 1);
+}
+template <int L> constexpr bool poly_groups_contiguous() {
+  using PT = PolyTable<L>;
+  for (int o = 0; o < PT::NOUT; ++o)
+    for (int s = PT::start(o); s < PT::start(o + 1); ++s)
+      for (int t = s + 1; t < PT::start(o + 1); ++t)
+        if ((poly_same_a<L>(s, t) && !poly_same_a<L>(t - 1, t)) ||
+            (poly_same_ab<L>(s, t) && !poly_same_ab<L>(t - 1, t)))
+          return false;
+  return true;
+}
+static_assert(poly_groups_contiguous<0>() && poly_groups_contiguous<1>(), "product terms must be (a, b, c)-sorted");
 
 template <int L, bool Bwd>
 __global__ void __launch_bounds__(32 * kPolyWarps, Bwd ? 2 : 3)
@@ -461,14 +499,20 @@ __global__ void __launch_bounds__(32 * kPolyWarps, Bwd ? 2 : 3)
     if constexpr (!Bwd) {
       PUnroll<0, PT::NOUT>::run([&](auto oc) {
         constexpr int o = decltype(oc)::value;
-        float acc[kPolyPair] = {};
+        float acc[kPolyPair], T[kPolyPair], S[kPolyPair];
         PUnroll<PT::start(o), PT::start(o + 1)>::run([&](auto kc) {
           constexpr int k = decltype(kc)::value;
           constexpr PolyABC t = PT::term(k);
+          constexpr int ab0 = ab_head<L>(o, k), a0 = a_head<L>(o, k);
           float cf = cs[k * 32 + lane];
 #pragma unroll
-          for (int q = 0; q < kPolyPair; ++q)
-            acc[q] = fmaf((cf * v[q][t.a]) * v[q][t.b], v[q][t.c], acc[q]);
+          for (int q = 0; q < kPolyPair; ++q) {
+            S[q] = k == ab0 ? cf * v[q][t.c] : fmaf(cf, v[q][t.c], S[q]);
+            if constexpr (ab_end<L>(o, k))
+              T[q] = ab0 == a0 ? v[q][t.b] * S[q] : fmaf(v[q][t.b], S[q], T[q]);
+            if constexpr (a_end<L>(o, k))
+              acc[q] = a0 == PT::start(o) ? v[q][t.a] * T[q] : fmaf(v[q][t.a], T[q], acc[q]);
+          }
         });
 #pragma unroll
         for (int q = 0; q < kPolyPair; ++q)
@@ -484,22 +528,29 @@ __global__ void __launch_bounds__(32 * kPolyWarps, Bwd ? 2 : 3)
           g[q][m] = 0.f;
       PUnroll<0, PT::NOUT>::run([&](auto oc) {
         constexpr int o = decltype(oc)::value;
-        float G[kPolyPair];
+        float G[kPolyPair], Gva[kPolyPair], u[kPolyPair], T[kPolyPair], S[kPolyPair];
 #pragma unroll
         for (int q = 0; q < kPolyPair; ++q)
           G[q] = ib + q < i1 ? grad[(size_t(o) * n + ib + q) * 512 + c0 + lane] : 0.f;
         PUnroll<PT::start(o), PT::start(o + 1)>::run([&](auto kc) {
           constexpr int k = decltype(kc)::value;
           constexpr PolyABC t = PT::term(k);
+          constexpr int ab0 = ab_head<L>(o, k), a0 = a_head<L>(o, k);
           float cf = cs[k * 32 + lane];
 #pragma unroll
           for (int q = 0; q < kPolyPair; ++q) {
-            float w = cf * G[q];
-            g[q][t.a] = fmaf(w * v[q][t.b], v[q][t.c], g[q][t.a]);
-            if constexpr (t.b != 16)
-              g[q][t.b] = fmaf(w * v[q][t.a], v[q][t.c], g[q][t.b]);
-            if constexpr (t.c != 16)
-              g[q][t.c] = fmaf(w * v[q][t.a], v[q][t.b], g[q][t.c]);
+            if constexpr (k == a0)
+              Gva[q] = G[q] * v[q][t.a];
+            if constexpr (k == ab0)
+              u[q] = Gva[q] * v[q][t.b];
+            S[q] = k == ab0 ? cf * v[q][t.c] : fmaf(cf, v[q][t.c], S[q]);
+            g[q][t.c] = fmaf(cf, u[q], g[q][t.c]);
+            if constexpr (ab_end<L>(o, k)) {
+              g[q][t.b] = fmaf(Gva[q], S[q], g[q][t.b]);
+              T[q] = ab0 == a0 ? v[q][t.b] * S[q] : fmaf(v[q][t.b], S[q], T[q]);
+            }
+            if constexpr (a_end<L>(o, k))
+              g[q][t.a] = fmaf(G[q], T[q], g[q][t.a]);
           }
         });
       });
