@@ -3,10 +3,13 @@
 //   C[z] (+)= A[z] * B      A: [M][K] fp32 row-major per batch z (node or edge features),
 //                           B: given as two K-major tf32 planes Bhi/Blo [N][K] with
 //                              B = Bhi + Blo (split once at model load).
-// Each A tile is split on the fly into hi = round_tf32(a) and lo = a - hi, and the tile
-// product is accumulated in TMEM as  A_hi*B_hi + A_lo*B_hi + A_hi*B_lo  (the dropped
-// A_lo*B_lo term is below 2^-22 relative), so the result carries FP32-level error while the
-// work runs on the tensor pipe.
+// A needs no hi plane: an MMA of kind::tf32 reads the top 19 bits of each fp32 operand, so
+// the loaded A tile itself acts as A_hi = trunc_tf32(a), and only
+// A_lo = round_tf32(a - trunc_tf32(a)) is written beside it.  The remainder a - trunc(a) has
+// the sign of a, so it is rounded (not left to the MMA's truncation) to keep the dropped part
+// unbiased.  The tile product is accumulated in TMEM as A_hi*B_hi + A_lo*B_hi + A_hi*B_lo (the
+// dropped parts are below 2^-21 relative and of either sign), so the result carries
+// FP32-level error while the work runs on the tensor pipe.
 //
 // The tensor pipe adds products into its accumulator with truncation toward zero, which
 // biases long accumulations coherently.  So the dominant A_hi*B_hi term is accumulated
@@ -21,7 +24,7 @@
 // while tile t is drained and stored.  CTA = 12 warps:
 //   warp 0       TMA producer (A, Bhi, Blo per 32-wide K slab, SWIZZLE_128B, 3-stage ring)
 //   warp 1       MMA issuer (one elected thread; UMMA 128 x 128 x 8)
-//   warps 2..3   split A into hi/lo in shared memory
+//   warps 2..3   write A_lo beside the A tile in shared memory
 //   warps 4..11  drain TMEM into FP32 registers: two warps per TMEM lane quadrant (lane =
 //                output row), each owning 64 of the 128 columns with two 32-column loads in
 //                flight; each writes its part of the tile as two 32 x 32 boxes staged
@@ -207,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_done_issued = 1;
     }
   } else if (warp < 4) {
-    // ---------------- A split: hi in place, lo beside it ----------------
+    // ---------------- A split: A_lo beside the tile (A_hi is the tile itself) ----------------
     int t = threadIdx.x - 64, g = 0, q = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < gg.tiles && ok; tile += gridDim.x)
@@ -218,14 +221,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        float4 *a = reinterpret_cast<float4 *>(smem + s * kStageBytes);
+        const float4 *a = reinterpret_cast<const float4 *>(smem + s * kStageBytes);
         float4 *lo = reinterpret_cast<float4 *>(smem + s * kStageBytes + kTileBytes);
 #pragma unroll
         for (int q = 0; q < kTileBytes / 16 / 64; ++q) {
-          float4 v = a[t + 64 * q], h, l;
-          h.x = tf32_hi(v.x), h.y = tf32_hi(v.y), h.z = tf32_hi(v.z), h.w = tf32_hi(v.w);
-          l.x = v.x - h.x, l.y = v.y - h.y, l.z = v.z - h.z, l.w = v.w - h.w;
-          a[t + 64 * q] = h;
+          float4 v = a[t + 64 * q], l;
+          l.x = tf32_hi(v.x - tf32_trunc(v.x)), l.y = tf32_hi(v.y - tf32_trunc(v.y));
+          l.z = tf32_hi(v.z - tf32_trunc(v.z)), l.w = tf32_hi(v.w - tf32_trunc(v.w));
           lo[t + 64 * q] = l;
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
