@@ -49,9 +49,9 @@ TRAFFIC_PER_EDGE = (1.052328e9 + 9.952512e6) / 97006
 def edge_backward1_bytes(edges: int, paths: int = 10) -> float:
     """Algorithmic HBM bytes of the layer-1 edge tensor-product backward per launch.
 
-    Per directed edge: the radial projection row R and its r-tangent dR (2 x paths x 128 fp32),
-    Y and dY/dd (16 + 48 fp32), the edge geometry (d, r: 16 B), cutoff and density pairs
-    (8 + 8 B), the sender index (4 B) and the edge force written (16 B).  The sender's
+    Per directed edge: the cutoff-scaled radial projection row and its r-derivative (2 x paths
+    x 128 fp32), Y and dY/dd (16 + 48 fp32), the edge geometry (d, r: 16 B), cutoff and density
+    pairs (8 + 8 B), the sender index (4 B) and the edge force written (16 B).  The sender's
     up-projected features and the up-gradient atomics stay in L2 and are not counted.
     """
     return edges * (2.0 * paths * 128 * 4 + 64 + 192 + 16 + 8 + 8 + 4 + 16)

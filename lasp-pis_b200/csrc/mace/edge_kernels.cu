@@ -157,11 +157,11 @@ struct RadialParams {
 };
 constexpr int kRadialThreads = 512, kRadialWarps = kRadialThreads / 32, kRadialEdgesPerWarp = 16;
 constexpr int kRadialEdges = kRadialWarps * kRadialEdgesPerWarp;
-constexpr int kRadialRow = 132, kRadialTan = 68, kRadialBasis = 20;
+constexpr int kRadialRow = 132, kRadialTan = 68, kRadialBasis = 22; // basis, d basis / dr, cut pair
 constexpr int kRadialPerm = 96; // floats per permuted 64-vector (8 groups x 12)
 __host__ __device__ constexpr int radial_perm(int u) { return (u >> 3) * 12 + (u & 7); }
 // Shared layout (floats): conv input [10][96], density input [10][96], W2 / W3 [64][96],
-// 13 permuted vectors, then per warp: rows [16][132] and basis [16][20].
+// 13 permuted vectors, then per warp: rows [16][132] and basis [16][22].
 constexpr int kRadialIn = 10 * kRadialPerm, kRadialW = 64 * kRadialPerm, kRadialVecs = 13 * kRadialPerm;
 constexpr int kRadialWarpFloats = kRadialEdgesPerWarp * (kRadialRow + kRadialBasis);
 constexpr int kRadialSmemFloats = 2 * kRadialIn + 2 * kRadialW + kRadialVecs + kRadialWarps * kRadialWarpFloats;
@@ -259,8 +259,10 @@ __device__ __forceinline__ void tile_store(float *rows, const float (&a)[4][8], 
   __syncwarp();
 }
 
+// scaled: write cut h and cut dh + dcut h (the projection GEMM then yields w and its r-derivative
+// directly); otherwise h and dh.
 __global__ void __launch_bounds__(kRadialThreads, 1) radial_kernel(long long E, RadialParams R, const int *pair,
-                                                                EdgeArrays ea, RadialOut ro) {
+                                                                EdgeArrays ea, RadialOut ro, int scaled) {
   extern __shared__ __align__(16) float sm[];
   float *c_in = sm, *d_in = c_in + kRadialIn, *c_w = d_in + kRadialIn, *vecs = c_w + 2 * kRadialW;
   float *c_b = vecs, *c_g = vecs + 3 * kRadialPerm, *c_bt = vecs + 6 * kRadialPerm;
@@ -307,6 +309,11 @@ __global__ void __launch_bounds__(kRadialThreads, 1) radial_kernel(long long E, 
       bool ok = j < wcnt;
       wbas[j * kRadialBasis + k] = ok ? ea.basis[size_t(wbase) * 10 + f] : 0.f;
       wbas[j * kRadialBasis + 10 + k] = ok ? ea.dbasis[size_t(wbase) * 10 + f] : 0.f;
+    }
+    if (scaled && lane < kRadialEdgesPerWarp) {
+      float2 cv = lane < wcnt ? ea.cut[wbase + lane] : make_float2(0.f, 0.f);
+      wbas[lane * kRadialBasis + 20] = cv.x;
+      wbas[lane * kRadialBasis + 21] = cv.y;
     }
     int zs[4], zr[4];
 #pragma unroll
@@ -362,8 +369,15 @@ __global__ void __launch_bounds__(kRadialThreads, 1) radial_kernel(long long E, 
       int r = f >> 6, c = f & 63;
       if (r < wcnt) {
         size_t o = size_t(wbase) * 64 + f;
-        ro.h[o] = wrows[r * kRadialRow + c];
-        ro.dh[o] = wrows[r * kRadialRow + kRadialTan + c];
+        float hv = wrows[r * kRadialRow + c], dv = wrows[r * kRadialRow + kRadialTan + c];
+        if (scaled) {
+          float cut = wbas[r * kRadialBasis + 20], dcut = wbas[r * kRadialBasis + 21];
+          ro.h[o] = cut * hv;
+          ro.dh[o] = fmaf(cut, dv, dcut * hv);
+        } else {
+          ro.h[o] = hv;
+          ro.dh[o] = dv;
+        }
       }
     }
     // ---- density network: 10 -> 64, LayerNorm + SiLU, -> 1, tanh(a^2) x cutoff ----
@@ -730,7 +744,7 @@ void launch_edge_geometry(cudaStream_t s, const DeviceGeometry &g, const int *sp
 }
 
 void launch_radial(cudaStream_t s, const DeviceGeometry &g, const Layer &l, const int *pair, EdgeArrays ea,
-                   RadialOut ro) {
+                   RadialOut ro, bool scaled) {
   long long E = g.edge_capacity;
   if (!E)
     return;
@@ -738,7 +752,8 @@ void launch_radial(cudaStream_t s, const DeviceGeometry &g, const Layer &l, cons
   lapis::check(cudaFuncSetAttribute(radial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   long long tiles = (E + kRadialEdges - 1) / kRadialEdges;
   int blocks = int(std::min<long long>(tiles, 148 * 2));
-  lapis::launch(radial_kernel, blocks, kRadialThreads, smem, s, E, RadialParams{l.radial, l.density}, pair, ea, ro);
+  lapis::launch(radial_kernel, blocks, kRadialThreads, smem, s, E, RadialParams{l.radial, l.density}, pair, ea, ro,
+                int(scaled));
 }
 
 void launch_message_forward(cudaStream_t s, int layer, const DeviceGeometry &g, const Layer &l, EdgeArrays ea,

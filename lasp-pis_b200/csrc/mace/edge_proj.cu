@@ -1,11 +1,13 @@
 // Edge tensor-product kernels over a precomputed radial projection.
 //
-// The radial projection of the reference's MH1Pair (mace/src/mh1.cu:331-353),
-//     R[e][p*128 + c] = sum_a h[e][a] W[a][p*128 + c]        (and dR from dh/dr),
-// is one dense E x 64 x (P*128) GEMM per layer.  It runs on the tensor cores (tc_gemm,
-// tf32 hi/lo split with FP32 drains) into an HBM buffer, chunked by receivers, and the
-// kernels below consume it:
-//   forward   messages and density, as mace/src/mh1.cu:331-389 (w = cut * (R + b));
+// The radial projection of the reference's MH1Pair (mace/src/mh1.cu:331-353) times the
+// envelope, w[e][p*128 + c] = cut_e (sum_a h[e][a] W[a][p*128 + c] + b[p*128 + c]), and its
+// r-derivative dw = cut dR + dcut (R + b), come from dense E x 64 x (P*128) GEMMs per layer
+// over rows the radial kernel has already scaled:
+//     R' = (cut h) W,   dR' = (cut dh + dcut h) W,   then  w = R' + cut b,  dw = dR' + dcut b.
+// They run on the tensor cores (tc_gemm, tf32 hi/lo split with FP32 drains) into an HBM
+// buffer, chunked by receivers, and the kernels below consume them:
+//   forward   messages and density, as mace/src/mh1.cu:331-389;
 //   backward  tensor-product adjoints, r-tangent and per-edge force, as mh1.cu:390-452.
 // The backward regroups the term sum into per-path Q_p = sum_t cg G[out] u[in] Y[sh] (then
 // dE/dr = sum_p Q_p dw_p), per-harmonic T_sh = sum_t cg G[out] u[in] w_p (then
@@ -61,7 +63,7 @@ struct ProjArgs {
   int n_up; // row stride of up / up_grad (the sender count)
   const int *row, *sender;
   const float4 *vec;
-  const float *R, *dR, *Y, *dY;
+  const float *R, *dR, *Y, *dY; // R', dR' (see above)
   const float2 *cut, *den;
   const float *up, *bias;
   const float *msg_grad, *rho_grad; // backward inputs
@@ -239,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, L ? 3 : 7) edge_proj_kernel(ProjArgs
         float w[P];
 #pragma unroll
         for (int p = 0; p < P; ++p)
-          w[p] = cv.x * (Rk[p * 128] + bias[p]);
+          w[p] = fmaf(cv.x, bias[p], Rk[p * 128]);
         Unroll<0, Tr::NT>::run([&](auto tc_) {
           constexpr int tt = decltype(tc_)::value;
           constexpr TPTerm q = Tr::term(tt);
@@ -251,9 +253,8 @@ __global__ void __launch_bounds__(kThreads, L ? 3 : 7) edge_proj_kernel(ProjArgs
         float w[P], dw[P];
 #pragma unroll
         for (int p = 0; p < P; ++p) {
-          float sv = Rk[p * 128] + bias[p];
-          w[p] = cv.x * sv;
-          dw[p] = cv.x * dRk[p * 128] + cv.y * sv;
+          w[p] = fmaf(cv.x, bias[p], Rk[p * 128]);
+          dw[p] = fmaf(cv.y, bias[p], dRk[p * 128]);
         }
         float Q[P], Tsh[16], ug[IN];
 #pragma unroll
@@ -380,9 +381,9 @@ ProjArgs proj_args(const DeviceGeometry &g, const Layer &l, EdgeArrays ea, Radia
   a.R = R;
   a.Y = ea.Y;
   a.dY = ea.dY;
-  a.cut = ea.cut;
   a.den = ro.density;
   a.up = up;
+  a.cut = ea.cut;
   a.bias = l.radial.out_b;
   a.status = g.status;
   return a;

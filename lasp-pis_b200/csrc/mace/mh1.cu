@@ -211,10 +211,11 @@ std::vector<Result> MH1::compute(bool batch) {
       dom->fetch_ghost_rows(c, up[k], l.in_comp, ns, 128);
     linear(s, n, l.res, up[k], res[k], false, false, status, ns);
     linear(s, n, l.skip, input, skip, false, false, status, in_rows);
-    launch_radial(s, c.geometry, l, pair, ea, ro[k]);
+    launch_radial(s, c.geometry, l, pair, ea, ro[k], projection);
     timer.mark("forward" + std::to_string(k) + ".linears/radial");
     if (projection) {
       for (auto &q : chunks) {
+        // (cut h) W per edge row and path channel; the edge kernel adds cut b.
         tc_gemm(s, int(q.e1 - q.e0), width, 64, 1, ro[k].h + q.e0 * 64, 0, l.radial.out_hi, l.radial.out_lo,
                 proj[k], width, 0, false, status);
         timer.mark("forward" + std::to_string(k) + ".projection");
@@ -283,7 +284,8 @@ std::vector<Result> MH1::compute(bool batch) {
       float *R = proj[k], *dR = proj[k] + size_t(chunk_cap) * width;
       for (auto &q : chunks) {
         int rows = int(q.e1 - q.e0);
-        if (chunks.size() == 1) // R is still in place from the forward pass
+        // (cut dh + dcut h) W; with several chunks, (cut h) W is recomputed beside it.
+        if (chunks.size() == 1) // (cut h) W is still in place from the forward pass
           tc_gemm(s, rows, width, 64, 1, ro[k].dh + q.e0 * 64, 0, l.radial.out_hi, l.radial.out_lo, dR, width, 0,
                   false, status);
         else
