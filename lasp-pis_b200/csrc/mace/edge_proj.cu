@@ -50,8 +50,8 @@ template <int L, bool Bwd> struct Stage {
   static constexpr int P = Traits<L>::P, IN = Traits<L>::IN;
   static constexpr int T = 2;                         // edges per tile
   // Ring depth: the layer-1 backward keeps 2 stages (50 KB) so that 3 CTAs fit an SM at its
-  // 128 registers; the lighter kernels take deeper rings within the same occupancy.
-  static constexpr int NS = Bwd ? (L ? 2 : 3) : 4;
+  // 128 registers, the layer-1 forward 3 (44 KB, 4 CTAs); layer 0 takes deeper rings.
+  static constexpr int NS = Bwd ? (L ? 2 : 3) : (L ? 3 : 4);
   static constexpr int ROW = P * 128 * 4;             // bytes of one R row
   static constexpr int R = 0, DR = R + T * ROW, U = DR + (Bwd ? T * ROW : 0), Y = U + T * IN * 512;
   static constexpr int DY = Y + T * 64, META = DY + (Bwd ? T * 192 : 0), BYTES = META + T * sizeof(EdgeMeta);
@@ -119,7 +119,7 @@ __device__ __forceinline__ bool channels_any(bool x) {
 }
 
 template <int L, bool Bwd, bool Accumulate>
-__global__ void __launch_bounds__(kThreads, L ? 3 : 7) edge_proj_kernel(ProjArgs a, TPValues cg) {
+__global__ void __launch_bounds__(kThreads, L ? (Bwd ? 3 : 4) : 7) edge_proj_kernel(ProjArgs a, TPValues cg) {
   using S = Stage<L, Bwd>;
   using Tr = Traits<L>;
   constexpr int P = Tr::P, NC = Tr::NC, IN = Tr::IN, T = S::T, kStages = S::NS;
