@@ -48,10 +48,12 @@ struct EdgeMeta {
 
 template <int L, bool Bwd> struct Stage {
   static constexpr int P = Traits<L>::P, IN = Traits<L>::IN;
-  static constexpr int T = 2;                         // edges per tile
+  // Edges per tile: layer 0 (16 terms per edge) takes 4 so that the per-tile channel reduction
+  // and its barrier are paid less often per edge.
+  static constexpr int T = L ? 2 : 4;
   // Ring depth: the layer-1 backward keeps 2 stages (50 KB) so that 3 CTAs fit an SM at its
-  // 128 registers, the layer-1 forward 3 (44 KB, 4 CTAs); layer 0 takes deeper rings.
-  static constexpr int NS = Bwd ? (L ? 2 : 3) : (L ? 3 : 4);
+  // 128 registers, the layer-1 forward 3 (44 KB, 4 CTAs); layer 0 keeps 8 edges in flight.
+  static constexpr int NS = L ? (Bwd ? 2 : 3) : 2;
   static constexpr int ROW = P * 128 * 4;             // bytes of one R row
   static constexpr int R = 0, DR = R + T * ROW, U = DR + (Bwd ? T * ROW : 0), Y = U + T * IN * 512;
   static constexpr int DY = Y + T * 64, META = DY + (Bwd ? T * 192 : 0), BYTES = META + T * sizeof(EdgeMeta);

@@ -184,7 +184,7 @@ std::vector<Result> MH1::compute(bool batch) {
   RadialOut ro[2];
   float *proj[2] = {nullptr, nullptr}; // [R | dR] per layer, chunk_cap rows each
   float *up[2], *rho[2], *raw[2], *res[2], *pin[2], *hidden[2];
-  float *skip = node("mh.t.skip", 2048), *msg = node("mh.t.msg", 5120),
+  float *msg = node("mh.t.msg", 5120),
         *gate = node("mh.t.gate", 8192), *poly = node("mh.t.poly", 2048), *node_e = node("mh.t.energy", 1);
   const float *input = x0;
   for (int k = 0; k < 2; ++k) {
@@ -210,7 +210,8 @@ std::vector<Result> MH1::compute(bool batch) {
     if (dom && k == 1)
       dom->fetch_ghost_rows(c, up[k], l.in_comp, ns, 128);
     linear(s, n, l.res, up[k], res[k], false, false, status, ns);
-    linear(s, n, l.skip, input, skip, false, false, status, in_rows);
+    // The skip connection goes straight into the layer output; the product linear adds onto it.
+    linear(s, n, l.skip, input, hidden[k], false, false, status, in_rows);
     launch_radial(s, c.geometry, l, pair, ea, ro[k], projection);
     timer.mark("forward" + std::to_string(k) + ".linears/radial");
     if (projection) {
@@ -231,8 +232,7 @@ std::vector<Result> MH1::compute(bool batch) {
     launch_normalize_gate(s, n, raw[k], res[k], rho[k], l.alpha, l.beta, cst[11], cst[12], gate);
     linear(s, n, l.two, gate, pin[k], false, false, status);
     launch_product(s, n, l, pin[k], poly);
-    linear(s, n, l.plin, poly, hidden[k], false, false, status);
-    launch_add(s, size_t(n) * (k ? 512 : 2048), skip, hidden[k], 1.f);
+    linear(s, n, l.plin, poly, hidden[k], false, true, status);
     if (k == 0) {
       linear(s, n, m.read0, hidden[0], node_e, false, false, status);
       launch_add(s, n, node_e, energy, cst[6]);
