@@ -334,30 +334,39 @@ __global__ void __launch_bounds__(kRadialThreads, 1) radial_kernel(long long E, 
       const float *W = c_w + (layer - 1) * kRadialW + po;
       float b[8];
       load8(c_b + layer * kRadialPerm + po, b);
+      // Output pairs (2 p, 2 p + 1) accumulate with paired FMAs (fma.rn.f32x2: two IEEE FMAs).
+      float2 a2[4][4], da2[4][4];
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {
-          a[i][m] = b[m];
-          da[i][m] = 0.f;
+        for (int p = 0; p < 4; ++p) {
+          a2[i][p] = make_float2(b[2 * p], b[2 * p + 1]);
+          da2[i][p] = make_float2(0.f, 0.f);
         }
 #pragma unroll 2
       for (int k = 0; k < 64; ++k) {
-        float w[8], hv[4], dv[4];
-        load8(W + k * kRadialPerm, w);
+        const float4 *w4 = reinterpret_cast<const float4 *>(W + k * kRadialPerm);
+        float4 wa = w4[0], wb = w4[1];
+        float2 w2[4] = {make_float2(wa.x, wa.y), make_float2(wa.z, wa.w), make_float2(wb.x, wb.y),
+                        make_float2(wb.z, wb.w)};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          hv[i] = rows[4 * i * kRadialRow + k];
-          dv[i] = rows[4 * i * kRadialRow + kRadialTan + k];
-        }
+          float hv = rows[4 * i * kRadialRow + k], dv = rows[4 * i * kRadialRow + kRadialTan + k];
+          float2 h2 = make_float2(hv, hv), d2 = make_float2(dv, dv);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int m = 0; m < 8; ++m) {
-            a[i][m] = fmaf(w[m], hv[i], a[i][m]);
-            da[i][m] = fmaf(w[m], dv[i], da[i][m]);
+          for (int p = 0; p < 4; ++p) {
+            a2[i][p] = __ffma2_rn(w2[p], h2, a2[i][p]);
+            da2[i][p] = __ffma2_rn(w2[p], d2, da2[i][p]);
           }
+        }
       }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          a[i][2 * p] = a2[i][p].x, a[i][2 * p + 1] = a2[i][p].y;
+          da[i][2 * p] = da2[i][p].x, da[i][2 * p + 1] = da2[i][p].y;
+        }
 #pragma unroll
       for (int i = 0; i < 4; ++i)
         tile_ln_silu(a[i], da[i], c_g + layer * kRadialPerm + po, c_bt + layer * kRadialPerm + po);

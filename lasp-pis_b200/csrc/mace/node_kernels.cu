@@ -477,8 +477,11 @@ template <int L> constexpr bool poly_groups_contiguous() {
 static_assert(poly_groups_contiguous<0>() && poly_groups_contiguous<1>(), "product terms must be (a, b, c)-sorted");
 
 template <int L, bool Bwd>
-__global__ void __launch_bounds__(32 * kPolyWarps, Bwd ? 2 : 3)
+__global__ void __launch_bounds__(32 * kPolyWarps, Bwd || L == 0 ? 2 : 3)
     product_fixed_kernel(int n, const float *coef, const float *x, const float *grad, float *y) {
+  // The thread's two nodes travel as float2 pairs, so every FMA and product below is one paired
+  // instruction (fma.rn.f32x2 / mul.rn.f32x2: two IEEE operations).
+  static_assert(kPolyPair == 2, "paired evaluation assumes two nodes per thread");
   using PT = PolyTable<L>;
   extern __shared__ float cs[]; // [NT][32]
   int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, c0 = blockIdx.x * 32;
@@ -487,79 +490,69 @@ __global__ void __launch_bounds__(32 * kPolyWarps, Bwd ? 2 : 3)
   __syncthreads();
   int i0 = blockIdx.y * kProdNodes, i1 = min(n, i0 + kProdNodes);
   for (int ib = i0 + warp * kPolyPair; ib < i1; ib += kPolyWarps * kPolyPair) {
-    float v[kPolyPair][17];
+    bool second = ib + 1 < i1;
+    float2 v[17];
 #pragma unroll
-    for (int q = 0; q < kPolyPair; ++q) {
-      int i = ib + q;
-#pragma unroll
-      for (int m = 0; m < 16; ++m)
-        v[q][m] = i < i1 ? x[(size_t(m) * n + i) * 512 + c0 + lane] : 0.f;
-      v[q][16] = 1.f;
-    }
+    for (int m = 0; m < 16; ++m)
+      v[m] = make_float2(x[(size_t(m) * n + ib) * 512 + c0 + lane],
+                         second ? x[(size_t(m) * n + ib + 1) * 512 + c0 + lane] : 0.f);
+    v[16] = make_float2(1.f, 1.f);
     if constexpr (!Bwd) {
       PUnroll<0, PT::NOUT>::run([&](auto oc) {
         constexpr int o = decltype(oc)::value;
-        float acc[kPolyPair], T[kPolyPair], S[kPolyPair];
+        float2 acc, T, S;
         PUnroll<PT::start(o), PT::start(o + 1)>::run([&](auto kc) {
           constexpr int k = decltype(kc)::value;
           constexpr PolyABC t = PT::term(k);
           constexpr int ab0 = ab_head<L>(o, k), a0 = a_head<L>(o, k);
           float cf = cs[k * 32 + lane];
-#pragma unroll
-          for (int q = 0; q < kPolyPair; ++q) {
-            S[q] = k == ab0 ? cf * v[q][t.c] : fmaf(cf, v[q][t.c], S[q]);
-            if constexpr (ab_end<L>(o, k))
-              T[q] = ab0 == a0 ? v[q][t.b] * S[q] : fmaf(v[q][t.b], S[q], T[q]);
-            if constexpr (a_end<L>(o, k))
-              acc[q] = a0 == PT::start(o) ? v[q][t.a] * T[q] : fmaf(v[q][t.a], T[q], acc[q]);
-          }
+          float2 cf2 = make_float2(cf, cf);
+          S = k == ab0 ? __fmul2_rn(cf2, v[t.c]) : __ffma2_rn(cf2, v[t.c], S);
+          if constexpr (ab_end<L>(o, k))
+            T = ab0 == a0 ? __fmul2_rn(v[t.b], S) : __ffma2_rn(v[t.b], S, T);
+          if constexpr (a_end<L>(o, k))
+            acc = a0 == PT::start(o) ? __fmul2_rn(v[t.a], T) : __ffma2_rn(v[t.a], T, acc);
         });
-#pragma unroll
-        for (int q = 0; q < kPolyPair; ++q)
-          if (ib + q < i1)
-            y[(size_t(o) * n + ib + q) * 512 + c0 + lane] = acc[q];
+        y[(size_t(o) * n + ib) * 512 + c0 + lane] = acc.x;
+        if (second)
+          y[(size_t(o) * n + ib + 1) * 512 + c0 + lane] = acc.y;
       });
     } else {
-      float g[kPolyPair][17];
+      float2 g[17];
 #pragma unroll
-      for (int q = 0; q < kPolyPair; ++q)
-#pragma unroll
-        for (int m = 0; m < 17; ++m)
-          g[q][m] = 0.f;
+      for (int m = 0; m < 17; ++m)
+        g[m] = make_float2(0.f, 0.f);
       PUnroll<0, PT::NOUT>::run([&](auto oc) {
         constexpr int o = decltype(oc)::value;
-        float G[kPolyPair], Gva[kPolyPair], u[kPolyPair], T[kPolyPair], S[kPolyPair];
-#pragma unroll
-        for (int q = 0; q < kPolyPair; ++q)
-          G[q] = ib + q < i1 ? grad[(size_t(o) * n + ib + q) * 512 + c0 + lane] : 0.f;
+        float2 G = make_float2(grad[(size_t(o) * n + ib) * 512 + c0 + lane],
+                               second ? grad[(size_t(o) * n + ib + 1) * 512 + c0 + lane] : 0.f);
+        float2 Gva, u, T, S;
         PUnroll<PT::start(o), PT::start(o + 1)>::run([&](auto kc) {
           constexpr int k = decltype(kc)::value;
           constexpr PolyABC t = PT::term(k);
           constexpr int ab0 = ab_head<L>(o, k), a0 = a_head<L>(o, k);
           float cf = cs[k * 32 + lane];
-#pragma unroll
-          for (int q = 0; q < kPolyPair; ++q) {
-            if constexpr (k == a0)
-              Gva[q] = G[q] * v[q][t.a];
-            if constexpr (k == ab0)
-              u[q] = Gva[q] * v[q][t.b];
-            S[q] = k == ab0 ? cf * v[q][t.c] : fmaf(cf, v[q][t.c], S[q]);
-            g[q][t.c] = fmaf(cf, u[q], g[q][t.c]);
-            if constexpr (ab_end<L>(o, k)) {
-              g[q][t.b] = fmaf(Gva[q], S[q], g[q][t.b]);
-              T[q] = ab0 == a0 ? v[q][t.b] * S[q] : fmaf(v[q][t.b], S[q], T[q]);
-            }
-            if constexpr (a_end<L>(o, k))
-              g[q][t.a] = fmaf(G[q], T[q], g[q][t.a]);
+          float2 cf2 = make_float2(cf, cf);
+          if constexpr (k == a0)
+            Gva = __fmul2_rn(G, v[t.a]);
+          if constexpr (k == ab0)
+            u = __fmul2_rn(Gva, v[t.b]);
+          S = k == ab0 ? __fmul2_rn(cf2, v[t.c]) : __ffma2_rn(cf2, v[t.c], S);
+          g[t.c] = __ffma2_rn(cf2, u, g[t.c]);
+          if constexpr (ab_end<L>(o, k)) {
+            g[t.b] = __ffma2_rn(Gva, S, g[t.b]);
+            T = ab0 == a0 ? __fmul2_rn(v[t.b], S) : __ffma2_rn(v[t.b], S, T);
           }
+          if constexpr (a_end<L>(o, k))
+            g[t.a] = __ffma2_rn(G, T, g[t.a]);
         });
       });
 #pragma unroll
-      for (int q = 0; q < kPolyPair; ++q)
-        if (ib + q < i1)
-#pragma unroll
-          for (int m = 0; m < 16; ++m)
-            y[(size_t(m) * n + ib + q) * 512 + c0 + lane] = g[q][m];
+      for (int m = 0; m < 16; ++m) {
+        y[(size_t(m) * n + ib) * 512 + c0 + lane] = g[m].x;
+        if (second)
+          y[(size_t(m) * n + ib + 1) * 512 + c0 + lane] = g[m].y;
+      }
     }
   }
 }
