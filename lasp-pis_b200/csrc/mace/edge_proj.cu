@@ -25,6 +25,7 @@
 #include "edge_common.cuh"
 #include "model.hpp"
 #include "tcgen05.cuh"
+#include <type_traits>
 
 namespace mace {
 using lapis::DeviceGeometry;
@@ -38,7 +39,33 @@ using tc::mbar_wait;
 using tc::smem_u32;
 
 constexpr int kStatusEdgeTimeout = 8;
-constexpr int kThreads = 160;
+
+// Channel values: a thread owns one channel (float) or two adjacent channels (float2, whose
+// arithmetic runs as paired FP32 instructions, fma.rn.f32x2 / mul.rn.f32x2).
+__device__ __forceinline__ float vfma(float a, float b, float c) { return fmaf(a, b, c); }
+__device__ __forceinline__ float2 vfma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float vmul(float a, float b) { return a * b; }
+__device__ __forceinline__ float2 vmul(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float hsum(float a) { return a; }
+__device__ __forceinline__ float hsum(float2 a) { return a.x + a.y; }
+template <class V> __device__ __forceinline__ V bcast(float x);
+template <> __device__ __forceinline__ float bcast<float>(float x) { return x; }
+template <> __device__ __forceinline__ float2 bcast<float2>(float x) { return make_float2(x, x); }
+template <class V> __device__ __forceinline__ V vzero() { return bcast<V>(0.f); }
+__device__ __forceinline__ void vatomic_add(float *p, float v) { atomicAdd(p, v); }
+__device__ __forceinline__ void vatomic_add(float2 *p, float2 v) { atomicAdd(p, v); }
+
+// Channel pairing per instantiation: the layer-1 backward keeps one channel per thread (its
+// register budget for two channels would leave one warp per scheduler).
+template <int L, bool Bwd> struct Lanes {
+  static constexpr bool kPair = !(L == 1 && Bwd);
+  static constexpr int W = kPair ? 2 : 1;        // channels per thread
+  static constexpr int kChanThreads = 128 / W;    // channel threads per CTA
+  static constexpr int kChanWarps = kChanThreads / 32;
+  static constexpr int kThreads = kChanThreads + 32; // plus the producer warp
+  static constexpr int kMinBlocks = L ? (Bwd ? 3 : 4) : (Bwd ? 5 : 8);
+  using V = std::conditional_t<kPair, float2, float>;
+};
 
 struct EdgeMeta {
   float4 vec; // d, r
@@ -107,27 +134,31 @@ __device__ __forceinline__ float warp_sum4(float v0, float v1, float v2, float v
   return k;
 }
 
-// OR of `x` over the 128 channel threads (named barrier 1); also a barrier among them.
-__device__ __forceinline__ bool channels_any(bool x) {
+// OR of `x` over the `count` channel threads (named barrier 1); also a barrier among them.
+__device__ __forceinline__ bool channels_any(bool x, int count) {
   unsigned r;
   asm volatile("{\n\t.reg .pred p, q;\n\t"
                "setp.ne.u32 q, %1, 0;\n\t"
-               "bar.red.or.pred p, 1, 128, q;\n\t"
+               "bar.red.or.pred p, 1, %2, q;\n\t"
                "selp.u32 %0, 1, 0, p;\n\t}"
                : "=r"(r)
-               : "r"(unsigned(x))
+               : "r"(unsigned(x)), "r"(count)
                : "memory");
   return r != 0;
 }
 
 template <int L, bool Bwd, bool Accumulate>
-__global__ void __launch_bounds__(kThreads, L ? (Bwd ? 3 : 4) : 7) edge_proj_kernel(ProjArgs a, TPValues cg) {
+__global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBlocks)
+    edge_proj_kernel(ProjArgs a, TPValues cg) {
   using S = Stage<L, Bwd>;
   using Tr = Traits<L>;
+  using LN = Lanes<L, Bwd>;
+  using V = typename LN::V;
   constexpr int P = Tr::P, NC = Tr::NC, IN = Tr::IN, T = S::T, kStages = S::NS;
+  constexpr int W = LN::W, kCW = LN::kChanWarps, kCT = LN::kChanThreads;
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t bars[2 * kStages]; // full[s] | empty[s]
-  __shared__ float red[2][4][T][4];
+  __shared__ float red[2][kCW][T][4];
   __shared__ volatile int abort_flag;
   int i = a.r0 + blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int begin = a.row[i], end = a.row[i + 1], ntiles = (end - begin + T - 1) / T;
@@ -136,13 +167,13 @@ __global__ void __launch_bounds__(kThreads, L ? (Bwd ? 3 : 4) : 7) edge_proj_ker
     abort_flag = 0;
     for (int s = 0; s < kStages; ++s) {
       mbar_init(full0 + 8 * s, 32);
-      mbar_init(empty0 + 8 * s, 128);
+      mbar_init(empty0 + 8 * s, kCT);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
-  if (warp == 4) {
+  if (warp == kCW) {
     // ---------------- producer ----------------
     // The forward reads edge metadata 32 edges (32 / T tiles) at a time, one edge per lane, so
     // the global round trip is paid once per chunk; the backward, whose tiles take longer,
@@ -198,27 +229,30 @@ __global__ void __launch_bounds__(kThreads, L ? (Bwd ? 3 : 4) : 7) edge_proj_ker
   }
 
   // ---------------- channels ----------------
+  // Thread c owns channels W c .. W c + W - 1; V holds them.
   int c = threadIdx.x;
-  float bias[P];
+  constexpr int CS = 128 / W; // stride of one 128-channel row in V units
+  V bias[P];
 #pragma unroll
   for (int p = 0; p < P; ++p)
-    bias[p] = a.bias[p * 128 + c];
-  float acc[Bwd ? 1 : NC], G[Bwd ? NC : 1], rg = 0.f, rsum = 0.f;
+    bias[p] = reinterpret_cast<const V *>(a.bias)[p * CS + c];
+  V acc[Bwd ? 1 : NC], G[Bwd ? NC : 1];
+  float rg = 0.f, rsum = 0.f;
   if constexpr (Bwd) {
 #pragma unroll
     for (int k = 0; k < NC; ++k)
-      G[k] = a.msg_grad[(size_t(k) * a.n + i) * 128 + c];
+      G[k] = reinterpret_cast<const V *>(a.msg_grad)[(size_t(k) * a.n + i) * CS + c];
     rg = a.rho_grad[i];
   } else {
 #pragma unroll
     for (int k = 0; k < NC; ++k)
-      acc[k] = 0.f;
+      acc[k] = vzero<V>();
   }
   bool ok = true;
   for (int t = 0; t < ntiles; ++t) {
     int s = t % kStages;
     ok = mbar_wait(full0 + 8 * s, (t / kStages) & 1, &abort_flag);
-    if (channels_any(!ok)) {
+    if (channels_any(!ok, kCT)) {
       ok = false;
       break;
     }
@@ -226,80 +260,84 @@ __global__ void __launch_bounds__(kThreads, L ? (Bwd ? 3 : 4) : 7) edge_proj_ker
     const EdgeMeta *meta = reinterpret_cast<const EdgeMeta *>(st + S::META);
     int cnt = min(T, end - (begin + t * T));
     for (int k = 0; k < cnt; ++k) {
-      const float *Rk = reinterpret_cast<const float *>(st + S::R + k * S::ROW) + c;
-      const float *Uk = reinterpret_cast<const float *>(st + S::U + k * IN * 512) + c;
+      const V *Rk = reinterpret_cast<const V *>(st + S::R + k * S::ROW) + c;
+      const V *Uk = reinterpret_cast<const V *>(st + S::U + k * IN * 512) + c;
       const float4 *Y4 = reinterpret_cast<const float4 *>(st + S::Y + k * 64);
       float2 cv = meta[k].cut;
-      float u[IN], y[16];
+      V u[IN];
+      float y[16];
 #pragma unroll
       for (int q = 0; q < IN; ++q)
-        u[q] = Uk[q * 128];
+        u[q] = Uk[q * CS];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         float4 v = Y4[q];
         y[4 * q] = v.x, y[4 * q + 1] = v.y, y[4 * q + 2] = v.z, y[4 * q + 3] = v.w;
       }
       if constexpr (!Bwd) {
-        float w[P];
+        V w[P];
 #pragma unroll
         for (int p = 0; p < P; ++p)
-          w[p] = fmaf(cv.x, bias[p], Rk[p * 128]);
+          w[p] = vfma(bcast<V>(cv.x), bias[p], Rk[p * CS]);
+        V uw = vzero<V>();
         Unroll<0, Tr::NT>::run([&](auto tc_) {
           constexpr int tt = decltype(tc_)::value;
           constexpr TPTerm q = Tr::term(tt);
-          acc[q.out] = fmaf(cg.v[tt] * y[q.sh], u[q.in] * w[q.path], acc[q.out]);
+          if constexpr (group_start<L>(tt))
+            uw = vmul(u[q.in], w[q.path]);
+          acc[q.out] = vfma(bcast<V>(cg.v[tt] * y[q.sh]), uw, acc[q.out]);
         });
         rsum += meta[k].den.x;
       } else {
-        const float *dRk = reinterpret_cast<const float *>(st + S::DR + k * S::ROW) + c;
-        float w[P], dw[P];
+        const V *dRk = reinterpret_cast<const V *>(st + S::DR + k * S::ROW) + c;
+        V w[P], dw[P];
 #pragma unroll
         for (int p = 0; p < P; ++p) {
-          w[p] = fmaf(cv.x, bias[p], Rk[p * 128]);
-          dw[p] = fmaf(cv.y, bias[p], dRk[p * 128]);
+          w[p] = vfma(bcast<V>(cv.x), bias[p], Rk[p * CS]);
+          dw[p] = vfma(bcast<V>(cv.y), bias[p], dRk[p * CS]);
         }
-        float Q[P], Tsh[16], ug[IN];
+        V Q[P], Tsh[16], ug[IN];
 #pragma unroll
         for (int p = 0; p < P; ++p)
-          Q[p] = 0.f;
+          Q[p] = vzero<V>();
 #pragma unroll
         for (int q = 0; q < 16; ++q)
-          Tsh[q] = 0.f;
+          Tsh[q] = vzero<V>();
 #pragma unroll
         for (int q = 0; q < IN; ++q)
-          ug[q] = 0.f;
+          ug[q] = vzero<V>();
         // Per group (p, in) with a_t = cg_t G[out_t] and S = sum_t a_t Y[sh_t]:
         //   Q_p += u[in] S,   ug[in] += w_p S,   T_sh += a_t (u[in] w_p)
         // -- three operations per term plus three per group.
-        float S = 0.f, uw = 0.f;
+        V S = vzero<V>(), uw = vzero<V>();
         Unroll<0, Tr::NT>::run([&](auto tc_) {
           constexpr int tt = decltype(tc_)::value;
           constexpr TPTerm q = Tr::term(tt);
-          float at = cg.v[tt] * G[q.out];
+          V at = vmul(bcast<V>(cg.v[tt]), G[q.out]);
           if constexpr (group_start<L>(tt)) {
-            uw = u[q.in] * w[q.path];
-            S = at * y[q.sh];
+            uw = vmul(u[q.in], w[q.path]);
+            S = vmul(at, bcast<V>(y[q.sh]));
           } else {
-            S = fmaf(at, y[q.sh], S);
+            S = vfma(at, bcast<V>(y[q.sh]), S);
           }
-          Tsh[q.sh] = fmaf(at, uw, Tsh[q.sh]);
+          Tsh[q.sh] = vfma(at, uw, Tsh[q.sh]);
           if constexpr (group_end<L>(tt)) {
-            Q[q.path] = fmaf(u[q.in], S, Q[q.path]);
+            Q[q.path] = vfma(u[q.in], S, Q[q.path]);
             if constexpr (L > 0)
-              ug[q.in] = fmaf(w[q.path], S, ug[q.in]);
+              ug[q.in] = vfma(w[q.path], S, ug[q.in]);
           }
         });
         if constexpr (L > 0) {
           int j = meta[k].sender;
 #pragma unroll
           for (int q = 0; q < IN; ++q)
-            atomicAdd(a.up_grad + (size_t(q) * a.n_up + j) * 128 + c, ug[q]);
+            vatomic_add(reinterpret_cast<V *>(a.up_grad + (size_t(q) * a.n_up + j) * 128) + c, ug[q]);
         }
-        float dr = 0.f;
+        V dr2 = vzero<V>();
 #pragma unroll
         for (int p = 0; p < P; ++p)
-          dr = fmaf(Q[p], dw[p], dr);
-        float gx = 0.f, gy = 0.f, gz = 0.f;
+          dr2 = vfma(Q[p], dw[p], dr2);
+        V g2[3] = {vzero<V>(), vzero<V>(), vzero<V>()};
         const float4 *g4 = reinterpret_cast<const float4 *>(st + S::DY + k * 192);
 #pragma unroll
         for (int q = 0; q < 12; ++q) {
@@ -308,23 +346,26 @@ __global__ void __launch_bounds__(kThreads, L ? (Bwd ? 3 : 4) : 7) edge_proj_ker
 #pragma unroll
           for (int m = 0; m < 4; ++m) {
             int idx = 4 * q + m, sh = idx / 3, ax = idx % 3;
-            float &g = ax == 0 ? gx : ax == 1 ? gy : gz;
-            g = fmaf(Tsh[sh], gv[m], g);
+            g2[ax] = vfma(Tsh[sh], bcast<V>(gv[m]), g2[ax]);
           }
         }
-        float sum = warp_sum4(dr, gx, gy, gz, lane);
+        float sum = warp_sum4(hsum(dr2), hsum(g2[0]), hsum(g2[1]), hsum(g2[2]), lane);
         if (lane < 4)
           red[t & 1][warp][k][2 * (lane & 1) + (lane >> 1)] = sum;
       }
     }
     if constexpr (Bwd) {
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, %0;" ::"r"(kCT) : "memory");
       if (c < cnt) {
         int e = begin + t * T + c;
         float sum[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          sum[q] = red[t & 1][0][c][q] + red[t & 1][1][c][q] + red[t & 1][2][c][q] + red[t & 1][3][c][q];
+        for (int q = 0; q < 4; ++q) {
+          sum[q] = red[t & 1][0][c][q];
+#pragma unroll
+          for (int w = 1; w < kCW; ++w)
+            sum[q] += red[t & 1][w][c][q];
+        }
         float4 v = meta[c].vec;
         float r = v.w > 0.f ? v.w : 1e-10f;
         float drt = sum[0] + rg * meta[c].den.y;
@@ -342,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, L ? (Bwd ? 3 : 4) : 7) edge_proj_ker
     if (ok) {
 #pragma unroll
       for (int k = 0; k < NC; ++k)
-        a.msg[(size_t(k) * a.n + i) * 128 + c] = acc[k];
+        reinterpret_cast<V *>(a.msg)[(size_t(k) * a.n + i) * CS + c] = acc[k];
       if (c == 0)
         a.rho[i] = rsum;
     }
@@ -364,10 +405,9 @@ __global__ void __launch_bounds__(kThreads, L ? (Bwd ? 3 : 4) : 7) edge_proj_ker
 template <int L, bool Bwd, bool Accumulate>
 void launch_proj(cudaStream_t s, int blocks, const ProjArgs &a, const TPValues &cg) {
   constexpr int smem = Stage<L, Bwd>::NS * Stage<L, Bwd>::BYTES;
-  static_assert(Stage<L, Bwd>::BYTES % 128 == 0 || true, "");
   lapis::check(
       cudaFuncSetAttribute(edge_proj_kernel<L, Bwd, Accumulate>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  lapis::launch(edge_proj_kernel<L, Bwd, Accumulate>, blocks, kThreads, smem, s, a, cg);
+  lapis::launch(edge_proj_kernel<L, Bwd, Accumulate>, blocks, Lanes<L, Bwd>::kThreads, smem, s, a, cg);
 }
 
 ProjArgs proj_args(const DeviceGeometry &g, const Layer &l, EdgeArrays ea, RadialOut ro, const ProjectionChunk &k,
