@@ -36,7 +36,9 @@ __device__ __forceinline__ D1 envelope(D1 r, float rc, float p) {
   return cst(1.f) - cst((p + 1) * (p + 2) * .5f) * dpow(x, p) + cst(p * (p + 2)) * dpow(x, p + 1) -
          cst(p * (p + 1) * .5f) * dpow(x, p + 2);
 }
-__device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + expf(-x)); }
+// Logistic sigmoid; __frcp_rn is the correctly rounded reciprocal, i.e. the same value as the
+// IEEE division 1 / y.
+__device__ __forceinline__ float sigm(float x) { return __frcp_rn(1.f + expf(-x)); }
 
 __device__ __forceinline__ float warp_allsum(float v) {
 #pragma unroll
