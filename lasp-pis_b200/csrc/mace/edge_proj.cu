@@ -83,8 +83,12 @@ template <int L, bool Bwd> struct Stage {
   static constexpr int NS = L ? (Bwd ? 2 : 3) : 2;
   static constexpr int ROW = P * 128 * 4;             // bytes of one R row
   static constexpr int R = 0, DR = R + T * ROW, U = DR + (Bwd ? T * ROW : 0), Y = U + T * IN * 512;
-  static constexpr int DY = Y + T * 64, META = DY + (Bwd ? T * 192 : 0), BYTES = META + T * sizeof(EdgeMeta);
-  static constexpr unsigned tx(int cnt) { return cnt * ((Bwd ? 2 : 1) * ROW + IN * 512 + 64 + (Bwd ? 192 : 0)); }
+  static constexpr int DY = Y + T * 64, META = DY + (Bwd ? T * 192 : 0), EF = META + T * sizeof(EdgeMeta);
+  // EF: an accumulating backward's current per-edge forces, copied in with the tile.
+  static constexpr int BYTES = EF + (Bwd ? T * 16 : 0);
+  static constexpr unsigned tx(int cnt, bool forces) {
+    return cnt * ((Bwd ? 2 : 1) * ROW + IN * 512 + 64 + (Bwd ? 192 : 0) + (forces ? 16 : 0));
+  }
 };
 
 struct ProjArgs {
@@ -205,7 +209,7 @@ __global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBl
           reinterpret_cast<EdgeMeta *>(st + S::META)[k] = m;
         __syncwarp();
         if (lane == 0)
-          mbar_expect_tx(full, S::tx(cnt));
+          mbar_expect_tx(full, S::tx(cnt, Bwd && Accumulate));
         __syncwarp();
         if (lane == 0) {
           size_t r = size_t(e0 - a.e_base) * (P * 128);
@@ -215,6 +219,8 @@ __global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBl
           bulk_load(sb + S::Y, a.Y + size_t(e0) * 16, cnt * 64, full);
           if constexpr (Bwd)
             bulk_load(sb + S::DY, a.dY + size_t(e0) * 48, cnt * 192, full);
+          if constexpr (Bwd && Accumulate)
+            bulk_load(sb + S::EF, a.edge_force + e0, cnt * 16, full);
         }
         if (mine) {
 #pragma unroll
@@ -371,7 +377,7 @@ __global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBl
         float drt = sum[0] + rg * meta[c].den.y;
         float4 f = make_float4(sum[1] + drt * v.x / r, sum[2] + drt * v.y / r, sum[3] + drt * v.z / r, 0.f);
         if (Accumulate) {
-          float4 o = a.edge_force[e];
+          float4 o = reinterpret_cast<const float4 *>(st + S::EF)[c];
           f.x += o.x, f.y += o.y, f.z += o.z;
         }
         a.edge_force[e] = f;
