@@ -15,8 +15,10 @@ extern "C" {
 #endif
 /* Replaces mace_create_mh1 (mace/include/mace/c_api.h:8). */
 MACE_EXPORT void *mace_create_mh1(const char *archive, int backend);
-/* Replaces mace_create_mh1_head (mace/include/mace/c_api.h:10).  Archives carry one
- * head; a non-empty head is rejected for them like the reference does. */
+/* Replaces mace_create_mh1_head (mace/include/mace/c_api.h:10).  `model` is a PWMH1001
+ * archive or an MH1 PyTorch ZIP checkpoint; a checkpoint is converted for `head` (NULL or ""
+ * selects "matpes_r2scan").  Archives carry one head; a non-empty head is rejected for them
+ * like the reference does. */
 MACE_EXPORT void *mace_create_mh1_head(const char *model, int backend, const char *head);
 /* Replaces mace_destroy (mace/include/mace/c_api.h:11). */
 MACE_EXPORT void mace_destroy(void *handle);
@@ -34,6 +36,8 @@ MACE_EXPORT int mace_diagnostics(void *handle, char *buffer, size_t capacity);
 /* Like mace_create_mh1 but binds the handle to CUDA device `device` (the reference binds
  * to whatever device is current at creation). */
 MACE_EXPORT void *mace_create_mh1_device(const char *archive, int backend, int device);
+/* mace_create_mh1_head bound to CUDA device `device`. */
+MACE_EXPORT void *mace_create_mh1_device_head(const char *model, int backend, const char *head, int device);
 /* Spatial domain decomposition of one structure across `world` ranks (one process per GPU;
  * B200 build addition, no counterpart in the reference).  Every rank creates its handle with
  * the same 128-byte NCCL id (from mace_nccl_unique_id on one rank) and then calls

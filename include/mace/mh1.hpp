@@ -13,7 +13,9 @@ class MACE_EXPORT MH1 final : public lapis::Calculator {
   std::vector<lapis::Result> evaluate_batch() override;
 
 public:
-  // PWMH1001 archive.  An empty head is required for archives (they carry one head).
+  // `model` is a PWMH1001 archive or an MH1 PyTorch ZIP checkpoint, which is converted on
+  // the host for `head` ("matpes_r2scan" when empty).  An empty head is required for
+  // archives (they carry one head).
   explicit MH1(const std::string &model, lapis::Options options = {});
   MH1(const std::string &model, lapis::Options options, const std::string &head);
   ~MH1() override;

@@ -140,11 +140,15 @@ void *mace_create_mh1_head(const char *path, int b, const char *head) {
 }
 
 void *mace_create_mh1_device(const char *path, int b, int device) {
+  return mace_create_mh1_device_head(path, b, nullptr, device);
+}
+
+void *mace_create_mh1_device_head(const char *path, int b, const char *head, int device) {
   try {
     error.clear();
     if (device < 0)
       throw Error("Invalid device");
-    return create(path, b, nullptr, device);
+    return create(path, b, head, device);
   } catch (const std::exception &e) {
     error = e.what();
     return nullptr;

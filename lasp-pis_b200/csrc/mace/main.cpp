@@ -86,7 +86,17 @@ int main(int argc, char **argv) {
     }
     std::ostream &out = output.empty() ? std::cout : file;
     out << std::setprecision(17);
-    std::cerr << "MACE head: fixed by processed archive\n";
+    // The head banner: the selected head for an original (ZIP) checkpoint, else the archive's.
+    bool checkpoint = false;
+    {
+      std::ifstream m(model, std::ios::binary);
+      char magic[2] = {};
+      checkpoint = m.read(magic, 2) && magic[0] == 'P' && magic[1] == 'K';
+    }
+    std::cerr << "MACE head: "
+              << (checkpoint ? (head.empty() ? std::string("matpes_r2scan") : head)
+                             : std::string("fixed by processed archive"))
+              << "\n";
     if (json) {
       out << "{\"frame\":" << frame << ",\"atoms\":" << result.energies.size()
           << ",\"units\":{\"energy\":\"eV\",\"forces\":\"eV/Angstrom\",\"virial\":\"eV\"},\"energy\":"

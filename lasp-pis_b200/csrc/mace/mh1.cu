@@ -30,10 +30,7 @@ struct MH1::Model {
 
 MH1::MH1(const std::string &archive, Options o, const std::string &head)
     : Calculator(6, o), model_(std::make_unique<Model>()) {
-  if (!head.empty())
-    throw Error("unsupported MH1 checkpoint: head selection requires an original checkpoint; an archive already "
-                "contains one head");
-  model_->data.load(archive);
+  model_->data.load(archive, head);
 }
 MH1::MH1(const std::string &archive, Options o) : MH1(archive, o, {}) {}
 MH1::~MH1() = default;

@@ -1,4 +1,5 @@
-// PWMH1001 archive loading for the B200 build.
+// Model loading for the B200 build: a PWMH1001 archive, or an MH1 PyTorch ZIP checkpoint
+// converted to one on the host first (checkpoint.hpp; mace/src/mh1.cu:626-627).
 //
 // Record format and validation rules follow the reference loader (mace/src/mh1.cu:626-734,
 // mace/src/weights.cpp:305-317): magic, record count <= 10000, name length <= 1024, record
@@ -8,6 +9,7 @@
 // transposed at load (as the reference does) for coalesced per-unit reads, and the
 // tensor-product terms are mapped onto the term table compiled into the edge kernels.
 #include "model.hpp"
+#include "checkpoint.hpp"
 #include "product_table.h"
 #include <algorithm>
 #include <cmath>
@@ -69,20 +71,45 @@ bool ends_with(const std::string &s, const char *t) {
   return s.size() >= n && s.compare(s.size() - n, n, t) == 0;
 }
 
-Archive read_archive(const std::string &path) {
+Archive read_archive(const std::string &path, const std::string &head) {
   std::ifstream in(path, std::ios::binary | std::ios::ate);
   if (!in)
     throw Error("Cannot open MH1 archive: " + path);
   auto size = in.tellg();
-  if (size < 0 || uint64_t(size) >= (uint64_t(1) << 31))
-    throw Error("unsupported MH1 checkpoint: archive size");
-  std::string bytes(size_t(size), '\0');
-  in.seekg(0);
-  if (!in.read(bytes.data(), bytes.size()))
-    throw Error("cannot read MH1 archive: " + path);
-  if (bytes.size() >= 4 && bytes.compare(0, 4, "PK\x03\x04", 4) == 0)
-    throw Error("unsupported MH1 checkpoint: original ZIP checkpoints must be converted to a PWMH1001 "
-                "archive for this build");
+  const bool zip = size >= 4 && [&] {
+    char magic[4];
+    in.seekg(0);
+    return in.read(magic, 4) && std::memcmp(magic, "PK\x03\x04", 4) == 0;
+  }();
+  std::string bytes;
+  if (zip) {
+    // An original checkpoint: convert it for the requested head (the ZIP layer enforces
+    // its own 2 GiB bound).
+    if (uint64_t(size) > (uint64_t(1) << 31))
+      throw Error("checkpoint: archive exceeds 2 GiB limit");
+    std::vector<char> file(static_cast<size_t>(size));
+    in.seekg(0);
+    if (!in.read(file.data(), std::streamsize(file.size())))
+      throw Error("cannot read MH1 archive: " + path);
+    try {
+      bytes = convert_checkpoint(std::move(file), head);
+    } catch (const Error &) {
+      throw;
+    } catch (const std::exception &e) {
+      throw Error(e.what());
+    }
+  } else {
+    if (!head.empty())
+      throw Error("unsupported MH1 checkpoint: head selection requires an original checkpoint; an archive "
+                  "already contains one head");
+    if (size < 0 || uint64_t(size) >= (uint64_t(1) << 31))
+      throw Error("unsupported MH1 checkpoint: archive size");
+    bytes.assign(size_t(size), '\0');
+    in.clear();
+    in.seekg(0);
+    if (!in.read(bytes.data(), std::streamsize(bytes.size())))
+      throw Error("cannot read MH1 archive: " + path);
+  }
   std::istringstream s(bytes, std::ios::binary);
   char magic[8]{};
   s.read(magic, 8);
@@ -135,8 +162,8 @@ std::vector<float> transposed(const std::vector<float> &a, int rows, int cols, c
 }
 } // namespace
 
-void ModelData::load(const std::string &path) {
-  Archive a = read_archive(path);
+void ModelData::load(const std::string &path, const std::string &head) {
+  Archive a = read_archive(path, head);
   auto up = [&](const std::vector<float> &v) {
     bytes += v.size() * 4;
     return device.upload(v.data(), v.size() * 4);

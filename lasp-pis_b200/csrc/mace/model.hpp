@@ -79,7 +79,9 @@ struct ModelData {
   const float *e0_z;  // [119] baseline energy by atomic number
   size_t bytes = 0;
   int species = 0;
-  void load(const std::string &path);
+  // `path` is a PWMH1001 archive (head must be empty) or an MH1 ZIP checkpoint, converted
+  // for `head` ("matpes_r2scan" when empty).
+  void load(const std::string &path, const std::string &head = {});
 };
 
 // ---- kernels (edge_kernels.cu / node_kernels.cu) ----

@@ -22,6 +22,8 @@ def load(path=None) -> ct.CDLL:
     lib.mace_create_mh1_head.restype = ct.c_void_p
     lib.mace_create_mh1_device.argtypes = [ct.c_char_p, ct.c_int, ct.c_int]
     lib.mace_create_mh1_device.restype = ct.c_void_p
+    lib.mace_create_mh1_device_head.argtypes = [ct.c_char_p, ct.c_int, ct.c_char_p, ct.c_int]
+    lib.mace_create_mh1_device_head.restype = ct.c_void_p
     lib.mace_destroy.argtypes = [ct.c_void_p]
     lib.mace_destroy.restype = None
     lib.mace_last_error.restype = ct.c_char_p
@@ -94,7 +96,8 @@ class NativeMH1:
             self.handle = self.lib.mace_create_mh1_domain(str(archive).encode(), b, device, rank, world,
                                                           ct.c_char_p(bytes(nccl_id)))
         elif device is not None:
-            self.handle = self.lib.mace_create_mh1_device(str(archive).encode(), b, device)
+            self.handle = self.lib.mace_create_mh1_device_head(
+                str(archive).encode(), b, None if head is None else head.encode(), device)
         elif head is not None:
             self.handle = self.lib.mace_create_mh1_head(str(archive).encode(), b, head.encode())
         else:

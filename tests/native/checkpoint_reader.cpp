@@ -1,0 +1,88 @@
+// Native test of the checkpoint reader (host only).  Pins what the reference's
+// checkpoint/tests/reader.cpp pins:
+//
+//   checkpoint-reader ZIP       the fixture must open and its data.pkl decode to None; then
+//                               inert reducers, malformed pickles and strided views are checked
+//   checkpoint-reader --open F  only open F and decode its root (exit 1 if rejected)
+//
+// Prints one line on success; exits 1 with the error otherwise.
+#include "checkpoint.hpp"
+
+#include <cstring>
+#include <iostream>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+using mace::ckpt::Node;
+
+static void require(bool ok, const char *what) {
+  if (!ok)
+    throw std::runtime_error(std::string("checkpoint test failed: ") + what);
+}
+
+static bool rejects(const std::string &pickle, const mace::ckpt::Zip &zip) {
+  try {
+    mace::ckpt::unpickle(std::vector<char>(pickle.begin(), pickle.end()), zip);
+  } catch (const std::exception &) {
+    return true;
+  }
+  return false;
+}
+
+int main(int argc, char **argv) {
+  try {
+    if (argc == 3 && std::string(argv[1]) == "--open") {
+      mace::ckpt::Zip zip{std::string(argv[2])};
+      mace::ckpt::load(zip);
+      return 0;
+    }
+    if (argc != 2)
+      throw std::runtime_error("usage: checkpoint-reader ZIP | --open FILE");
+    mace::ckpt::Zip zip{std::string(argv[1])};
+    require(mace::ckpt::load(zip)->kind == Node::None, "fixture root is None");
+
+    // A reducer naming a Python callable is recorded, never called.
+    const std::string inert("\x80\x02" "cbuiltins\neval\n" ")R.");
+    auto obj = mace::ckpt::unpickle(std::vector<char>(inert.begin(), inert.end()), zip);
+    require(obj->kind == Node::Instance && obj->text == "builtins eval", "inert reducer");
+
+    // Malformed pickles: memo miss, no STOP, SETITEMS without a mark, oversized string.
+    require(rejects(std::string("\x80\x02" "h\x01.", 5), zip), "memo reference");
+    require(rejects(std::string("\x80\x02" "N"), zip), "missing STOP");
+    require(rejects(std::string("\x80\x02" "u."), zip), "SETITEMS without mark");
+    require(rejects(std::string("\x80\x02" "X\xff\xff\xff\x7f.", 8), zip), "oversized string");
+    require(rejects(std::string("\x80\x02" "NN.", 5), zip), "two values at STOP");
+    require(rejects(std::string("\x80\x01" "N.", 4), zip), "protocol 1");
+    require(rejects(std::string("\x80\x02" "I1\n.", 6), zip), "text opcode");
+
+    // Views honour the storage offset and row strides, and stay inside the storage.
+    mace::ckpt::Tensor t;
+    t.dtype = "FloatStorage";
+    const float storage[] = {0, 1, 2, 3, 4, 5};
+    auto bytes = std::make_shared<std::vector<char>>(sizeof(storage));
+    std::memcpy(bytes->data(), storage, sizeof(storage));
+    t.storage = bytes;
+    t.offset = 1;
+    t.shape = {2, 2};
+    t.stride = {3, 1};
+    require(t.values() == std::vector<double>({1, 2, 4, 5}), "strided view");
+    t.shape = {2, 2};
+    t.stride = {1, 2};
+    require(t.values() == std::vector<double>({1, 3, 2, 4}), "transposed view");
+    t.offset = 2;
+    t.stride = {3, 1};
+    bool outside = false;
+    try {
+      t.values();
+    } catch (const std::exception &) {
+      outside = true;
+    }
+    require(outside, "view past the storage");
+    std::cout << "ZIP fixture, inert reducers, malformed pickles and strided views passed\n";
+  } catch (const std::exception &e) {
+    std::cerr << e.what() << '\n';
+    return 1;
+  }
+  return 0;
+}

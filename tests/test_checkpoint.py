@@ -1,0 +1,260 @@
+"""The MH1 checkpoint route: ZIP/pickle reader and checkpoint -> archive converter (CPU).
+
+Follows the reference's own checks for this path: checkpoint/tests/reader.py (stored and
+deflated records, ZIP64 end records, truncation and CRC corruption), checkpoint/tests/
+reader.cpp (inert reducers, malformed pickles, strided views; here tests/native/
+checkpoint_reader.cpp) and mace/tests/check_checkpoint.py (every head converted byte for
+byte like the reference, a changed-weight checkpoint, an unknown head).  The byte-for-byte
+reference is the reference's converter compiled from its sources (oracle/_ref, when built)
+and the SHA-256 digests it produced for the seeded checkpoints (tests/golden/checkpoint_ref.json).
+"""
+import hashlib
+import io
+import json
+import struct
+import subprocess
+import zipfile
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, ROOT
+
+BIN = ROOT / "lasp-pis_b200" / "bin"
+DUMP = BIN / "mace-weights-dump"
+READER = BIN / "checkpoint-reader"
+REF_DUMP = ROOT / "oracle" / "_ref" / "mace-weights-dump-ref"
+GOLD = json.loads((GOLDEN / "checkpoint_ref.json").read_text())
+
+
+@pytest.fixture(scope="module")
+def tools():
+    if not (DUMP.exists() and READER.exists()):
+        subprocess.run(["make", "-s", "-C", str(ROOT / "lasp-pis_b200"), str(DUMP), str(READER)], check=True)
+    return DUMP, READER
+
+
+@pytest.fixture(scope="module")
+def checkpoints(tmp_path_factory):
+    from lasp_b200 import checkpoint
+    out = {}
+    for name, case in GOLD["cases"].items():
+        path = tmp_path_factory.mktemp("ckpt") / f"mh1_{name}.model"
+        checkpoint.write_checkpoint(path, case["seed"], getattr(torch, case["dtype"]))
+        out[name] = path
+    return out
+
+
+def run(*args):
+    return subprocess.run([str(a) for a in args], capture_output=True, text=True)
+
+
+def convert(model, out, head=None, tool=DUMP):
+    r = run(tool, model, out, *([head] if head is not None else []))
+    return r.returncode, r.stderr.strip()
+
+
+# ------------------------------------------------------------------------------- reader
+
+def zip_fixture(compression):
+    mem = io.BytesIO()
+    with zipfile.ZipFile(mem, "w", compression=compression) as z:
+        with z.open("archive/data.pkl", "w", force_zip64=True) as f:
+            f.write(b"\x80\x02N.")
+        z.writestr("archive/byteorder", "little")
+    return mem.getvalue()
+
+
+def with_zip64_end(data):
+    """The same archive ending in a ZIP64 end record, locator and saturated classic end record."""
+    end = len(data) - 22
+    _, _, _, count, _, size, offset, _ = struct.unpack("<IHHHHIIH", data[end:])
+    zip64 = struct.pack("<IQHHIIQQQQ", 0x06064B50, 44, 45, 45, 0, 0, count, count, size, offset)
+    locator = struct.pack("<IIQI", 0x07064B50, 0, end, 1)
+    eocd = struct.pack("<IHHHHIIH", 0x06054B50, 0, 0, 0xFFFF, 0xFFFF, 0xFFFFFFFF, 0xFFFFFFFF, 0)
+    return data[:end] + zip64 + locator + eocd
+
+
+@pytest.mark.parametrize("compression", [zipfile.ZIP_STORED, zipfile.ZIP_DEFLATED])
+def test_zip_reader_fixtures(tools, tmp_path, compression):
+    _, reader = tools
+    data = zip_fixture(compression)
+    path = tmp_path / "fixture.zip"
+    for good in (data, with_zip64_end(data)):
+        path.write_bytes(good)
+        r = run(reader, path)
+        assert r.returncode == 0, r.stderr
+    end = len(data) - 22
+    offset = struct.unpack("<I", data[end + 16:end + 20])[0]
+    truncated = data[:-8]
+    bad_crc = data[:offset + 16] + b"\0\0\0\0" + data[offset + 20:]
+    for bad, why in ((truncated, "end record"), (bad_crc, "checksum")):
+        path.write_bytes(bad)
+        r = run(reader, "--open", path)
+        assert r.returncode == 1 and why in r.stderr, (why, r.stderr)
+
+
+def test_zip_reader_rejects_unsupported(tools, tmp_path):
+    _, reader = tools
+    path = tmp_path / "x.zip"
+    mem = io.BytesIO()
+    with zipfile.ZipFile(mem, "w", compression=zipfile.ZIP_BZIP2) as z:
+        z.writestr("archive/data.pkl", b"\x80\x02N.")
+    path.write_bytes(mem.getvalue())
+    assert "unsupported ZIP compression" in run(reader, "--open", path).stderr
+    mem = io.BytesIO()
+    with zipfile.ZipFile(mem, "w") as z:
+        z.writestr("data.pkl", b"\x80\x02N.")
+    path.write_bytes(mem.getvalue())
+    assert "root directory" in run(reader, "--open", path).stderr
+    mem = io.BytesIO()
+    with zipfile.ZipFile(mem, "w") as z:
+        z.writestr("archive/data.pkl", b"\x80\x02N.")
+        z.writestr("archive/byteorder", "big")
+    path.write_bytes(mem.getvalue())
+    assert "little-endian" in run(reader, "--open", path).stderr
+
+
+def test_torch_save_decodes(tools, tmp_path):
+    """A plain torch.save file (parameters, buffers, OrderedDicts, sets, memo references)."""
+    _, reader = tools
+    m = torch.nn.Sequential(torch.nn.Linear(3, 4), torch.nn.LayerNorm(4), torch.nn.SiLU())
+    path = tmp_path / "seq.pt"
+    torch.save(m, path)
+    r = run(reader, "--open", path)
+    assert r.returncode == 0, r.stderr
+
+
+# ---------------------------------------------------------------------------- converter
+
+def records(data: bytes):
+    assert data[:8] == b"PWMH1001"
+    (count,) = struct.unpack("<I", data[8:12])
+    out, at = {}, 12
+    for _ in range(count):
+        n, size = struct.unpack("<IQ", data[at:at + 12])
+        name = data[at + 12:at + 12 + n].decode()
+        out[name] = data[at + 12 + n:at + 12 + n + size]
+        at += 12 + n + size
+    assert at == len(data)
+    return out
+
+
+@pytest.mark.parametrize("case", ["float64", "float32"])
+def test_conversion_matches_reference_digests(tools, checkpoints, tmp_path, case):
+    """Every head converts to the bytes the reference's converter wrote for it."""
+    for head, gold in GOLD["cases"][case]["heads"].items():
+        out = tmp_path / f"{head}.pwm"
+        rc, err = convert(checkpoints[case], out, head)
+        assert rc == 0, err
+        data = out.read_bytes()
+        assert len(data) == gold["bytes"] and hashlib.sha256(data).hexdigest() == gold["sha256"], head
+
+
+def test_default_head_is_matpes_r2scan(tools, checkpoints, tmp_path):
+    rc, err = convert(checkpoints["float64"], tmp_path / "d.pwm")
+    assert rc == 0, err
+    gold = GOLD["cases"]["float64"]["heads"]["matpes_r2scan"]["sha256"]
+    assert hashlib.sha256((tmp_path / "d.pwm").read_bytes()).hexdigest() == gold
+
+
+def test_converted_archive_is_a_valid_model(tools, checkpoints, tmp_path):
+    """The converted archive has the record set and shapes the loader validates, and the
+    float64 oracle evaluates it to finite energies, forces and virial."""
+    import oracle
+    from lasp_b200 import structures
+    out = tmp_path / "m.pwm"
+    assert convert(checkpoints["float64"], out)[0] == 0
+    rec = records(out.read_bytes())
+    assert len(rec) == 117
+    dims = np.frombuffer(rec["layer1.linear_1.dims"], np.int32)
+    assert list(dims) == [5120, 9728]
+    assert np.frombuffer(rec["layer1.tp.dims"], np.int32).tolist() == [10, 4, 40]
+    oracle.build()
+    s = structures.load("C1", ROOT / "lasp-pis_b200" / "data")
+    r = oracle.Oracle(out).calculate(s.positions, s.numbers, s.cell)
+    assert np.isfinite(r["energy"]) and np.isfinite(r["forces"]).all() and np.isfinite(r["virial"]).all()
+    assert np.abs(r["forces"].sum(axis=0)).max() < 1e-8 * max(1.0, np.abs(r["forces"]).max())
+
+
+@pytest.mark.skipif(not REF_DUMP.exists(), reason="reference converter not built here")
+def test_changed_weights_match_reference(tools, tmp_path):
+    """A changed-weight checkpoint (check_checkpoint.py's second case) converts like the
+    reference's converter does, record for record."""
+    from lasp_b200 import checkpoint
+    model = checkpoint.build_model(11, torch.float32)
+    with torch.no_grad():
+        model.node_embedding.linear.weight[0] += 0.125
+        model.interactions[1].conv_tp_weights.net[3].weight[2, 5] -= 0.5
+    path = checkpoint.save(model, tmp_path / "changed.model")
+    for head in ("matpes_r2scan", "synthetic_scan"):
+        assert convert(path, tmp_path / "a.pwm", head)[0] == 0
+        assert convert(path, tmp_path / "b.pwm", head, REF_DUMP)[0] == 0
+        a, b = records((tmp_path / "a.pwm").read_bytes()), records((tmp_path / "b.pwm").read_bytes())
+        assert a.keys() == b.keys()
+        for key in a:
+            assert a[key] == b[key], key
+
+
+def broken(kind):
+    """A checkpoint with one defect, and the converter message it must produce."""
+    from lasp_b200 import checkpoint
+    m = checkpoint.build_model(3, torch.float32)
+    if kind == "heads":
+        m.heads = m.heads[:5]
+        return m, "expected six-head MH1 architecture"
+    if kind == "nonfinite":
+        with torch.no_grad():
+            m.interactions[0].linear_up.weight[7] = float("nan")
+        return m, "nonfinite tensor value"
+    if kind == "eps":
+        m.interactions[0].conv_tp_weights.net[1].eps = 1e-6
+        return m, "radial LayerNorm epsilon"
+    if kind == "connection":
+        inst = m.interactions[1].conv_tp.instructions
+        inst[2] = inst[2]._replace(connection_mode="uuu")
+        return m, "tensor product connectivity"
+    if kind == "gate":
+        m.interactions[1].equivariant_nonlin.act_gates.acts[0].cst = 1.5
+        return m, "different gate normalization"
+    if kind == "cutoff":
+        m.radial_embedding.apply_cutoff = True
+        return m, "radial cutoff"
+    if kind == "root":
+        return m.interactions[0], "expected ScaleShiftMACE"
+    raise ValueError(kind)
+
+
+@pytest.mark.parametrize("kind", ["heads", "nonfinite", "eps", "connection", "gate", "cutoff", "root"])
+def test_conversion_errors(tools, tmp_path, kind):
+    from lasp_b200 import checkpoint
+    model, message = broken(kind)
+    path = checkpoint.save(model, tmp_path / "bad.model")
+    rc, err = convert(path, tmp_path / "o.pwm")
+    assert rc == 1 and message in err, err
+    if REF_DUMP.exists():
+        rc_ref, err_ref = convert(path, tmp_path / "r.pwm", tool=REF_DUMP)
+        assert rc_ref == 1 and err_ref == err
+
+
+def test_head_rules(tools, checkpoints, archive_path, tmp_path):
+    rc, err = convert(checkpoints["float32"], tmp_path / "o.pwm", "no_such_head")
+    assert rc == 1 and "unknown head: no_such_head" in err
+    rc, err = convert(archive_path, tmp_path / "o.pwm", "matpes_r2scan")
+    assert rc == 1 and "head selection requires an original checkpoint" in err
+    rc, err = convert(archive_path, tmp_path / "o.pwm")
+    assert rc == 0 and (tmp_path / "o.pwm").read_bytes() == archive_path.read_bytes()
+    assert run(DUMP).returncode == 1
+
+
+def test_cg_table_matches_reference_constants():
+    """The converter's compiled coupling table equals e3nn 0.4.4's float32 constants, row for row."""
+    import re
+    text = (ROOT / "lasp-pis_b200" / "csrc" / "mace" / "cg_table.h").read_text()
+    rows = re.findall(r"\{(\d), (\d), (\d), (\d), (\d), (\d), (\S+)f\}", text)
+    ref = [line.split() for line in (GOLDEN / "cg_e3nn044.txt").read_text().splitlines() if line.strip()]
+    assert len(rows) == len(ref)
+    for mine, theirs in zip(rows, ref):
+        assert mine[:6] == tuple(theirs[:6])
+        assert np.float32(float.fromhex(mine[6])) == np.float32(float(theirs[6]))

@@ -188,3 +188,41 @@ def test_cli_matches_reference(library, archive_path, tmp_path):
     out = tmp_path / "out.txt"
     r = subprocess.run([str(exe), str(archive_path), str(arc), "--output", str(out)], capture_output=True, text=True)
     assert r.returncode == 0 and "Energy (eV)" in out.read_text()
+
+
+def test_checkpoint_route(library, tmp_path):
+    """An MH1 PyTorch ZIP checkpoint loads through mace_create_mh1_head and the
+    device-binding constructor, evaluates bit for bit like the archive the converter writes
+    for the same head, and that archive matches the float64 oracle.  The CLI accepts the
+    checkpoint with --head and names the head on stderr; unknown heads are errors.  (The
+    converter itself is pinned byte for byte against the reference's in test_checkpoint.py.)
+    Oracle bounds are 3x check_close's: this random model's forces and virial are 4-7x
+    smaller than the synthetic archive's, so the same absolute float32 error is a larger
+    fraction of them."""
+    import torch
+    from lasp_b200 import checkpoint
+    from mace_inference import NativeMH1
+    ckpt = checkpoint.write_checkpoint(tmp_path / "mh1.model", 5, torch.float32)
+    head = "synthetic_scan"
+    pwm = tmp_path / "mh1.pwm"
+    dump = ROOT / "lasp-pis_b200" / "bin" / "mace-weights-dump"
+    subprocess.run([str(dump), str(ckpt), str(pwm), head], check=True)
+    s = structures.load("C1", DATA)
+    with NativeMH1(ckpt, head=head, library=library) as a, NativeMH1(pwm, library=library) as b, \
+            NativeMH1(ckpt, head=head, device=0, library=library) as c, NativeMH1(ckpt, library=library) as d:
+        ra, rb, rc, rd = (m.calculate(s.positions, s.numbers, s.cell) for m in (a, b, c, d))
+    for r in (ra, rc):
+        assert r["energy"] == rb["energy"]
+        for k in ("energies", "forces", "virial"):
+            assert np.array_equal(r[k], rb[k]), k
+    assert rd["energy"] != ra["energy"]  # the default head (matpes_r2scan) has its own e0 and scale
+    check_close(ra, O.Oracle(pwm).calculate(s.positions, s.numbers, s.cell), fscale=3.0)
+    with pytest.raises(RuntimeError, match="unknown head: no_such_head"):
+        NativeMH1(ckpt, head="no_such_head", library=library)
+    arc = tmp_path / "C1.arc"
+    structures.write_arc(arc, [s])
+    exe = ROOT / "lasp-pis_b200" / "bin" / "mace-main"
+    r = subprocess.run([str(exe), str(ckpt), str(arc), "--head", head, "--json"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    assert f"MACE head: {head}" in r.stderr
+    assert json.loads(r.stdout)["energy"] == pytest.approx(ra["energy"], rel=1e-6)
