@@ -192,13 +192,14 @@ def test_cli_matches_reference(library, archive_path, tmp_path):
 
 def test_checkpoint_route(library, tmp_path):
     """An MH1 PyTorch ZIP checkpoint loads through mace_create_mh1_head and the
-    device-binding constructor, evaluates bit for bit like the archive the converter writes
-    for the same head, and that archive matches the float64 oracle.  The CLI accepts the
-    checkpoint with --head and names the head on stderr; unknown heads are errors.  (The
-    converter itself is pinned byte for byte against the reference's in test_checkpoint.py.)
-    Oracle bounds are 3x check_close's: this random model's forces and virial are 4-7x
-    smaller than the synthetic archive's, so the same absolute float32 error is a larger
-    fraction of them."""
+    device-binding constructor and evaluates like the archive the converter writes for the
+    same head: energies bit for bit, forces and virial up to the ordering of the layer-1
+    up-gradient atomics (which differs between handles), and that archive matches the
+    float64 oracle.  The CLI accepts the checkpoint with --head and names the head on
+    stderr; unknown heads are errors.  (The converter itself is pinned byte for byte against
+    the reference's in test_checkpoint.py.)  Oracle bounds are 3x check_close's: this random
+    model's forces and virial are 4-7x smaller than the synthetic archive's, so the same
+    absolute float32 error is a larger fraction of them."""
     import torch
     from lasp_b200 import checkpoint
     from mace_inference import NativeMH1
@@ -211,10 +212,12 @@ def test_checkpoint_route(library, tmp_path):
     with NativeMH1(ckpt, head=head, library=library) as a, NativeMH1(pwm, library=library) as b, \
             NativeMH1(ckpt, head=head, device=0, library=library) as c, NativeMH1(ckpt, library=library) as d:
         ra, rb, rc, rd = (m.calculate(s.positions, s.numbers, s.cell) for m in (a, b, c, d))
+    fmax, wmax = max(1.0, float(np.abs(rb["forces"]).max())), float(np.abs(rb["virial"]).max())
     for r in (ra, rc):
         assert r["energy"] == rb["energy"]
-        for k in ("energies", "forces", "virial"):
-            assert np.array_equal(r[k], rb[k]), k
+        assert np.array_equal(r["energies"], rb["energies"])
+        assert float(np.abs(r["forces"] - rb["forces"]).max()) <= 1e-6 * fmax
+        assert float(np.abs(r["virial"] - rb["virial"]).max()) <= 1e-6 * wmax
     assert rd["energy"] != ra["energy"]  # the default head (matpes_r2scan) has its own e0 and scale
     check_close(ra, O.Oracle(pwm).calculate(s.positions, s.numbers, s.cell), fscale=3.0)
     with pytest.raises(RuntimeError, match="unknown head: no_such_head"):
