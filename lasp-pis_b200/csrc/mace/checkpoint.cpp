@@ -257,16 +257,29 @@ size_t Tensor::count() const {
   return n;
 }
 
+namespace {
+template <class T> double widen(const char *p) {
+  T x;
+  std::memcpy(&x, p, sizeof(T));
+  return double(x);
+}
+} // namespace
+
 std::vector<double> Tensor::values() const {
   if (!storage || shape.size() != stride.size() || shape.size() > 8 || offset < 0)
     fail("invalid tensor metadata");
   size_t width;
-  if (dtype == "DoubleStorage" || dtype == "LongStorage")
-    width = 8;
-  else if (dtype == "FloatStorage" || dtype == "IntStorage")
-    width = 4;
+  double (*read)(const char *);
+  if (dtype == "FloatStorage")
+    width = 4, read = widen<float>;
+  else if (dtype == "DoubleStorage")
+    width = 8, read = widen<double>;
+  else if (dtype == "LongStorage")
+    width = 8, read = widen<int64_t>;
+  else if (dtype == "IntStorage")
+    width = 4, read = widen<int32_t>;
   else if (dtype == "BoolStorage" || dtype == "ByteStorage")
-    width = 1;
+    width = 1, read = widen<uint8_t>;
   else
     fail("unsupported tensor dtype " + dtype);
   uint64_t total = 1;
@@ -276,48 +289,45 @@ std::vector<double> Tensor::values() const {
       fail("invalid tensor shape or stride");
     total *= uint64_t(shape[d]);
   }
-  const uint64_t slots = storage->size() / width;
   std::vector<double> out(static_cast<size_t>(total));
-  // Odometer over the shape: idx holds the current coordinates, at the element offset.
-  std::vector<int64_t> idx(shape.size(), 0);
-  for (uint64_t i = 0; i < total; ++i) {
-    uint64_t at = uint64_t(offset);
-    for (size_t d = 0; d < shape.size(); ++d) {
-      const uint64_t c = uint64_t(idx[d]);
-      if (c && uint64_t(stride[d]) > (std::numeric_limits<uint64_t>::max() - at) / c)
-        fail("tensor offset overflow");
-      at += c * uint64_t(stride[d]);
-    }
-    if (at >= slots)
-      fail("tensor exceeds storage");
-    const char *p = storage->data() + at * width;
-    double v;
-    if (dtype == "FloatStorage") {
-      float f;
-      std::memcpy(&f, p, 4);
-      v = f;
-    } else if (dtype == "DoubleStorage") {
-      std::memcpy(&v, p, 8);
-    } else if (dtype == "LongStorage") {
-      int64_t q;
-      std::memcpy(&q, p, 8);
-      v = double(q);
-    } else if (dtype == "IntStorage") {
-      int32_t q;
-      std::memcpy(&q, p, 4);
-      v = q;
-    } else {
-      v = uint8_t(*p);
-    }
-    if (!std::isfinite(v))
-      fail("nonfinite tensor value");
-    out[size_t(i)] = v;
-    for (size_t d = shape.size(); d-- > 0;) {
-      if (++idx[d] < shape[d])
-        break;
-      idx[d] = 0;
+  if (total == 0)
+    return out;
+  // Strides are non-negative, so the last element of the view is the farthest one: bound it
+  // once instead of every element.
+  uint64_t last = uint64_t(offset);
+  for (size_t d = 0; d < shape.size(); ++d) {
+    const uint64_t c = uint64_t(shape[d] - 1);
+    if (c && uint64_t(stride[d]) > (std::numeric_limits<uint64_t>::max() - last) / c)
+      fail("tensor offset overflow");
+    last += c * uint64_t(stride[d]);
+  }
+  if (last >= storage->size() / width)
+    fail("tensor exceeds storage");
+  const char *base = storage->data() + size_t(offset) * width;
+  bool dense = true;
+  for (size_t d = shape.size(), step = 1; d-- > 0; step *= size_t(shape[d]))
+    dense = dense && (shape[d] == 1 || size_t(stride[d]) == step);
+  if (dense) {
+    for (size_t i = 0; i < out.size(); ++i)
+      out[i] = read(base + i * width);
+  } else {
+    // Odometer over the shape, tracking the element offset incrementally.
+    std::vector<int64_t> idx(shape.size(), 0);
+    uint64_t at = 0;
+    for (size_t i = 0; i < out.size(); ++i) {
+      out[i] = read(base + at * width);
+      for (size_t d = shape.size(); d-- > 0;) {
+        at += uint64_t(stride[d]);
+        if (++idx[d] < shape[d])
+          break;
+        at -= uint64_t(stride[d]) * uint64_t(shape[d]);
+        idx[d] = 0;
+      }
     }
   }
+  for (double v : out)
+    if (!std::isfinite(v))
+      fail("nonfinite tensor value");
   return out;
 }
 

@@ -174,10 +174,15 @@ void emit_linear(Records &ar, const std::string &name, const NodeRef &m, const s
                                int(c.size()), bi.dim(), int(packed.size())});
     const double path_weight = inst->item(3)->number;
     for (int a : r)
-      for (int b : c) {
-        need(a >= 0 && a < bi.mul && b >= 0 && b < bo.mul, "head index");
-        packed.push_back(w[consumed + size_t(a) * size_t(bo.mul) + size_t(b)] * path_weight);
-      }
+      need(a >= 0 && a < bi.mul, "head index");
+    for (int b : c)
+      need(b >= 0 && b < bo.mul, "head index");
+    packed.reserve(packed.size() + r.size() * c.size());
+    for (int a : r) {
+      const double *row = &w[consumed + size_t(a) * size_t(bo.mul)];
+      for (int b : c)
+        packed.push_back(row[b] * path_weight);
+    }
     consumed += block;
   }
   need(consumed == w.size(), "unconsumed linear weights");
