@@ -92,11 +92,13 @@ class Records {
 public:
   void floats(const std::string &name, const std::vector<double> &v) {
     std::string bytes(v.size() * 4, '\0');
+    bool finite = true;
     for (size_t i = 0; i < v.size(); ++i) {
       const float f = float(v[i]);
-      need(std::isfinite(v[i]) && std::isfinite(f), "nonfinite " + name);
+      finite = finite && std::isfinite(v[i]) && std::isfinite(f);
       std::memcpy(&bytes[i * 4], &f, 4);
     }
+    need(finite, "nonfinite " + name);
     add(name, std::move(bytes));
   }
   void ints(const std::string &name, const std::vector<int> &v) {
