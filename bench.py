@@ -17,6 +17,10 @@ e2e    the reference-facing C ABI (mace_calculate) with host buffers: the host-t
 --impl reference   the reference's own implementation of this path -- its CUDA build
        compiled from its sources (oracle/_ref/libmace_ref.so) -- through its C ABI on the
        same config, on rank 0; falls back to the float64 CPU oracle if that build is absent.
+--host  host-side input work instead (no GPU): ARC reads of C1, C2, C3 and C5 and the
+       conversion of the seeded synthetic MH1 checkpoint, each the median of --steps runs on
+       one pinned core (bin/mace-host-bench; with --impl reference the reference's own
+       chemio and converter code, oracle/_ref/host-bench-ref).
 """
 from __future__ import annotations
 
@@ -291,6 +295,45 @@ def c4_ours(args, archive, rank, local, world):
         torch.distributed.destroy_process_group()
 
 
+def host_arm(args):
+    """One JSON line of host-side input timings (rank 0 only; no GPU)."""
+    import tempfile
+    import torch
+    from lasp_b200 import checkpoint, structures
+    if args.impl == "reference":
+        exe = ROOT / "oracle" / "_ref" / "host-bench-ref"
+        if not exe.exists():
+            print(json.dumps({"impl": "reference", "unavailable": "reference host tools absent (oracle/_ref)"}))
+            return
+    else:
+        exe = ROOT / "lasp-pis_b200" / "bin" / "mace-host-bench"
+        if not exe.exists():
+            raise SystemExit("mace-host-bench is not built: run __graft_entry__.build() (make -C lasp-pis_b200)")
+    pin = ["taskset", "-c", str(min(os.sched_getaffinity(0)))] if subprocess.run(
+        ["which", "taskset"], capture_output=True).returncode == 0 else []
+    steps = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        jobs = []
+        for name in ("C1", "C2", "C3", "C5"):
+            path = Path(tmp) / f"{name}.arc"
+            structures.write_arc(path, [structures.load(name, DATA)])
+            jobs.append((f"arc_{name}", "arc", path))
+        model = checkpoint.write_checkpoint(Path(tmp) / "mh1.model", checkpoint.SEED, torch.float64)
+        jobs.append(("convert_checkpoint", "convert", model))
+        for key, step, path in jobs:
+            r = subprocess.run(pin + [str(exe), step, str(path), str(args.steps)], capture_output=True, text=True,
+                               check=True)
+            steps[key] = json.loads(r.stdout)
+    cpu = next((line.split(":", 1)[1].strip() for line in Path("/proc/cpuinfo").read_text().splitlines()
+                if line.startswith("model name")), "unknown")
+    print(json.dumps({"impl": args.impl, "metric": "host input work (ARC read, MH1 checkpoint conversion)",
+                      "unit": "ms", "higher_is_better": False, "cores": 1, "pinned": bool(pin), "cpu": cpu,
+                      "nproc": os.cpu_count(), "repeat": args.steps,
+                      "steps": {k: {"median_ms": v["median_ms"], "min_ms": v["min_ms"], "units": v["units"]}
+                                for k, v in steps.items()},
+                      "data": "synthetic (C1-C5 ARC files; seeded torch.save MH1-shaped checkpoint, 54 MB float64)"}))
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -302,8 +345,14 @@ def main():
     ap.add_argument("--decompose", action="store_true",
                     help="one structure split across the GPUs (spatial domain decomposition, strong scaling) "
                          "instead of one structure per GPU")
+    ap.add_argument("--host", action="store_true",
+                    help="time the host-side input work (ARC reads, checkpoint conversion) instead; no GPU")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.host:
+        if int(os.environ.get("RANK", 0)) == 0:
+            host_arm(args)
+        return
     rank = int(os.environ.get("RANK", 0))
     local = int(os.environ.get("LOCAL_RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

@@ -7,8 +7,10 @@
 #include <cctype>
 #include <cmath>
 #include <fstream>
+#include <iterator>
 #include <sstream>
 #include <stdexcept>
+#include <unordered_map>
 
 namespace mace {
 namespace {
@@ -19,13 +21,45 @@ const char *const kSymbols =
     "Cn Nh Fl Mc Lv Ts Og";
 
 int atomic_number(const std::string &symbol) {
-  std::istringstream in(kSymbols);
-  std::string s;
-  for (int z = 1; in >> s; ++z)
-    if (s == symbol)
-      return z;
-  return 0;
+  static const std::unordered_map<std::string, int> table = [] {
+    std::unordered_map<std::string, int> t;
+    std::istringstream in(kSymbols);
+    std::string s;
+    for (int z = 1; in >> s; ++z)
+      t.emplace(s, z);
+    return t;
+  }();
+  auto it = table.find(symbol);
+  return it == table.end() ? 0 : it->second;
 }
+
+// The whitespace operator>> skips in the C locale.
+bool blank(char c) { return c == ' ' || c == '\t' || c == '\n' || c == '\v' || c == '\f' || c == '\r'; }
+
+// Whitespace-separated fields of one line, reusing the strings' storage between lines.
+struct Fields {
+  std::vector<std::string> word;
+  size_t count = 0;
+  void split(const std::string &line) {
+    count = 0;
+    for (size_t i = 0, n = line.size();;) {
+      while (i < n && blank(line[i]))
+        ++i;
+      if (i == n)
+        return;
+      size_t j = i;
+      while (j < n && !blank(line[j]))
+        ++j;
+      if (count == word.size())
+        word.emplace_back();
+      word[count++].assign(line, i, j - i);
+      i = j;
+    }
+  }
+  const std::string &operator[](size_t k) const { return word[k]; }
+  size_t size() const { return count; }
+  bool empty() const { return count == 0; }
+};
 
 double parse_number(const std::string &s) {
   std::size_t used = 0;
@@ -57,21 +91,26 @@ std::vector<ArcFrame> read_arc(const std::string &path) {
   std::transform(ext.begin(), ext.end(), ext.begin(), [](unsigned char ch) { return char(std::tolower(ch)); });
   if (ext != ".arc")
     throw std::runtime_error("unsupported structure format: " + ext + " (supported: .arc)");
-  std::ifstream in(path);
+  std::ifstream in(path, std::ios::binary);
   if (!in)
     throw std::runtime_error("cannot open structure: " + path);
+  // The whole file at once, then '\n'-separated lines as getline would return them.
+  const std::string text((std::istreambuf_iterator<char>(in)), std::istreambuf_iterator<char>());
+  if (in.bad())
+    throw std::runtime_error("error reading structure: " + path);
   std::vector<ArcFrame> frames;
   ArcFrame cur;
   bool periodic = false, have_cell = false, first_end = false, pending = false;
   std::string line;
+  Fields f;
   std::size_t lineno = 0;
-  while (std::getline(in, line)) {
+  for (size_t at = 0; at < text.size();) {
+    const size_t eol = std::min(text.find('\n', at), text.size());
+    line.assign(text, at, eol - at);
+    at = eol + 1;
     ++lineno;
     try {
-      std::istringstream words(line);
-      std::vector<std::string> f;
-      for (std::string w; words >> w;)
-        f.push_back(w);
+      f.split(line);
       if (f.empty() || f[0][0] == '!')
         continue;
       if (f[0] == "PBC=ON" || f[0] == "PBC=OFF") {
@@ -127,8 +166,6 @@ std::vector<ArcFrame> read_arc(const std::string &path) {
       throw std::runtime_error(path + ":" + std::to_string(lineno) + ": " + e.what());
     }
   }
-  if (in.bad())
-    throw std::runtime_error("error reading structure: " + path);
   if (pending || have_cell || first_end)
     throw std::runtime_error(path + ": incomplete ARC frame");
   if (frames.empty())
