@@ -18,8 +18,21 @@ class MH1Calculator(Calculator):
     def close(self):
         if getattr(self, "native", None):
             self.native.close()
+            self.native = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *args):
+        self.close()
+
+    def __del__(self):
+        self.close()
 
     def evaluate(self, atoms):
+        """Always execute, bypassing ASE's geometry cache (for trajectory replay)."""
+        if not getattr(self, "native", None):
+            raise RuntimeError("Calculator is closed")
         if not np.all(atoms.pbc):
             raise ValueError("v1 requires three periodic axes")
         r = self.native.calculate(atoms.positions, atoms.numbers, atoms.cell.array)
