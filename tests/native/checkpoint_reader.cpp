@@ -4,11 +4,15 @@
 //   checkpoint-reader ZIP       the fixture must open and its data.pkl decode to None; then
 //                               inert reducers, malformed pickles and strided views are checked
 //   checkpoint-reader --open F  only open F and decode its root (exit 1 if rejected)
+//   checkpoint-reader --tensors F   the root's class, then every tensor reachable through the
+//                               module tree: "name [d0,d1,...] first-value" per line
+//                               (what the reference's checkpoint_inspect prints)
 //
 // Prints one line on success; exits 1 with the error otherwise.
 #include "checkpoint.hpp"
 
 #include <cstring>
+#include <iomanip>
 #include <iostream>
 #include <stdexcept>
 #include <string>
@@ -37,8 +41,22 @@ int main(int argc, char **argv) {
       mace::ckpt::load(zip);
       return 0;
     }
+    if (argc == 3 && std::string(argv[1]) == "--tensors") {
+      mace::ckpt::Zip zip{std::string(argv[2])};
+      auto root = mace::ckpt::load(zip);
+      auto all = mace::ckpt::tensors(root);
+      std::cout << std::setprecision(17) << root->text << " " << all.size() << " tensors\n";
+      for (const auto &[name, t] : all) {
+        auto v = t.values();
+        std::cout << name << " [";
+        for (auto d : t.shape)
+          std::cout << d << ",";
+        std::cout << "] " << (v.empty() ? 0.0 : v[0]) << "\n";
+      }
+      return 0;
+    }
     if (argc != 2)
-      throw std::runtime_error("usage: checkpoint-reader ZIP | --open FILE");
+      throw std::runtime_error("usage: checkpoint-reader ZIP | --open FILE | --tensors FILE");
     mace::ckpt::Zip zip{std::string(argv[1])};
     require(mace::ckpt::load(zip)->kind == Node::None, "fixture root is None");
 

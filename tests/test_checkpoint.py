@@ -126,6 +126,28 @@ def test_torch_save_decodes(tools, tmp_path):
     assert r.returncode == 0, r.stderr
 
 
+def test_module_tree_tensors_match_state_dict(tools, tmp_path):
+    """Every parameter and buffer reachable through _parameters / _buffers / _modules, with
+    torch's state_dict names, shapes and values (the reference's checkpoint_inspect view)."""
+    from lasp_b200 import checkpoint
+    _, reader = tools
+    model = checkpoint.build_model(9, torch.float32)
+    path = checkpoint.save(model, tmp_path / "m.model")
+    r = run(reader, "--tensors", path)
+    assert r.returncode == 0, r.stderr
+    head, *lines = r.stdout.splitlines()
+    state = model.state_dict()
+    assert head == f"mace.modules.models ScaleShiftMACE {len(state)} tensors"
+    seen = {}
+    for line in lines:
+        name, shape, first = line.split(" ")
+        seen[name] = ([int(d) for d in shape.strip("[]").split(",") if d], float(first))
+    assert seen.keys() == state.keys()
+    for name, t in state.items():
+        assert seen[name][0] == list(t.shape), name
+        assert seen[name][1] == (float(t.flatten()[0]) if t.numel() else 0.0), name
+
+
 # ---------------------------------------------------------------------------- converter
 
 def records(data: bytes):
