@@ -52,7 +52,7 @@ UNIT = "atoms*evals/s"
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 # DRAM read + write bytes per edge of the roofline kernel, from an ncu capture of the C2
-# workload (profiles/edge_backward1_C2.md: 1.0523 GB read + 9.95 MB written over 97,006
+# workload (edge_proj_kernel<1, backward>: 1.0523 GB read + 9.95 MB written over 97,006
 # edges), scaled by the edge count.
 TRAFFIC_PER_EDGE = (1.052328e9 + 9.952512e6) / 97006
 
