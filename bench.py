@@ -159,6 +159,8 @@ def reference_arm(args, archive, structure):
     lib.mace_last_error.restype = ct.c_char_p
     lib.mace_calculate.argtypes = [ct.c_void_p, ct.c_int] + [ct.c_void_p] * 7
     lib.mace_destroy.argtypes = [ct.c_void_p]
+    lib.mace_diagnostics.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_size_t]
+    lib.mace_diagnostics.restype = ct.c_int
     h = lib.mace_create_mh1(str(archive).encode(), 0)
     if not h:
         print(json.dumps({"impl": "reference", "unavailable": lib.mace_last_error().decode()}))
@@ -172,20 +174,32 @@ def reference_arm(args, archive, structure):
     ptrs = [x.ctypes.data for x in (s.positions, s.numbers, s.cell, e, a, f, v)]
     for _ in range(args.warmup):
         assert lib.mace_calculate(h, n, *ptrs) == 0, lib.mace_last_error()
-    times = []
-    for _ in range(args.steps):
-        t = time.perf_counter()
-        assert lib.mace_calculate(h, n, *ptrs) == 0
-        times.append(time.perf_counter() - t)
+    times, device = [], []
+    diag = ct.create_string_buffer(1 << 16)
+    with ClockSampler(0) as clocks:
+        for _ in range(args.steps):
+            t = time.perf_counter()
+            assert lib.mace_calculate(h, n, *ptrs) == 0
+            times.append(time.perf_counter() - t)
+            # The reference's own CUDA-event time of the call (lapis/src/runtime.cu:287), read
+            # outside the timed window.
+            if lib.mace_diagnostics(h, diag, len(diag)) == 0:
+                try:
+                    device.append(float(json.loads(diag.value)["device_ms"]))
+                except (ValueError, KeyError):
+                    pass
     lib.mace_destroy(h)
     total = float(np.sum(times))
     value = n * args.steps / total
     line = {"impl": "reference", "metric": metric_for(args.config), "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "C3: 10,000-atom perturbed FCC cube, 46.4 A, cutoff 6 A", "atoms": n,
+            "config": {"workload": f"{args.config}: {WORKLOADS.get(args.config, args.config)}, cutoff 6 A",
+                       "atoms": n,
                        "implementation": "reference CUDA build (LipidL/LASP-PIS libmace) compiled for sm_100a from "
                                          "its sources, called through its C ABI with host buffers"},
+            "reference_device_ms": float(np.median(device)) if device else None,
+            "clocks": clocks.summary(),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": 1, "kind": "reference",
                              "sample": "full C3 workload per step; the reference has no CPU inference path, its "
                                        "host code (prepare/finish) is single-threaded and the model runs on one B200"},
@@ -212,6 +226,8 @@ def c4_reference(args, archive):
     lib.mace_last_error.restype = ct.c_char_p
     lib.mace_calculate.argtypes = [ct.c_void_p, ct.c_int] + [ct.c_void_p] * 7
     lib.mace_destroy.argtypes = [ct.c_void_p]
+    lib.mace_diagnostics.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_size_t]
+    lib.mace_diagnostics.restype = ct.c_int
     h = lib.mace_create_mh1(str(archive).encode(), 0)
     e = np.zeros(1)
     v = np.zeros((3, 3), np.float32)
