@@ -113,3 +113,21 @@ def test_config_files_parse_like_reference(tool, tmp_path):
         assert np.allclose(np.array(mine["positions"]).reshape(-1, 3), s.positions, atol=1e-5)
         if REF.exists():
             assert dump(REF, path) == (0, mine)
+
+
+def test_bench_host_mode(tool):
+    """bench.py --host prints one JSON line with every host step for this build's arm and, with
+    --impl reference, for the reference's (when its tools are built)."""
+    import sys
+    for impl in ("ours", "reference"):
+        r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--host", "--steps", "2", "--impl", impl],
+                           capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stderr
+        line = json.loads(r.stdout.strip().splitlines()[-1])
+        if impl == "reference" and "unavailable" in line:
+            continue
+        assert line["impl"] == impl and line["unit"] == "ms" and line["higher_is_better"] is False
+        assert set(line["steps"]) == {"arc_C1", "arc_C2", "arc_C3", "arc_C5", "convert_checkpoint"}
+        assert line["steps"]["arc_C5"]["units"] == 198904
+        assert line["steps"]["convert_checkpoint"]["units"] == 25621837
+        assert all(v["median_ms"] > 0 for v in line["steps"].values())
