@@ -280,3 +280,14 @@ def test_cg_table_matches_reference_constants():
     for mine, theirs in zip(rows, ref):
         assert mine[:6] == tuple(theirs[:6])
         assert np.float32(float.fromhex(mine[6])) == np.float32(float(theirs[6]))
+
+
+def test_generated_tables_are_current(tmp_path):
+    """The compiled tables (coupling constants, tensor-product and product-basis layouts)
+    equal what their generators produce now."""
+    import sys
+    gen = ROOT / "lasp-pis_b200" / "csrc" / "mace"
+    for script, header in (("gen_cg_table.py", "cg_table.h"), ("gen_tp_table.py", "tp_table.h"),
+                           ("gen_product_table.py", "product_table.h")):
+        subprocess.run([sys.executable, str(gen / script), str(tmp_path)], check=True)
+        assert (tmp_path / header).read_text() == (gen / header).read_text(), header
