@@ -54,6 +54,26 @@ const NodeRef &Node::field(const std::string &key) const {
   return it->second;
 }
 
+Node::~Node() {
+  std::vector<NodeRef> pending;
+  auto detach = [&pending](Node &n) {
+    for (auto &x : n.items)
+      pending.push_back(std::move(x));
+    n.items.clear();
+    for (auto &kv : n.fields)
+      pending.push_back(std::move(kv.second));
+    n.fields.clear();
+  };
+  detach(*this);
+  while (!pending.empty()) {
+    NodeRef x = std::move(pending.back());
+    pending.pop_back();
+    // Only the last owner empties a node; its release below then has nothing nested left.
+    if (x && x.use_count() == 1)
+      detach(*x);
+  }
+}
+
 int64_t Node::integer() const {
   // Exactly representable integers only (|x| < 2^53).
   if (kind != Number || !std::isfinite(number) || std::trunc(number) != number ||

@@ -54,6 +54,13 @@ struct Node {
   const NodeRef &item(size_t i) const;
   const NodeRef &field(const std::string &key) const;
   int64_t integer() const; // exact integers only
+
+  Node() = default;
+  Node(const Node &) = default;
+  Node &operator=(const Node &) = default;
+  // Releases nested values iteratively: a pickle can nest containers far deeper than the
+  // call stack would allow a recursive release to go.
+  ~Node();
 };
 
 class Zip {

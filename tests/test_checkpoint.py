@@ -116,6 +116,22 @@ def test_zip_reader_rejects_unsupported(tools, tmp_path):
     assert "little-endian" in run(reader, "--open", path).stderr
 
 
+def test_deep_and_cyclic_pickles(tools, tmp_path):
+    """200,000 nested lists and a list that contains itself decode and are released without
+    exhausting the call stack (the reference's recursive release overflows it on the first)."""
+    _, reader = tools
+    n = 200000
+    for name, pickle in (("deep", b"\x80\x02" + b"]" * n + b"a" * (n - 1) + b"."),
+                         ("cycle", b"\x80\x02]q\x00h\x00a.")):
+        path = tmp_path / f"{name}.zip"
+        with zipfile.ZipFile(path, "w") as z:
+            z.writestr("archive/data.pkl", pickle)
+        r = run(reader, "--open", path)
+        assert r.returncode == 0, (name, r.returncode, r.stderr)
+        r = run(DUMP, path, tmp_path / "o.pwm")
+        assert r.returncode == 1 and "unsupported MH1 checkpoint" in r.stderr, (name, r.stderr)
+
+
 def test_torch_save_decodes(tools, tmp_path):
     """A plain torch.save file (parameters, buffers, OrderedDicts, sets, memo references)."""
     _, reader = tools
