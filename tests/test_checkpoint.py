@@ -307,3 +307,38 @@ def test_generated_tables_are_current(tmp_path):
                            ("gen_product_table.py", "product_table.h")):
         subprocess.run([sys.executable, str(gen / script), str(tmp_path)], check=True)
         assert (tmp_path / header).read_text() == (gen / header).read_text(), header
+
+
+def test_mutated_checkpoints_fail_cleanly(tools, tmp_path):
+    """Seeded byte mutations of a torch.save file -- inside its pickle (re-zipped with valid
+    checksums) and in the raw ZIP -- are either decoded or rejected with an error: the
+    reader never crashes on them."""
+    import random
+    _, reader = tools
+    buf = io.BytesIO()
+    torch.save(torch.nn.Sequential(torch.nn.Linear(3, 4), torch.nn.LayerNorm(4)), buf)
+    data = buf.getvalue()
+    src = zipfile.ZipFile(io.BytesIO(data))
+    names = src.namelist()
+    pkl_name = next(n for n in names if n.endswith("data.pkl"))
+    pkl = src.read(pkl_name)
+    rng = random.Random(2026)
+    path = tmp_path / "m.zip"
+    for it in range(300):
+        if it % 2 == 0:
+            p = bytearray(pkl)
+            for _ in range(rng.randint(1, 4)):
+                p[rng.randrange(len(p))] = rng.randrange(256)
+            out = io.BytesIO()
+            with zipfile.ZipFile(out, "w") as w:
+                for n in names:
+                    w.writestr(n, bytes(p) if n == pkl_name else src.read(n))
+            path.write_bytes(out.getvalue())
+        else:
+            p = bytearray(data)
+            for _ in range(rng.randint(1, 3)):
+                k = rng.randrange(len(p)) if rng.random() < 0.5 else len(p) - 1 - rng.randrange(600)
+                p[k] = rng.randrange(256)
+            path.write_bytes(bytes(p))
+        r = run(reader, "--open", path)
+        assert r.returncode in (0, 1), (it, r.returncode, r.stderr)
