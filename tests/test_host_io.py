@@ -131,3 +131,27 @@ def test_bench_host_mode(tool):
         assert line["steps"]["arc_C5"]["units"] == 198904
         assert line["steps"]["convert_checkpoint"]["units"] == 25621837
         assert all(v["median_ms"] > 0 for v in line["steps"].values())
+
+
+def test_mutated_arc_files_match_reference(tool, tmp_path):
+    """Seeded mutations of the C1 ARC file (digits, signs, separators, keywords, random
+    bytes): this build never crashes and, where the reference's reader is built, returns
+    exactly its result or its error message for every one."""
+    import random
+    from lasp_b200 import structures
+    base_path = tmp_path / "C1.arc"
+    structures.write_arc(base_path, [structures.load("C1", DATA)])
+    base = base_path.read_bytes()
+    rng = random.Random(3)
+    path = tmp_path / "m.arc"
+    for it in range(200):
+        p = bytearray(base)
+        for _ in range(rng.randint(1, 5)):
+            k = rng.randrange(len(p))
+            p[k] = rng.choice(b" \t\n\r0123456789.-+eEx!PBCORend") if rng.random() < 0.8 else rng.randrange(256)
+        path.write_bytes(bytes(p))
+        mine = subprocess.run([str(tool), "arc-dump", str(path), "0"], capture_output=True)
+        assert mine.returncode in (0, 1), (it, mine.returncode)
+        if REF.exists():
+            ref = subprocess.run([str(REF), "arc-dump", str(path), "0"], capture_output=True)
+            assert (mine.returncode, mine.stdout, mine.stderr) == (ref.returncode, ref.stdout, ref.stderr), it
