@@ -36,6 +36,11 @@ MACE_EXPORT int mace_diagnostics(void *handle, char *buffer, size_t capacity);
 /* Like mace_create_mh1 but binds the handle to CUDA device `device` (the reference binds
  * to whatever device is current at creation). */
 MACE_EXPORT void *mace_create_mh1_device(const char *archive, int backend, int device);
+/* Parses and validates a model (PWMH1001 archive, or an MH1 ZIP checkpoint converted for
+ * `head`; NULL or "" = "matpes_r2scan") exactly as the constructors do, in host memory: no
+ * GPU is needed.  Returns 0, or -1 with the constructor's error in mace_last_error.  No
+ * reference counterpart (the reference validates only while creating a handle). */
+MACE_EXPORT int mace_check_model(const char *model, const char *head);
 /* mace_create_mh1_head bound to CUDA device `device`. */
 MACE_EXPORT void *mace_create_mh1_device_head(const char *model, int backend, const char *head, int device);
 /* Spatial domain decomposition of one structure across `world` ranks (one process per GPU;

@@ -4,6 +4,7 @@
 // Handles remember the CUDA device they were created on and make it current per call.
 #include "mace/c_api.h"
 #include "mace/mh1.hpp"
+#include "model.hpp"
 #include <algorithm>
 #include <array>
 #include <cstring>
@@ -128,6 +129,20 @@ int calculate(void *handle, int n, const float *xyz, const int *z, const float *
 
 extern "C" {
 void *mace_create_mh1(const char *path, int b) { return mace_create_mh1_head(path, b, nullptr); }
+
+int mace_check_model(const char *path, const char *head) {
+  try {
+    error.clear();
+    if (!path)
+      throw Error("Null archive path");
+    mace::ModelData data;
+    data.validate(path, head ? head : "");
+    return 0;
+  } catch (const std::exception &e) {
+    error = e.what();
+    return -1;
+  }
+}
 
 void *mace_create_mh1_head(const char *path, int b, const char *head) {
   try {

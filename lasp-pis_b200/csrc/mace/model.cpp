@@ -25,16 +25,35 @@ using lapis::check;
 
 Device::~Device() {
   for (void *p : allocations)
-    cudaFree(p);
+    if (host_only)
+      std::free(p);
+    else
+      cudaFree(p);
 }
 
 float *Device::upload(const void *data, size_t bytes) {
   void *p = nullptr;
+  if (host_only) {
+    p = std::malloc(bytes ? bytes : 4);
+    if (!p)
+      throw Error("out of host memory");
+    allocations.push_back(p);
+    if (bytes)
+      std::memcpy(p, data, bytes);
+    return static_cast<float *>(p);
+  }
   check(cudaMalloc(&p, bytes ? bytes : 4));
   allocations.push_back(p);
   if (bytes)
     check(cudaMemcpy(p, data, bytes, cudaMemcpyHostToDevice));
   return static_cast<float *>(p);
+}
+
+void ModelData::validate(const std::string &path, const std::string &head) {
+  if (!device.allocations.empty())
+    throw Error("validate() needs a fresh model");
+  device.host_only = true;
+  load(path, head);
 }
 
 void split_tf32(const float *w, size_t count, float *hi, float *lo) {

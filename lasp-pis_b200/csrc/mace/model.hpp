@@ -65,6 +65,8 @@ struct Layer {
 
 struct Device {
   std::vector<void *> allocations;
+  // Validation without a GPU: uploads are copied into host memory instead.
+  bool host_only = false;
   ~Device();
   float *upload(const void *data, size_t bytes);
 };
@@ -82,6 +84,9 @@ struct ModelData {
   // `path` is a PWMH1001 archive (head must be empty) or an MH1 ZIP checkpoint, converted
   // for `head` ("matpes_r2scan" when empty).
   void load(const std::string &path, const std::string &head = {});
+  // Every parse and validation step of load() with host memory in place of the device, so
+  // a model can be checked where no GPU is present.
+  void validate(const std::string &path, const std::string &head = {});
 };
 
 // ---- kernels (edge_kernels.cu / node_kernels.cu) ----

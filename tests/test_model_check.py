@@ -1,0 +1,126 @@
+"""Model validation without a GPU: mace_check_model runs the loader's every parse and
+validation step (mace/src/mh1.cu:626-734 for archives, mace/src/weights.cpp:305-393 for
+checkpoints) in host memory.  Valid models pass; each defect gets the loader's own message;
+mutated archives are accepted or rejected but never crash the process.
+"""
+import ctypes as ct
+import struct
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+
+@pytest.fixture(scope="module")
+def lib(library):
+    lib = ct.CDLL(str(library))
+    lib.mace_check_model.argtypes = [ct.c_char_p, ct.c_char_p]
+    lib.mace_check_model.restype = ct.c_int
+    lib.mace_last_error.restype = ct.c_char_p
+    return lib
+
+
+def check(lib, path, head=None):
+    rc = lib.mace_check_model(str(path).encode(), None if head is None else head.encode())
+    return rc, lib.mace_last_error().decode()
+
+
+def test_valid_models_pass(lib, archive_path, tmp_path):
+    from lasp_b200 import checkpoint
+    assert check(lib, archive_path) == (0, "")
+    ckpt = checkpoint.write_checkpoint(tmp_path / "m.model", 4, torch.float32)
+    for head in (None, "synthetic_pbe", "synthetic_scan"):
+        assert check(lib, ckpt, head) == (0, "")
+    rc, err = check(lib, ckpt, "nope")
+    assert rc == -1 and err == "unsupported MH1 checkpoint: unknown head: nope"
+    rc, err = check(lib, archive_path, "matpes_r2scan")
+    assert rc == -1 and "head selection requires an original checkpoint" in err
+    rc, err = check(lib, tmp_path / "missing.pwm")
+    assert rc == -1 and err.startswith("Cannot open MH1 archive")
+
+
+def defects():
+    """(name, edit of the records or the bytes, expected message fragment)."""
+    def drop(key):
+        return lambda r: r.pop(key)
+
+    def setv(key, fn):
+        def edit(r):
+            r[key] = fn(r[key].copy())
+        return edit
+
+    def nan_at(a):
+        a[3] = np.nan
+        return a
+
+    return [
+        ("missing_embedding", drop("embedding"), "Invalid MH1 tensor size: embedding"),
+        ("linear_dims", setv("layer0.linear_up.dims", lambda a: a + 1), "Unsupported MH1 linear dimensions: layer0.linear_up"),
+        ("nonfinite", setv("layer1.linear_2.weight", nan_at), "Nonfinite MH1 tensor: layer1.linear_2.weight"),
+        ("constants", setv("constants", lambda a: a[:13]), "Unsupported MH1 constants"),
+        ("cutoff", setv("constants", lambda a: np.concatenate([[5.0], a[1:]])), "Unsupported MH1 constants"),
+        ("duplicate_z", setv("atomic_numbers", lambda a: np.concatenate([[a[1]], a[1:]])), "Invalid MH1 element map"),
+        ("path_bounds", setv("layer0.linear_res.paths", lambda a: np.concatenate([[a[0] + 10**6], a[1:]])),
+         "Invalid linear path: layer0.linear_res"),
+    ]
+
+
+@pytest.mark.parametrize("case", defects(), ids=lambda c: c[0])
+def test_defects_are_reported(lib, archive_path, tmp_path, case):
+    from lasp_b200 import archive
+    name, edit, message = case
+    records = archive.read(archive_path)
+    edit(records)
+    path = tmp_path / f"{name}.pwm"
+    archive.write(path, records)
+    rc, err = check(lib, path)
+    assert rc == -1 and message in err, err
+
+
+def test_malformed_files_are_reported(lib, archive_path, tmp_path):
+    blob = archive_path.read_bytes()
+    for name, data, message in (("magic", b"PWMH1002" + blob[8:], "Invalid MH1 archive magic"),
+                                ("truncated", blob[:len(blob) // 2], "Truncated MH1 archive"),
+                                ("count", blob[:8] + struct.pack("<I", 0) + blob[12:], "Invalid MH1 tensor count"),
+                                ("short", blob[:10], "")):
+        path = tmp_path / f"{name}.pwm"
+        path.write_bytes(data)
+        rc, err = check(lib, path)
+        assert rc == -1 and message in err, (name, err)
+
+
+MUTATE = r'''
+import ctypes as ct, random, struct, sys
+lib = ct.CDLL(sys.argv[1])
+lib.mace_check_model.argtypes = [ct.c_char_p, ct.c_char_p]
+lib.mace_last_error.restype = ct.c_char_p
+blob = open(sys.argv[2], "rb").read()
+heads, pos = [], 12
+for _ in range(struct.unpack_from("<I", blob, 8)[0]):
+    n, size = struct.unpack_from("<IQ", blob, pos)
+    heads.append((pos, 12 + n))
+    pos += 12 + n + size
+rng = random.Random(int(sys.argv[4]))
+accepted = 0
+for it in range(int(sys.argv[5])):
+    p = bytearray(blob)
+    for _ in range(rng.randint(1, 3)):
+        if rng.random() < 0.7:   # a record header: its name length, byte size or name
+            start, length = rng.choice(heads)
+            p[start + rng.randrange(length)] = rng.randrange(256)
+        else:
+            p[rng.randrange(len(p))] = rng.randrange(256)
+    open(sys.argv[3], "wb").write(p)
+    accepted += lib.mace_check_model(sys.argv[3].encode(), None) == 0
+    print(it, flush=True)
+print("accepted", accepted, flush=True)
+'''
+
+
+def test_mutated_archives_never_crash(library, archive_path, tmp_path):
+    r = subprocess.run([sys.executable, "-c", MUTATE, str(library), str(archive_path), str(tmp_path / "m.pwm"),
+                        "2026", "120"], capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, (r.returncode, r.stdout[-200:], r.stderr[-500:])
+    assert r.stdout.strip().splitlines()[-1].startswith("accepted")
