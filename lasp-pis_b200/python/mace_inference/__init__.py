@@ -5,9 +5,9 @@ calculator (importable only when ``ase`` is installed) and ``library_path`` loca
 library (``MACE_LIBRARY`` overrides).  ``NativeMH1`` is the same binding without ASE.
 """
 from .library import library_path
-from .native import NativeMH1, nccl_unique_id, neighbor_edges
+from .native import NativeMH1, check_model, nccl_unique_id, neighbor_edges
 
-__all__ = ["NativeMH1", "library_path", "nccl_unique_id", "neighbor_edges"]
+__all__ = ["NativeMH1", "check_model", "library_path", "nccl_unique_id", "neighbor_edges"]
 try:  # ase is optional
     from .calculator import MH1Calculator  # noqa: F401
     __all__.append("MH1Calculator")

@@ -46,6 +46,8 @@ def load(path=None) -> ct.CDLL:
     lib.lapis_neighbor_edges.argtypes = [ct.c_int, ct.c_void_p, ct.c_void_p, ct.c_float, ct.c_int, ct.c_longlong,
                                          ct.c_void_p, ct.c_longlong]
     lib.lapis_neighbor_edges.restype = ct.c_longlong
+    lib.mace_check_model.argtypes = [ct.c_char_p, ct.c_char_p]
+    lib.mace_check_model.restype = ct.c_int
     _libs[path] = lib
     return lib
 
@@ -67,6 +69,14 @@ def neighbor_edges(xyz, cell, cutoff=6.0, backend=0, grid_bytes=0, library=None)
     lib.lapis_neighbor_edges(len(xyz), xyz.ctypes.data, cell.ctypes.data, cutoff, backend, grid_bytes,
                              out.ctypes.data, count)
     return out[:count]
+
+
+def check_model(model, head=None, library=None) -> None:
+    """Parse and validate a model (archive or MH1 checkpoint for ``head``) as the
+    constructors do, without a GPU; raises RuntimeError with the loader's message."""
+    lib = load(library)
+    if lib.mace_check_model(str(model).encode(), None if head is None else head.encode()):
+        raise RuntimeError(_error(lib))
 
 
 def nccl_unique_id(library=None) -> bytes:

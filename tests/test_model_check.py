@@ -41,6 +41,15 @@ def test_valid_models_pass(lib, archive_path, tmp_path):
     assert rc == -1 and err.startswith("Cannot open MH1 archive")
 
 
+def test_python_helper(library, archive_path, tmp_path):
+    from mace_inference import check_model
+    check_model(archive_path, library=library)
+    with pytest.raises(RuntimeError, match="Invalid MH1 archive magic"):
+        bad = tmp_path / "bad.pwm"
+        bad.write_bytes(b"PWMH1002" + archive_path.read_bytes()[8:])
+        check_model(bad, library=library)
+
+
 def defects():
     """(name, edit of the records or the bytes, expected message fragment)."""
     def drop(key):
