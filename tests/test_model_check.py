@@ -4,9 +4,11 @@ checkpoints) in host memory.  Valid models pass; each defect gets the loader's o
 mutated archives are accepted or rejected but never crash the process.
 """
 import ctypes as ct
+import json
 import struct
 import subprocess
 import sys
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -133,3 +135,53 @@ def test_mutated_archives_never_crash(library, archive_path, tmp_path):
                         "2026", "120"], capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, (r.returncode, r.stdout[-200:], r.stderr[-500:])
     assert r.stdout.strip().splitlines()[-1].startswith("accepted")
+
+
+REF_CREATE = r'''
+import ctypes as ct, json, sys
+lib = ct.CDLL(sys.argv[1])
+lib.mace_create_mh1_head.argtypes = [ct.c_char_p, ct.c_int, ct.c_char_p]
+lib.mace_create_mh1_head.restype = ct.c_void_p
+lib.mace_last_error.restype = ct.c_char_p
+lib.mace_destroy.argtypes = [ct.c_void_p]
+out = []
+for path in sys.argv[2:]:
+    h = lib.mace_create_mh1_head(path.encode(), 0, None)
+    out.append(None if h else lib.mace_last_error().decode())
+    if h:
+        lib.mace_destroy(h)
+print(json.dumps(out))
+'''
+
+
+@pytest.mark.gpu
+def test_loader_errors_match_reference_library(lib, archive_path, tmp_path):
+    """On a GPU: the reference's own library (oracle/_ref/libmace_ref.so, built from its
+    sources) rejects every defective archive above with the message mace_check_model and this
+    build's constructor give, and accepts the valid one."""
+    from lasp_b200 import archive
+    from mace_inference import NativeMH1
+    ref_lib = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "libmace_ref.so"
+    if not ref_lib.exists():
+        pytest.skip("reference library not built")
+    paths = [archive_path]
+    for name, edit, _ in defects():
+        records = archive.read(archive_path)
+        edit(records)
+        paths.append(tmp_path / f"{name}.pwm")
+        archive.write(paths[-1], records)
+    blob = archive_path.read_bytes()
+    for name, data in (("magic", b"PWMH1002" + blob[8:]), ("truncated", blob[:len(blob) // 2])):
+        paths.append(tmp_path / f"{name}.pwm")
+        paths[-1].write_bytes(data)
+    r = subprocess.run([sys.executable, "-c", REF_CREATE, str(ref_lib)] + [str(p) for p in paths],
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-500:]
+    theirs = json.loads(r.stdout.strip().splitlines()[-1])
+    for path, ref_err in zip(paths, theirs):
+        rc, err = check(lib, path)
+        assert (rc == 0) == (ref_err is None) and (ref_err is None or err == ref_err), (path.name, err, ref_err)
+        if ref_err is not None:
+            with pytest.raises(RuntimeError) as e:
+                NativeMH1(path, device=0)
+            assert str(e.value) == ref_err
