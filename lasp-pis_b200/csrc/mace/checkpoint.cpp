@@ -270,13 +270,6 @@ bool is_zip(const std::string &path) {
 
 // ---------------------------------------------------------------------------- tensor view
 
-size_t Tensor::count() const {
-  size_t n = 1;
-  for (auto s : shape)
-    n *= size_t(s);
-  return n;
-}
-
 namespace {
 template <class T> double widen(const char *p) {
   T x;

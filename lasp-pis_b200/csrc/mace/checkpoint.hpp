@@ -33,7 +33,6 @@ struct Tensor {
   // Elements in row-major order of `shape`, widened to double; throws on bad metadata, a
   // view outside its storage or a nonfinite value.
   std::vector<double> values() const;
-  size_t count() const;
 };
 
 struct Node;
