@@ -4,6 +4,9 @@
 //   checkpoint-reader ZIP       the fixture must open and its data.pkl decode to None; then
 //                               inert reducers, malformed pickles and strided views are checked
 //   checkpoint-reader --open F  only open F and decode its root (exit 1 if rejected)
+//   checkpoint-reader --tree F  the decoded root as JSON: numbers, strings (bytes as
+//                               \u00XX escapes), lists, objects; class records as
+//                               {"$class", "items", "fields"}, tensors as {"$tensor", "shape"}
 //   checkpoint-reader --tensors F   the root's class, then every tensor reachable through the
 //                               module tree: "name [d0,d1,...] first-value" per line
 //                               (what the reference's checkpoint_inspect prints)
@@ -11,6 +14,7 @@
 // Prints one line on success; exits 1 with the error otherwise.
 #include "checkpoint.hpp"
 
+#include <cstdio>
 #include <cstring>
 #include <iomanip>
 #include <iostream>
@@ -23,6 +27,87 @@ using mace::ckpt::Node;
 static void require(bool ok, const char *what) {
   if (!ok)
     throw std::runtime_error(std::string("checkpoint test failed: ") + what);
+}
+
+static void json_text(const std::string &t) {
+  std::cout << '"';
+  for (unsigned char c : t) {
+    if (c == '"' || c == '\\')
+      std::cout << '\\' << c;
+    else if (c < 0x20 || c >= 0x7f) {
+      char buf[8];
+      std::snprintf(buf, sizeof(buf), "\\u%04x", c);
+      std::cout << buf;
+    } else
+      std::cout << c;
+  }
+  std::cout << '"';
+}
+
+static void json_node(const mace::ckpt::NodeRef &n, int depth) {
+  if (depth > 200)
+    throw std::runtime_error("tree too deep to print");
+  auto list = [&](const std::vector<mace::ckpt::NodeRef> &items) {
+    std::cout << '[';
+    for (size_t k = 0; k < items.size(); ++k) {
+      if (k)
+        std::cout << ',';
+      json_node(items[k], depth + 1);
+    }
+    std::cout << ']';
+  };
+  auto dict = [&](const std::map<std::string, mace::ckpt::NodeRef> &fields) {
+    std::cout << '{';
+    bool first = true;
+    for (const auto &[k, v] : fields) {
+      if (!first)
+        std::cout << ',';
+      first = false;
+      json_text(k);
+      std::cout << ':';
+      json_node(v, depth + 1);
+    }
+    std::cout << '}';
+  };
+  switch (n->kind) {
+  case Node::None:
+    std::cout << "null";
+    break;
+  case Node::Number: {
+    // Always a float literal, so that -0.0 keeps its sign through a JSON parser.
+    char buf[40];
+    std::snprintf(buf, sizeof(buf), "%.17g", n->number);
+    std::cout << buf << (std::strpbrk(buf, ".eni") ? "" : ".0");
+    break;
+  }
+  case Node::Text:
+    json_text(n->text);
+    break;
+  case Node::Items:
+    list(n->items);
+    break;
+  case Node::Fields:
+    dict(n->fields);
+    break;
+  case Node::Global:
+  case Node::Instance:
+    std::cout << "{\"$class\":";
+    json_text(n->text);
+    std::cout << ",\"items\":";
+    list(n->items);
+    std::cout << ",\"fields\":";
+    dict(n->fields);
+    std::cout << '}';
+    break;
+  case Node::TensorView:
+    std::cout << "{\"$tensor\":";
+    json_text(n->tensor.dtype);
+    std::cout << ",\"shape\":[";
+    for (size_t k = 0; k < n->tensor.shape.size(); ++k)
+      std::cout << (k ? "," : "") << n->tensor.shape[k];
+    std::cout << "]}";
+    break;
+  }
 }
 
 static bool rejects(const std::string &pickle, const mace::ckpt::Zip &zip) {
@@ -41,6 +126,13 @@ int main(int argc, char **argv) {
       mace::ckpt::load(zip);
       return 0;
     }
+    if (argc == 3 && std::string(argv[1]) == "--tree") {
+      mace::ckpt::Zip zip{std::string(argv[2])};
+      std::cout << std::setprecision(17);
+      json_node(mace::ckpt::load(zip), 0);
+      std::cout << "\n";
+      return 0;
+    }
     if (argc == 3 && std::string(argv[1]) == "--tensors") {
       mace::ckpt::Zip zip{std::string(argv[2])};
       auto root = mace::ckpt::load(zip);
@@ -56,7 +148,7 @@ int main(int argc, char **argv) {
       return 0;
     }
     if (argc != 2)
-      throw std::runtime_error("usage: checkpoint-reader ZIP | --open FILE | --tensors FILE");
+      throw std::runtime_error("usage: checkpoint-reader ZIP | --open FILE | --tree FILE | --tensors FILE");
     mace::ckpt::Zip zip{std::string(argv[1])};
     require(mace::ckpt::load(zip)->kind == Node::None, "fixture root is None");
 

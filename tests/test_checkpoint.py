@@ -342,3 +342,80 @@ def test_mutated_checkpoints_fail_cleanly(tools, tmp_path):
             path.write_bytes(bytes(p))
         r = run(reader, "--open", path)
         assert r.returncode in (0, 1), (it, r.returncode, r.stderr)
+
+
+def _random_value(rng, depth=0):
+    """Random data of the kinds a checkpoint pickles: ints (|x| < 2^52), floats, bools, None,
+    ASCII text, bytes, tuples, lists, sets, dicts with text or int keys, OrderedDicts."""
+    import collections
+    kinds = ["int", "float", "bool", "none", "str", "bytes"] + (["tuple", "list", "set", "dict", "odict"]
+                                                               if depth < 4 else [])
+    k = rng.choice(kinds)
+    if k == "int":
+        return rng.choice([rng.randrange(256), rng.randrange(65536), rng.randrange(-2**31, 2**31),
+                           rng.randrange(-2**52, 2**52)])
+    if k == "float":
+        return rng.choice([rng.uniform(-1e6, 1e6), rng.random() * 1e-300, -0.0, float(rng.randrange(100))])
+    if k == "bool":
+        return rng.random() < 0.5
+    if k == "none":
+        return None
+    if k == "str":
+        return "".join(rng.choice("abcXYZ_.019 ") for _ in range(rng.randrange(0, 300)))
+    if k == "bytes":
+        return bytes(rng.randrange(256) for _ in range(rng.randrange(0, 300)))
+    n = rng.randrange(0, 6)
+    if k in ("tuple", "list"):
+        items = [_random_value(rng, depth + 1) for _ in range(n)]
+        return tuple(items) if k == "tuple" else items
+    if k == "set":
+        return {rng.randrange(-1000, 1000) for _ in range(n)}
+    keys = [rng.choice([str(rng.randrange(1000)), rng.randrange(-1000, 1000)]) for _ in range(n)]
+    d = {key: _random_value(rng, depth + 1) for key in keys}
+    return collections.OrderedDict(d) if k == "odict" else d
+
+
+def _expected(value):
+    """What the decoder must produce for a value, in the reader's JSON form."""
+    if isinstance(value, bool):
+        return int(value)
+    if isinstance(value, bytes):
+        return value.decode("latin1")
+    if isinstance(value, (list, tuple)):
+        return [_expected(v) for v in value]
+    if isinstance(value, set):
+        return [_expected(v) for v in value]
+    if isinstance(value, dict):
+        return {str(k): _expected(v) for k, v in value.items()}
+    return value
+
+
+def test_pickle_layer_matches_python_pickle(tools, tmp_path):
+    """Seeded random values pickled by Python (protocol 2, with memo references for shared
+    and repeated objects) decode to the same data: every container, number, text and byte."""
+    import pickle
+    import random
+    _, reader = tools
+    rng = random.Random(4242)
+    path = tmp_path / "v.zip"
+    for it in range(150):
+        value = _random_value(rng)
+        shared = [value, value] if rng.random() < 0.3 else value  # memo BINGET of a shared object
+        with zipfile.ZipFile(path, "w") as z:
+            z.writestr("archive/data.pkl", pickle.dumps(shared, protocol=2))
+        r = run(reader, "--tree", path)
+        assert r.returncode == 0, (it, r.stderr)
+        assert _same(json.loads(r.stdout), _expected(shared)), it
+
+
+def _same(got, want):
+    """Structural equality; numbers equal as doubles, including the sign of zero."""
+    import math
+    if isinstance(want, (int, float)) and not isinstance(want, bool):
+        return isinstance(got, float) and got == float(want) and math.copysign(1, got) == math.copysign(1, want)
+    if isinstance(want, list):
+        return isinstance(got, list) and len(got) == len(want) and all(map(_same, got, want))
+    if isinstance(want, dict):
+        return isinstance(got, dict) and got.keys() == want.keys() and all(_same(got[k], want[k]) for k in want)
+    return got == want
+
