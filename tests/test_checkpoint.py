@@ -419,3 +419,19 @@ def _same(got, want):
         return isinstance(got, dict) and got.keys() == want.keys() and all(_same(got[k], want[k]) for k in want)
     return got == want
 
+
+
+@pytest.mark.parametrize("protocol", [4, 5])
+def test_newer_pickle_protocols_convert_the_same(tools, tmp_path, protocol):
+    """torch.save with pickle protocol 4 or 5 (frames, memoize, stack globals) converts to the
+    same archive as the default protocol 2."""
+    from lasp_b200 import checkpoint
+    case = GOLD["cases"]["float64"]
+    model = checkpoint.build_model(case["seed"], torch.float64)
+    path = tmp_path / f"p{protocol}.model"
+    with checkpoint._registered():
+        torch.save(model, path, pickle_protocol=protocol)
+    rc, err = convert(path, tmp_path / "o.pwm")
+    assert rc == 0, err
+    digest = hashlib.sha256((tmp_path / "o.pwm").read_bytes()).hexdigest()
+    assert digest == case["heads"]["matpes_r2scan"]["sha256"]
