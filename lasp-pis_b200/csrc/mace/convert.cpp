@@ -46,13 +46,13 @@ ckpt::Tensor tensor_of(const NodeRef &m, const std::string &path) {
   return v->tensor;
 }
 std::vector<double> values_of(const NodeRef &m, const std::string &path) { return tensor_of(m, path).values(); }
-// A Python number or a one-element tensor.
+// A Python number or a one-element tensor.  Anything else fails as a tensor without
+// storage would ("checkpoint: invalid tensor metadata"), as in the reference.
 double scalar_of(const NodeRef &m, const std::string &path) {
   NodeRef v = ckpt::walk(m, path);
   if (v->kind == Node::Number)
     return v->number;
-  need(v->kind == Node::TensorView, "expected scalar " + path);
-  auto d = v->tensor.values();
+  auto d = v->kind == Node::TensorView ? v->tensor.values() : ckpt::Tensor{}.values();
   need(d.size() == 1, "expected scalar " + path);
   return d[0];
 }

@@ -261,10 +261,13 @@ def broken(kind):
         return m, "radial cutoff"
     if kind == "root":
         return m.interactions[0], "expected ScaleShiftMACE"
+    if kind == "scalar_text":
+        m.radial_embedding.apply_cutoff = "no"
+        return m, "invalid tensor metadata"
     raise ValueError(kind)
 
 
-@pytest.mark.parametrize("kind", ["heads", "nonfinite", "eps", "connection", "gate", "cutoff", "root"])
+@pytest.mark.parametrize("kind", ["heads", "nonfinite", "eps", "connection", "gate", "cutoff", "root", "scalar_text"])
 def test_conversion_errors(tools, tmp_path, kind):
     from lasp_b200 import checkpoint
     model, message = broken(kind)
