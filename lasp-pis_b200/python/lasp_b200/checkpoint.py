@@ -33,23 +33,29 @@ SEED = 20261202
 class _Irrep(tuple):
     __slots__ = ()
 
-    def __new__(cls, l, p):
+    def __new__(cls, l, p=None):
+        if p is None:  # rebuilt from its pickled form Irrep((l, p))
+            l, p = l
         return super().__new__(cls, (l, p))
 
 
 class _MulIr(tuple):
     __slots__ = ()
 
-    def __new__(cls, mul, ir):
+    def __new__(cls, mul, ir=None):
+        if ir is None:  # rebuilt from its pickled form _MulIr((mul, ir))
+            mul, ir = mul
         return super().__new__(cls, (mul, ir))
 
 
 class _Irreps(tuple):
-    """e3nn Irreps: a tuple of (mul, (l, parity)); pickles as Irreps((...,)) like e3nn's."""
+    """e3nn Irreps: a tuple of (mul, (l, parity)); pickles as Irreps((...,)) like e3nn's.
+    Built from (mul, l, parity) triples, or rebuilt from its own elements."""
     __slots__ = ()
 
     def __new__(cls, blocks):
-        return super().__new__(cls, tuple(_MulIr(m, _Irrep(l, p)) for m, l, p in blocks))
+        return super().__new__(cls, tuple(b if isinstance(b, _MulIr) else _MulIr(b[0], _Irrep(b[1], b[2]))
+                                          for b in blocks))
 
 
 _LinearInstruction = collections.namedtuple("Instruction", "i_in i_out path_shape path_weight")
