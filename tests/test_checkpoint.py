@@ -438,3 +438,96 @@ def test_newer_pickle_protocols_convert_the_same(tools, tmp_path, protocol):
     assert rc == 0, err
     digest = hashlib.sha256((tmp_path / "o.pwm").read_bytes()).hexdigest()
     assert digest == case["heads"]["matpes_r2scan"]["sha256"]
+
+
+def _structural_mutation(rng, model):
+    """One seeded structural defect of the module tree: a parameter one element short, a
+    changed instruction field, a changed irreps block, a removed child module, a truncated
+    buffer, a transposed matrix, or shuffled heads.  Returns a label, or None if not applied."""
+    from lasp_b200 import checkpoint
+
+    def modules(m, prefix=""):
+        out = [(prefix, m)]
+        for n, c in m._modules.items():
+            if c is not None:
+                out += modules(c, prefix + n + ".")
+        return out
+
+    name, mod = rng.choice(modules(model))
+    kind = rng.randrange(7)
+    if kind == 0 and mod._parameters:
+        k = rng.choice(list(mod._parameters))
+        t = mod._parameters[k]
+        if t is not None and t.numel() > 1:
+            mod._parameters[k] = torch.nn.Parameter(t.data.flatten()[:-1].clone(), requires_grad=False)
+            return f"short {name}{k}"
+    if kind == 1 and getattr(mod, "instructions", None):
+        i = rng.randrange(len(mod.instructions))
+        inst = mod.instructions[i]
+        f = rng.randrange(len(inst))
+        v = inst[f]
+        if isinstance(v, bool):
+            v = not v
+        elif isinstance(v, int):
+            v += rng.choice([-1, 1, 7])
+        elif isinstance(v, float):
+            v *= 2
+        elif isinstance(v, str):
+            v = "uuw"
+        elif isinstance(v, tuple):
+            v = (v[0] + 1,) + v[1:]
+        mod.instructions[i] = inst._replace(**{inst._fields[f]: v})
+        return f"instruction {name}{i}.{inst._fields[f]}"
+    attrs = [a for a in ("irreps_in", "irreps_out", "irreps_in1", "irreps_in2") if hasattr(mod, a)]
+    if kind == 2 and attrs:
+        attr = rng.choice(attrs)
+        blocks = [(mul, ir[0], ir[1]) for mul, ir in getattr(mod, attr)]
+        j = rng.randrange(len(blocks))
+        mul, l, p = blocks[j]
+        blocks[j] = rng.choice([(mul + 1, l, p), (mul, min(l + 1, 3), p), (mul, l, -p), (0, l, p)])
+        setattr(mod, attr, checkpoint._Irreps(blocks))
+        return f"irreps {name}{attr}"
+    if kind == 3 and mod._modules:
+        k = rng.choice(list(mod._modules))
+        del mod._modules[k]
+        return f"removed {name}{k}"
+    if kind == 4 and mod._buffers:
+        k = rng.choice(list(mod._buffers))
+        t = mod._buffers[k]
+        if t is not None:
+            mod._buffers[k] = t.reshape(-1)[:t.numel() - 1].clone() if t.numel() > 1 else t * 2
+            return f"buffer {name}{k}"
+    if kind == 5 and mod._parameters:
+        k = rng.choice(list(mod._parameters))
+        t = mod._parameters[k]
+        if t is not None and t.dim() == 2:
+            mod._parameters[k] = torch.nn.Parameter(t.data.t().contiguous(), requires_grad=False)
+            return f"transposed {name}{k}"
+    if kind == 6:
+        model.heads = list(model.heads)
+        rng.shuffle(model.heads)
+        return "shuffled heads"
+    return None
+
+
+def test_structural_defects_match_reference(tools, tmp_path):
+    """Seeded structural defects of the module tree (one or two each, random head): this
+    build never crashes and, where the reference's converter is built, gives its exit code,
+    its message and, when it converts, its archive bytes."""
+    import copy
+    import random
+    from lasp_b200 import checkpoint
+    base = checkpoint.build_model(3, torch.float32)
+    rng = random.Random(2)
+    path = tmp_path / "s.model"
+    for it in range(25):
+        model = copy.deepcopy(base)
+        labels = [_structural_mutation(rng, model) for _ in range(rng.randint(1, 2))]
+        checkpoint.save(model, path)
+        head = rng.choice([None] + list(checkpoint.HEADS))
+        rc, err = convert(path, tmp_path / "a.pwm", head)
+        assert rc in (0, 1), (it, labels, err)
+        if REF_DUMP.exists():
+            assert convert(path, tmp_path / "b.pwm", head, REF_DUMP) == (rc, err), (it, labels)
+            if rc == 0:
+                assert (tmp_path / "a.pwm").read_bytes() == (tmp_path / "b.pwm").read_bytes(), (it, labels)
