@@ -229,3 +229,35 @@ def test_checkpoint_route(library, tmp_path):
     assert r.returncode == 0, r.stderr
     assert f"MACE head: {head}" in r.stderr
     assert json.loads(r.stdout)["energy"] == pytest.approx(ra["energy"], rel=1e-6)
+
+
+def test_engine_invariances(engine):
+    """The engine's own physics checks (as the reference's check_invariants.py:14-96 runs
+    them on its build): translation, wrapping an atom by a lattice vector, a rigid rotation
+    of positions and cell (forces and virial rotate with it), and zero net force.  Bounds:
+    energy 3e-6 relative (float32 rounding of the moved coordinates), forces 1e-4 eV/A x
+    max(1, max|F|) and virial 1e-5 x max|W| under rotation, 3e-5 / 6e-6 otherwise."""
+    from lasp_b200 import so3
+    s = structures.load("C1", DATA)
+    m = engine[0]
+    base = m.calculate(s.positions, s.numbers, s.cell)
+    fmax, wmax = max(1.0, float(np.abs(base["forces"]).max())), float(np.abs(base["virial"]).max())
+
+    def close(r, f_bound, w_bound, rot=None):
+        f, w = base["forces"].astype(np.float64), base["virial"].astype(np.float64)
+        if rot is not None:
+            f, w = f @ rot.T, rot @ w @ rot.T
+        assert abs(r["energy"] - base["energy"]) <= 3e-6 * abs(base["energy"])
+        assert float(np.abs(r["forces"] - f).max()) <= f_bound * fmax
+        assert float(np.abs(r["virial"] - w).max()) <= w_bound * wmax
+
+    shift = np.array([0.37, -1.2, 2.9], np.float32)
+    close(m.calculate(s.positions + shift, s.numbers, s.cell), 3e-5, 6e-6)
+    wrapped = s.positions.copy()
+    wrapped[5] += s.cell[1] - s.cell[2]
+    close(m.calculate(wrapped, s.numbers, s.cell), 3e-5, 6e-6)
+    rot = so3.rotation(3)
+    rx = (s.positions.astype(np.float64) @ rot.T).astype(np.float32)
+    rc = (s.cell.astype(np.float64) @ rot.T).astype(np.float32)
+    close(m.calculate(rx, s.numbers, rc), 1e-4, 1e-5, rot)
+    assert float(np.abs(base["forces"].astype(np.float64).sum(0)).max()) <= 1e-4 * fmax
