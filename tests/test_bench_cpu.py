@@ -1,0 +1,54 @@
+"""CPU checks of bench.py's reporting logic (the GPU runs are checked by the driver): the
+headline metric name, the roofline's algorithmic bytes and ncu traffic per edge, and the
+parsing of nvidia-smi clock samples into clocks and throttle reasons."""
+import importlib.util
+import subprocess
+import sys
+
+import pytest
+
+from conftest import ROOT
+
+
+@pytest.fixture(scope="module")
+def bench():
+    spec = importlib.util.spec_from_file_location("bench_under_test", ROOT / "bench.py")
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+def test_metric_names(bench):
+    assert bench.metric_for("C3") == bench.METRIC == "atoms*evals/s (E+F+virial), MH1-shape, C3 10k-atom cell"
+    assert bench.metric_for("C1").endswith("C1 64-atom cell")
+    assert bench.metric_for("C5").endswith("C5 ~200k-atom cell")
+
+
+def test_roofline_bytes(bench):
+    # R and dR rows (2 x 10 paths x 128 fp32), Y and dY, geometry, cutoff and density pairs,
+    # sender index, edge force.
+    assert bench.edge_backward1_bytes(1) == 10548
+    assert bench.edge_backward1_bytes(846394, paths=10) == 846394 * 10548
+    # The measured DRAM traffic is within 4% of the algorithmic bytes (no re-reads).
+    assert 1.0 < bench.TRAFFIC_PER_EDGE / bench.edge_backward1_bytes(1) < 1.04
+
+
+def test_clock_summary(bench):
+    sampler = bench.ClockSampler(0)
+    sampler.lines = [
+        "0, 1965, 1965, 700.1, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active",
+        "0, 1890, 1965, 998.7, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
+        "0, 1900, 1965, 990.0, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
+        "garbage",
+        "0, [N/A], 1965, 0, 0x0, Not Active, Not Active, Not Active, Not Active",
+    ]
+    s = sampler.summary()
+    assert s == {"sm_mhz": 1900.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"], "samples": 3}
+    sampler.lines = ["0, 1200, 1965, 500, 0x8, Active, Not Active, Active, Not Active"]
+    assert sampler.summary()["reasons"] == ["hw_slowdown", "sw_thermal_slowdown"]
+    assert bench.ClockSampler(0).summary() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+
+
+def test_help_runs_without_a_gpu():
+    r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--help"], capture_output=True, text=True)
+    assert r.returncode == 0 and "--impl" in r.stdout and "--host" in r.stdout
