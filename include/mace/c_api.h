@@ -93,10 +93,12 @@ MACE_EXPORT long long lapis_neighbor_edges(int n, const float *xyz, const float 
  * are enumerated by brute force over all atoms and periodic images.  Limits: n <= 16384.
  * Returns the edge count E; if E exceeds `capacity` only row is written, so the caller can
  * retry with larger buffers.  Returns -1 on error (message in mace_last_error), including
- * n above the limit.  Runs on the current device and on `stream` (NULL = default stream) and
- * blocks until done.  The first call on a device looks up that device's copy of the array;
- * make that first call before capturing any stream.  Every call reuses the same array, so
- * calls that overlap on the GPU race with each other: serialise them. */
+ * n above the limit.  Runs on the current device and on `stream` (NULL = default stream).
+ * The call is synchronous: it waits on `stream` for its results before it returns.  The first
+ * call on a device does that device's set-up (it looks up the device address of the array);
+ * make that first call before any stream capture.  The set-up is repeated if the device's
+ * context is replaced (cudaDeviceReset).  Every call reuses the same array, so calls that
+ * overlap on the GPU race with each other: serialise them. */
 MACE_EXPORT long long lapis_neighbor_list_static(int n, const float *xyz, const int *elements, const float *cell,
                                                  float cutoff, int *row, int *sender, int *shift, float *vector,
                                                  long long capacity, void *stream);

@@ -1075,13 +1075,48 @@ static __device__ __align__(256) int g_static_scratch[kStaticWords];
 
 struct StaticScratch {
   int *base = nullptr;
-  bool ready = false;
+  unsigned long long context = 0; // id of the context the address belongs to (0: none yet)
 };
 StaticScratch g_static_by_device[64];
 std::atomic_flag g_static_lock = ATOMIC_FLAG_INIT;
 
+// Unique id of the calling thread's current context (CUDA 12 driver entry points, reached
+// through the runtime so the library keeps no link dependency on libcuda); 0 when no
+// context is current yet.
+unsigned long long current_context_id() {
+  using GetCurrent = int (*)(void **);
+  using GetId = int (*)(void *, unsigned long long *);
+  static GetCurrent get_current = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    return cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+                   q == cudaDriverEntryPointSuccess
+               ? reinterpret_cast<GetCurrent>(p)
+               : nullptr;
+  }();
+  static GetId get_id = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    return cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+                   q == cudaDriverEntryPointSuccess
+               ? reinterpret_cast<GetId>(p)
+               : nullptr;
+  }();
+  void *ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id)
+    throw Error("cuCtxGetCurrent/cuCtxGetId are unavailable");
+  if (get_current(&ctx) != 0 || !ctx)
+    return 0;
+  if (get_id(ctx, &id) != 0)
+    throw Error("cuCtxGetId failed");
+  return id;
+}
+
 // Device address of g_static_scratch for the current device (the host-side symbol is only a
-// stand-in).  Resolved once per device, on that device.
+// stand-in).  Set-up runs once per device, on that device: cudaGetSymbolAddress, whose
+// return code is checked.  The address is tied to the device's context and is looked up
+// again if that context has been replaced since (for example after cudaDeviceReset).
 int *static_scratch_address() {
   int device = 0;
   check(cudaGetDevice(&device));
@@ -1093,11 +1128,14 @@ int *static_scratch_address() {
     ~Unlock() { g_static_lock.clear(std::memory_order_release); }
   } unlock;
   auto &slot = g_static_by_device[device];
-  if (!slot.ready) {
+  unsigned long long ctx = current_context_id();
+  if (!slot.context || ctx != slot.context) {
     void *p = nullptr;
-    check(cudaGetSymbolAddress(&p, g_static_scratch));
+    check(cudaGetSymbolAddress(&p, g_static_scratch)); // makes the primary context current
     slot.base = static_cast<int *>(p);
-    slot.ready = true;
+    slot.context = current_context_id();
+    if (!slot.context)
+      throw Error("No current CUDA context after cudaGetSymbolAddress");
   }
   return slot.base;
 }

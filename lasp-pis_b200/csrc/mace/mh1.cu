@@ -160,9 +160,8 @@ std::vector<Result> MH1::compute(bool batch) {
     c.clear(force + size_t(3) * n, size_t(ns - n) * 3 * sizeof(float));
   launch_zbl(s, c.geometry, m.constants_dev, m.zbl_radii, m.zbl_c, cst[7], energy, force, virial);
   // Projection path: radial projections on the tensor cores into chunk buffers, tensor
-  // products from those (default); otherwise the fused SIMT or tcgen05 edge kernels.
-  bool projection = !tensor_core_edges() && tensor_core_linears() && m.layers[0].radial.out_hi &&
-                    m.layers[1].radial.out_hi;
+  // products from those (default); otherwise the fused SIMT edge kernels.
+  bool projection = tensor_core_linears() && m.layers[0].radial.out_hi && m.layers[1].radial.out_hi;
   if (dom && !projection)
     throw Error("Domain decomposition requires the tensor-core projection path");
   std::vector<ProjectionChunk> chunks;
@@ -220,9 +219,7 @@ std::vector<Result> MH1::compute(bool batch) {
         launch_message_forward_proj(s, k, c.geometry, l, ea, ro[k], q, proj[k], up[k], msg, rho[k], ns);
         timer.mark("forward" + std::to_string(k) + ".messages");
       }
-    } else if (tensor_core_edges())
-      launch_message_forward_tc(s, k, c.geometry, l, ea, ro[k], up[k], msg, rho[k]);
-    else
+    } else
       launch_message_forward(s, k, c.geometry, l, ea, ro[k], up[k], msg, rho[k]);
     timer.mark("forward" + std::to_string(k) + ".messages");
     linear(s, n, l.one, msg, raw[k], false, false, status);
@@ -293,9 +290,7 @@ std::vector<Result> MH1::compute(bool batch) {
                                      edge_force, k == 0, ns);
         timer.mark("backward" + std::to_string(k) + ".edges");
       }
-    } else if (tensor_core_edges())
-      launch_message_backward_tc(s, k, c.geometry, l, ea, ro[k], up[k], msggrad, rhograd, upgrad, edge_force, k == 0);
-    else
+    } else
       launch_message_backward(s, k, c.geometry, l, ea, ro[k], up[k], msggrad, rhograd, upgrad, edge_force, k == 0);
     timer.mark("backward" + std::to_string(k) + ".edges");
     if (k == 1) {

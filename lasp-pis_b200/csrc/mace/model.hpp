@@ -117,14 +117,7 @@ void launch_message_forward(cudaStream_t, int layer, const lapis::DeviceGeometry
 void launch_message_backward(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &,
                              EdgeArrays, RadialOut, const float *up, const float *message_grad,
                              const float *density_grad, float *up_grad, float4 *edge_force, bool accumulate);
-// Tensor-core versions (edge_tc.cu): same contracts as the SIMT launches above.
-void launch_message_forward_tc(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &, EdgeArrays,
-                               RadialOut, const float *up, float *message, float *density);
-void launch_message_backward_tc(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &,
-                                EdgeArrays, RadialOut, const float *up, const float *message_grad,
-                                const float *density_grad, float *up_grad, float4 *edge_force, bool accumulate);
 CUtensorMap tc_map_2d(const float *base, int cols, long long rows, int box_cols, int box_rows);
-bool tensor_core_edges();
 // Projection path (edge_proj.cu): the radial projection R = h W (and dR = dh W) runs as a
 // tensor-core GEMM into a buffer covering the edges of receivers [r0, r1) = [e0, e1); the
 // tensor-product kernels read rows e - e0.

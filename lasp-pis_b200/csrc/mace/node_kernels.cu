@@ -588,16 +588,6 @@ void launch_embed(cudaStream_t s, int n, const int *species, const float *embedd
     lapis::launch(embed_kernel, blocks_for(size_t(n) * 512, 256), 256, 0, s, n, species, embedding, x);
 }
 
-// The fused tensor-core edge kernels are opt-in (MACE_TC_EDGES=1) until they beat the SIMT
-// kernels on both time and accuracy.
-bool tensor_core_edges() {
-  static const bool on = [] {
-    const char *v = std::getenv("MACE_TC_EDGES");
-    return v && v[0] == '1';
-  }();
-  return on;
-}
-
 bool tensor_core_linears() {
   static const bool on = [] {
     const char *v = std::getenv("MACE_SIMT_LINEARS");

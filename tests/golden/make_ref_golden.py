@@ -3,10 +3,16 @@
 Runs the reference's own ``libmace.so`` (built from its sources by oracle/ref/Makefile)
 through its C ABI on the seeded synthetic archive and configs, plus its Lapis traversal
 (oracle/_ref/libref_edges.so) on the neighbour scenarios, and writes the results to
-``<out>/`` as .npz / .json files.  The committed fixtures in tests/golden/ were produced
-by running this script on the GPU box:
+``<out>/`` (default: this folder) as .npz / .json files.  The committed fixtures in
+tests/golden/ were produced by running this script on a B200:
 
-    python tests/golden/make_ref_golden.py --out gpurun_out/golden
+    python tests/golden/make_ref_golden.py                      # C1-C3, scenarios, CLI
+    python tests/golden/make_ref_golden.py --configs C5 --merge # adds C5 to ref_summary.json
+
+Structures above 20,000 atoms (C5) are stored compactly: energy, virial, float64 sums of the
+per-atom energies and forces, and the forces and energies of a seeded sample of 4,096 atoms.
+Their edge digest comes from the reference's cell-list traversal only (brute force over
+200,000 atoms is not a useful fixture).
 
 Only this script and the tests read oracle/_ref.
 """
@@ -103,29 +109,37 @@ def digest(edges):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--out", default="gpurun_out/golden")
+    ap.add_argument("--out", default=str(Path(__file__).resolve().parent))
     ap.add_argument("--configs", default="C1,C2,C3")
     ap.add_argument("--timing-calls", type=int, default=20)
+    ap.add_argument("--merge", action="store_true",
+                    help="add the configs to the existing ref_summary.json in --out instead of rewriting it "
+                         "(skips the scenarios and the CLI case)")
     args = ap.parse_args()
     out = Path(args.out)
     out.mkdir(parents=True, exist_ok=True)
     archive = DATA / "mh1_synth.pwm"
     info = synth.write_archive(archive)
     lib, elib = load_ref(), load_edges()
-    summary = {"archive": info, "nproc": os.cpu_count(), "configs": {}, "edges": {}}
-    # Neighbour scenarios (reference traversal on the GPU).
-    for name, xyz, cell, cutoff, grid, backends in scenarios.framework_scenarios():
-        rec = {}
-        for b in backends:
-            e = ref_edge_list(elib, xyz, cell, b, cutoff, grid)
-            rec[str(b)] = {"count": int(len(e)), "sha256": digest(e)}
-        summary["edges"][name] = rec
+    if args.merge:
+        summary = json.loads((out / "ref_summary.json").read_text())
+    else:
+        summary = {"archive": info, "nproc": os.cpu_count(), "configs": {}, "edges": {}}
+        # Neighbour scenarios (reference traversal on the GPU).
+        for name, xyz, cell, cutoff, grid, backends in scenarios.framework_scenarios():
+            rec = {}
+            for b in backends:
+                e = ref_edge_list(elib, xyz, cell, b, cutoff, grid)
+                rec[str(b)] = {"count": int(len(e)), "sha256": digest(e)}
+            summary["edges"][name] = rec
     for name in args.configs.split(","):
         s = structures.load(name, DATA)
         rec = {"atoms": s.size}
-        for b in (1, 2):
+        large = s.size > 20000
+        for b in ((2,) if large else (1, 2)):
             e = ref_edge_list(elib, s.positions, s.cell, b)
             rec[f"edges_{b}"] = {"count": int(len(e)), "sha256": digest(e)}
+            del e
         backends = (0, 1, 2) if s.size <= 1000 else (0,)
         results = {}
         for b in backends:
@@ -152,9 +166,18 @@ def main():
                 rec["diagnostics"] = m.diagnostics()
             m.close()
         b0 = backends[0]
-        np.savez_compressed(out / f"ref_{name}.npz", energy=results[b0]["energy"],
-                            energies=results[b0]["energies"], forces=results[b0]["forces"],
-                            virial=results[b0]["virial"])
+        r0 = results[b0]
+        if large:
+            idx = np.sort(np.random.default_rng(4096).choice(s.size, 4096, replace=False)).astype(np.int32)
+            np.savez_compressed(out / f"ref_{name}.npz", energy=r0["energy"], virial=r0["virial"], sample=idx,
+                                forces_sample=r0["forces"][idx], energies_sample=r0["energies"][idx],
+                                energies_sum=np.float64(r0["energies"].astype(np.float64).sum()),
+                                forces_sum=r0["forces"].astype(np.float64).sum(0),
+                                forces_abs_sum=np.float64(np.abs(r0["forces"].astype(np.float64)).sum()),
+                                forces_abs_max=np.float64(np.abs(r0["forces"]).max()))
+        else:
+            np.savez_compressed(out / f"ref_{name}.npz", energy=r0["energy"], energies=r0["energies"],
+                                forces=r0["forces"], virial=r0["virial"])
         for b in backends[1:]:
             rec[f"backend_{b}_vs_{b0}"] = {
                 "energy": float(abs(results[b]["energy"] - results[b0]["energy"])),
@@ -162,6 +185,10 @@ def main():
             }
         summary["configs"][name] = rec
         print(name, json.dumps(rec)[:400], flush=True)
+    if args.merge:
+        (out / "ref_summary.json").write_text(json.dumps(summary, indent=1) + "\n")
+        print("done")
+        return
     # C-ABI behaviour case (native.py-like) and the CLI on C1.
     xyz, z, cell = scenarios.native_case()
     m = RefMH1(lib, archive, 1)
