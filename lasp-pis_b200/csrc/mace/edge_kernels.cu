@@ -511,7 +511,7 @@ template <int L, bool Accumulate>
 __global__ void __launch_bounds__(128) message_backward_kernel(
     int n, const int *row, const int *sender, const float4 *vec, const float *h, const float *dh, const float2 *cut,
     const float2 *den, const float *up, const float *Wt, const float *Wb, TPValues cg, const float *msg_grad,
-    const float *rho_grad, float *up_grad, float4 *edge_force) {
+    const float *rho_grad, float *ug_edge, float4 *edge_force) {
   using T = Traits<L>;
   constexpr int P = T::P, NC = T::NC, IN = T::IN, EC = T::EC;
   __shared__ __align__(16) float hs[64][EC];
@@ -621,7 +621,7 @@ __global__ void __launch_bounds__(128) message_backward_kernel(
         if constexpr (L > 0) {
 #pragma unroll
           for (int q = 0; q < IN; ++q)
-            atomicAdd(up_grad + (size_t(q) * n + j) * 128 + c, ug[q]);
+            ug_edge[(size_t(base + e) * IN + q) * 128 + c] = ug[q];
         }
       }
       dr = warp_allsum(dr);
@@ -715,28 +715,12 @@ __global__ void force_gather_domain_kernel(DeviceGeometry g, const float4 *ef, f
       virial[9 * i + k] += acc[3 + k];
   }
 }
-// The reaction of every local edge on a ghost sender, accumulated in the ghost's force row.
-__global__ void ghost_reaction_kernel(long long E, int n_own, const int *sender, const float4 *ef, float *force) {
-  long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-  if (e >= E)
-    return;
-  int j = sender[e];
-  if (j >= n_own) {
-    float4 f = ef[e];
-    atomicAdd(force + 3 * j, -f.x);
-    atomicAdd(force + 3 * j + 1, -f.y);
-    atomicAdd(force + 3 * j + 2, -f.z);
-  }
-}
 } // namespace
 
 void launch_force_gather_domain(cudaStream_t s, const DeviceGeometry &g, const float4 *edge_force, float *force,
                                 float *virial) {
   if (g.n && g.edge_capacity)
     lapis::launch(force_gather_domain_kernel, (g.n * 32 + 255) / 256, 256, 0, s, g, edge_force, force, virial);
-  if (g.edge_capacity)
-    lapis::launch(ghost_reaction_kernel, int((g.edge_capacity + 255) / 256), 256, 0, s, g.edge_capacity, g.n,
-                  g.edge_sender, edge_force, force);
 }
 
 void launch_zbl(cudaStream_t s, const DeviceGeometry &g, const float *constants, const float *radii,
@@ -779,13 +763,13 @@ void launch_message_forward(cudaStream_t s, int layer, const DeviceGeometry &g, 
 
 void launch_message_backward(cudaStream_t s, int layer, const DeviceGeometry &g, const Layer &l, EdgeArrays ea,
                              RadialOut ro, const float *up, const float *message_grad, const float *density_grad,
-                             float *up_grad, float4 *edge_force, bool accumulate) {
+                             float *ug_edge, float4 *edge_force, bool accumulate) {
   if (!g.n)
     return;
 #define MH1_BWD(L, A)                                                                                              \
   lapis::launch(message_backward_kernel<L, A>, g.n, 128, 0, s, g.n, g.edge_offsets, g.edge_sender, g.edge_vector, ro.h, ro.dh, \
                                                     ea.cut, ro.density, up, l.radial.out_t, l.radial.out_b, l.tp,  \
-                                                    message_grad, density_grad, up_grad, edge_force)
+                                                    message_grad, density_grad, ug_edge, edge_force)
   if (layer == 0) {
     if (accumulate)
       MH1_BWD(0, true);

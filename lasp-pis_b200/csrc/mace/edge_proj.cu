@@ -52,8 +52,6 @@ template <class V> __device__ __forceinline__ V bcast(float x);
 template <> __device__ __forceinline__ float bcast<float>(float x) { return x; }
 template <> __device__ __forceinline__ float2 bcast<float2>(float x) { return make_float2(x, x); }
 template <class V> __device__ __forceinline__ V vzero() { return bcast<V>(0.f); }
-__device__ __forceinline__ void vatomic_add(float *p, float v) { atomicAdd(p, v); }
-__device__ __forceinline__ void vatomic_add(float2 *p, float2 v) { atomicAdd(p, v); }
 
 // Channel pairing per instantiation: the layer-1 backward keeps one channel per thread (its
 // register budget for two channels would leave one warp per scheduler).
@@ -70,7 +68,7 @@ template <int L, bool Bwd> struct Lanes {
 struct EdgeMeta {
   float4 vec; // d, r
   float2 cut, den;
-  int sender, pad[3];
+  int sender, row, pad[2]; // row: e - e_base (the edge's row in the chunk buffers)
 };
 
 template <int L, bool Bwd> struct Stage {
@@ -85,7 +83,10 @@ template <int L, bool Bwd> struct Stage {
   static constexpr int R = 0, DR = R + T * ROW, U = DR + (Bwd ? T * ROW : 0), Y = U + T * IN * 512;
   static constexpr int DY = Y + T * 64, META = DY + (Bwd ? T * 192 : 0), EF = META + T * sizeof(EdgeMeta);
   // EF: an accumulating backward's current per-edge forces, copied in with the tile.
-  static constexpr int BYTES = EF + (Bwd ? T * 16 : 0);
+  // UG: the layer-1 backward's per-edge up-gradient rows, written by the channel threads and
+  // copied out to global memory in one bulk store per tile.
+  static constexpr int UG = EF + (Bwd ? T * 16 : 0);
+  static constexpr int BYTES = UG + (Bwd && L > 0 ? T * IN * 512 : 0);
   static constexpr unsigned tx(int cnt, bool forces) {
     return cnt * ((Bwd ? 2 : 1) * ROW + IN * 512 + 64 + (Bwd ? 192 : 0) + (forces ? 16 : 0));
   }
@@ -101,7 +102,7 @@ struct ProjArgs {
   const float *up, *bias;
   const float *msg_grad, *rho_grad; // backward inputs
   float *msg, *rho;                 // forward outputs
-  float *up_grad;                   // backward, layer 1
+  float *ug_edge;                   // backward, layer 1: per-edge up-gradient rows [e - e_base][IN][128]
   float4 *edge_force;               // backward output
   int *status;
 };
@@ -192,6 +193,7 @@ __global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBl
         m.cut = a.cut[me];
         m.den = a.den[me];
         m.sender = j = a.sender[me];
+        m.row = me - a.e_base;
       }
       int tend = min(ntiles, c0 + kChunkTiles);
       for (int t = c0; t < tend; ++t) {
@@ -265,6 +267,14 @@ __global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBl
     const unsigned char *st = smem + s * S::BYTES;
     const EdgeMeta *meta = reinterpret_cast<const EdgeMeta *>(st + S::META);
     int cnt = min(T, end - (begin + t * T));
+    if constexpr (Bwd && L > 0) {
+      // This thread's entries of the stage's up-gradient rows start at zero (the bulk store
+      // that last read them finished before the barrier above).
+      float *ugs = reinterpret_cast<float *>(const_cast<unsigned char *>(st) + S::UG) + c;
+#pragma unroll
+      for (int q = 0; q < T * IN; ++q)
+        ugs[q * 128] = 0.f;
+    }
     for (int k = 0; k < cnt; ++k) {
       const V *Rk = reinterpret_cast<const V *>(st + S::R + k * S::ROW) + c;
       const V *Uk = reinterpret_cast<const V *>(st + S::U + k * IN * 512) + c;
@@ -296,12 +306,11 @@ __global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBl
         rsum += meta[k].den.x;
       } else {
         const V *dRk = reinterpret_cast<const V *>(st + S::DR + k * S::ROW) + c;
-        V w[P], dw[P];
+        // dw = dcut b + dR' is formed after the term loop, where it is used (fewer live registers).
+        V w[P];
 #pragma unroll
-        for (int p = 0; p < P; ++p) {
+        for (int p = 0; p < P; ++p)
           w[p] = vfma(bcast<V>(cv.x), bias[p], Rk[p * CS]);
-          dw[p] = vfma(bcast<V>(cv.y), bias[p], dRk[p * CS]);
-        }
         V Q[P], Tsh[16], ug[IN];
 #pragma unroll
         for (int p = 0; p < P; ++p)
@@ -334,15 +343,18 @@ __global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBl
           }
         });
         if constexpr (L > 0) {
-          int j = meta[k].sender;
+          // An add onto the zeroed slot (0 + x = x exactly): a reduction instruction here keeps
+          // the compiler from interleaving the next edge's loads, which would spill registers.
+          static_assert(W == 1, "the up-gradient staging assumes one channel per thread");
+          float *dst = reinterpret_cast<float *>(const_cast<unsigned char *>(st) + S::UG + k * IN * 512) + c;
 #pragma unroll
           for (int q = 0; q < IN; ++q)
-            vatomic_add(reinterpret_cast<V *>(a.up_grad + (size_t(q) * a.n_up + j) * 128) + c, ug[q]);
+            atomicAdd(dst + q * 128, hsum(ug[q]));
         }
         V dr2 = vzero<V>();
 #pragma unroll
         for (int p = 0; p < P; ++p)
-          dr2 = vfma(Q[p], dw[p], dr2);
+          dr2 = vfma(Q[p], vfma(bcast<V>(cv.y), bias[p], dRk[p * CS]), dr2);
         V g2[3] = {vzero<V>(), vzero<V>(), vzero<V>()};
         const float4 *g4 = reinterpret_cast<const float4 *>(st + S::DY + k * 192);
 #pragma unroll
@@ -361,7 +373,19 @@ __global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBl
       }
     }
     if constexpr (Bwd) {
+      if constexpr (L > 0)
+        tc::fence_proxy_async_smem();
       asm volatile("bar.sync 1, %0;" ::"r"(kCT) : "memory");
+      if constexpr (L > 0) {
+        // One bulk store of the tile's rows (contiguous: consecutive edges); before the next
+        // tile starts, the store issued NS - 1 = 1 tiles ago has finished reading its stage.
+        static_assert(kStages == 2, "the up-gradient staging assumes a 2-stage ring");
+        if (c == 0) {
+          tc::bulk_store(a.ug_edge + size_t(meta[0].row) * IN * 128, smem_u32(st + S::UG), unsigned(cnt) * IN * 512);
+          tc::bulk_commit();
+          tc::bulk_wait_read1();
+        }
+      }
       if (c < cnt) {
         int e = begin + t * T + c;
         float sum[4];
@@ -384,6 +408,10 @@ __global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBl
       }
     }
     mbar_arrive(empty0 + 8 * s);
+  }
+  if constexpr (Bwd && L > 0) {
+    if (c == 0)
+      tc::bulk_wait(); // the last tiles' up-gradient stores are complete
   }
   if constexpr (!Bwd) {
     if (ok) {
@@ -456,7 +484,7 @@ void launch_message_forward_proj(cudaStream_t s, int layer, const DeviceGeometry
 void launch_message_backward_proj(cudaStream_t s, int layer, const DeviceGeometry &g, const Layer &l,
                                   EdgeArrays ea, RadialOut ro, const ProjectionChunk &k, const float *R,
                                   const float *dR, const float *up, const float *message_grad,
-                                  const float *density_grad, float *up_grad, float4 *edge_force, bool accumulate,
+                                  const float *density_grad, float *ug_edge, float4 *edge_force, bool accumulate,
                                   int n_up) {
   int blocks = k.r1 - k.r0;
   if (blocks <= 0)
@@ -465,7 +493,7 @@ void launch_message_backward_proj(cudaStream_t s, int layer, const DeviceGeometr
   a.dR = dR;
   a.msg_grad = message_grad;
   a.rho_grad = density_grad;
-  a.up_grad = up_grad;
+  a.ug_edge = ug_edge;
   a.edge_force = edge_force;
   if (layer == 0) {
     if (accumulate)

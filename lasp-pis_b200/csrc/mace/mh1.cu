@@ -161,7 +161,7 @@ std::vector<Result> MH1::compute(bool batch) {
   launch_zbl(s, c.geometry, m.constants_dev, m.zbl_radii, m.zbl_c, cst[7], energy, force, virial);
   // Projection path: radial projections on the tensor cores into chunk buffers, tensor
   // products from those (default); otherwise the fused SIMT edge kernels.
-  bool projection = tensor_core_linears() && m.layers[0].radial.out_hi && m.layers[1].radial.out_hi;
+  bool projection = projection_edges() && m.layers[0].radial.out_hi && m.layers[1].radial.out_hi;
   if (dom && !projection)
     throw Error("Domain decomposition requires the tensor-core projection path");
   std::vector<ProjectionChunk> chunks;
@@ -247,6 +247,14 @@ std::vector<Result> MH1::compute(bool batch) {
   float *rawgrad = node("mh.b.raw", 9728), *rhograd = node("mh.b.rho", 1);
   float *msggrad = msg, *upgrad = sender_node("mh.b.up", 512);
   float4 *edge_force = c.array<float4>("mh.edge.force", E);
+  // Layer-1 up-gradients: every edge's row is written once by the edge backward and summed
+  // onto its sender in ascending edge order (no float atomics, reproducible bit for bit).
+  // On the projection path the rows reuse the layer-0 dR' half of proj[0], which is free until
+  // the layer-0 backward (chunk_cap x 512 floats, exactly one row per chunk edge).
+  if (projection && m.layers[0].paths * 128 < 512)
+    throw Error("layer-0 projection buffer too small for the up-gradient rows");
+  SenderIndex senders_of = build_sender_index(s, c, (long long)E, ns, c.geometry.edge_sender);
+  float *ug_edge = projection ? proj[0] + size_t(chunk_cap) * 512 : c.array<float>("mh.edge.ug", E * 512);
   launch_fill(s, n, one, cst[6]);
   linear(s, n, m.read1down, one, rgrad, true, false, status);
   launch_readout_act(s, n * 16, rpre, rgrad, rdpre, cst[13], true);
@@ -286,12 +294,19 @@ std::vector<Result> MH1::compute(bool batch) {
           tc_gemm(s, rows, width, 64, 2, ro[k].h + q.e0 * 64, (long long)E * 64, l.radial.out_hi,
                   l.radial.out_lo, R, width, (long long)chunk_cap * width, false, status);
         timer.mark("backward" + std::to_string(k) + ".projection");
-        launch_message_backward_proj(s, k, c.geometry, l, ea, ro[k], q, R, dR, up[k], msggrad, rhograd, upgrad,
+        launch_message_backward_proj(s, k, c.geometry, l, ea, ro[k], q, R, dR, up[k], msggrad, rhograd, ug_edge,
                                      edge_force, k == 0, ns);
         timer.mark("backward" + std::to_string(k) + ".edges");
+        if (k == 1) {
+          launch_sender_gather(s, senders_of, q.e0, q.e1, ug_edge, 4, upgrad, ns);
+          timer.mark("backward1.sender-gather");
+        }
       }
-    } else
-      launch_message_backward(s, k, c.geometry, l, ea, ro[k], up[k], msggrad, rhograd, upgrad, edge_force, k == 0);
+    } else {
+      launch_message_backward(s, k, c.geometry, l, ea, ro[k], up[k], msggrad, rhograd, ug_edge, edge_force, k == 0);
+      if (k == 1)
+        launch_sender_gather(s, senders_of, 0, (long long)E, ug_edge, 4, upgrad, ns);
+    }
     timer.mark("backward" + std::to_string(k) + ".edges");
     if (k == 1) {
       if (dom)
@@ -303,6 +318,7 @@ std::vector<Result> MH1::compute(bool batch) {
   }
   if (dom) {
     launch_force_gather_domain(s, c.geometry, edge_force, force, virial);
+    launch_ghost_reactions(s, senders_of, n, edge_force, force);
     dom->return_ghost_rows(c, force, 1, ns, 3);
   } else {
     launch_force_gather(s, c.geometry, edge_force, force, virial);

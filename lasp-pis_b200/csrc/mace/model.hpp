@@ -114,9 +114,11 @@ void launch_radial(cudaStream_t, const lapis::DeviceGeometry &, const Layer &, c
                    RadialOut, bool scaled = false);
 void launch_message_forward(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &, EdgeArrays,
                             RadialOut, const float *up, float *message, float *density);
+// ug_edge (layer 1): each edge's up-projection gradient, [E][4][128]; summed onto the senders
+// by launch_sender_gather.
 void launch_message_backward(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &,
                              EdgeArrays, RadialOut, const float *up, const float *message_grad,
-                             const float *density_grad, float *up_grad, float4 *edge_force, bool accumulate);
+                             const float *density_grad, float *ug_edge, float4 *edge_force, bool accumulate);
 CUtensorMap tc_map_2d(const float *base, int cols, long long rows, int box_cols, int box_rows);
 // Projection path (edge_proj.cu): the radial projection R = h W (and dR = dh W) runs as a
 // tensor-core GEMM into a buffer covering the edges of receivers [r0, r1) = [e0, e1); the
@@ -129,19 +131,35 @@ struct ProjectionChunk {
 void launch_message_forward_proj(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &, EdgeArrays,
                                  RadialOut, const ProjectionChunk &, const float *R, const float *up,
                                  float *message, float *density, int n_up = 0);
+// ug_edge (layer 1): the chunk's per-edge up-projection gradients, row e - e0 of [rows][4][128].
 void launch_message_backward_proj(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &,
                                   EdgeArrays, RadialOut, const ProjectionChunk &, const float *R, const float *dR,
                                   const float *up, const float *message_grad, const float *density_grad,
-                                  float *up_grad, float4 *edge_force, bool accumulate, int n_up = 0);
+                                  float *ug_edge, float4 *edge_force, bool accumulate, int n_up = 0);
 // Edges per projection chunk (bounds the R / dR buffers at 2 x 1280 floats per edge):
 // 2^20, or MACE_PROJECTION_CHUNK_EDGES when set to a positive value.
 long long projection_chunk_edges();
 void launch_force_gather(cudaStream_t, const lapis::DeviceGeometry &, const float4 *edge_force, float *force,
                          float *virial);
-// Domain-decomposed form: reverse edges outside the local graph (index < 0) are skipped and
-// every edge's reaction on a ghost sender (rows >= g.n of force) is accumulated for its owner.
+// Domain-decomposed form: reverse edges outside the local graph (index < 0) are skipped; the
+// reactions on ghost senders come from launch_ghost_reactions.
 void launch_force_gather_domain(cudaStream_t, const lapis::DeviceGeometry &, const float4 *edge_force, float *force,
                                 float *virial);
+
+// Sender index (sender_gather.cu): for each sender j < n, its edges in ascending edge order,
+// edges[offsets[j] .. offsets[j + 1]).  Sender-side sums run over it in that order, so they
+// are bitwise reproducible (no float atomics).
+struct SenderIndex {
+  int n;
+  int *offsets, *edges;
+};
+SenderIndex build_sender_index(cudaStream_t, lapis::Context &, long long E, int n_senders, const int *sender);
+// out[q][j][c] (row stride `stride`) += sum over sender j's edges e in [e0, e1) of
+// rows[e - e0][q][c], for q < comps (4) and 128 channels c.
+void launch_sender_gather(cudaStream_t, const SenderIndex &, long long e0, long long e1, const float *rows, int comps,
+                          float *out, int stride);
+// force[j] -= sum of the edge forces of ghost sender j, for j in [n_own, index.n).
+void launch_ghost_reactions(cudaStream_t, const SenderIndex &, int n_own, const float4 *edge_force, float *force);
 
 // Equivariant linear over n nodes: Y (+)= X W per path and component, or the transposed
 // product for the backward.  Paths with tensor-core-eligible shapes run on tc_gemm.
@@ -172,6 +190,9 @@ void tc_gemm_group(cudaStream_t, const GemmSpec *specs, int count, int *status);
 void split_tf32(const float *w, size_t count, float *hi, float *lo);
 // Use the tensor-core path in linear() (default true; MACE_SIMT_LINEARS=1 disables).
 bool tensor_core_linears();
+// Edge kernels over tensor-core radial projections (default true; false with SIMT linears or
+// MACE_SIMT_EDGES=1, which selects the fused SIMT edge kernels).
+bool projection_edges();
 // pre = raw / (alpha + beta density) + res is not stored: the backward recomputes it from raw
 // and res (the same FP32 expression, so the same values).  pre_grad may alias res.
 void launch_normalize_gate(cudaStream_t, int n, const float *raw, const float *res, const float *density,

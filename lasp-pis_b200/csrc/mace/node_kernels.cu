@@ -596,6 +596,14 @@ bool tensor_core_linears() {
   return on;
 }
 
+bool projection_edges() {
+  static const bool on = [] {
+    const char *v = std::getenv("MACE_SIMT_EDGES");
+    return tensor_core_linears() && !(v && v[0] == '1');
+  }();
+  return on;
+}
+
 void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bool backward, bool add, int *status,
             int nx, int ny) {
   if (!n)

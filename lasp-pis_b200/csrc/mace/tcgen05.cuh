@@ -166,6 +166,16 @@ __device__ __forceinline__ void bulk_load(unsigned dst, const void *src, unsigne
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Shared -> global bulk copy (both addresses 16-byte aligned, bytes a multiple of 16), in the
+// calling thread's bulk group.
+__device__ __forceinline__ void bulk_store(void *dst, unsigned src, unsigned bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+}
+// At most one of the calling thread's bulk groups still reading shared memory.
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+// Generic-proxy shared-memory writes before this fence are visible to later bulk copies.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 // Wait until the issued bulk copies have read their shared-memory source / fully completed.
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
