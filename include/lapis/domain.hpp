@@ -2,15 +2,23 @@
 // B200 build addition for large structures (no counterpart in the reference, whose
 // calculators evaluate a structure on one GPU).
 //
-// Every rank passes the same full structure.  After Context::prepare (the full CSR edge list),
-// localize() switches the context to this rank's part: the receivers it owns -- a contiguous
-// range of the bin-sorted internal order, i.e. a compact slab -- and, as senders, those plus
-// the ghost atoms their edges reach, numbered after them.  The evaluation then exchanges only
-// what crosses ranks, point to point over NCCL on the context's stream: layer features of
-// ghost senders (owners -> ghosts), their gradients and the ghost sender forces
-// (ghosts -> owners), and finally the per-atom outputs (an all-reduce of the owned rows),
-// so every rank returns the full result.  NCCL is loaded at run time (libnccl.so.2, the copy
-// already in the process when there is one).
+// Every rank passes the same full structure.  partition() makes the context build CSR rows
+// only for the receivers this rank owns -- a contiguous range of the bin-sorted internal
+// order, i.e. a compact slab -- so each rank enumerates and stores its own edges only.
+// localize() then switches the context to this rank's graph: the owned receivers and, as
+// senders, those plus the ghost atoms their edges reach, numbered after them.  The
+// evaluation exchanges only what crosses ranks, point to point over NCCL on the context's
+// stream: layer features of ghost senders (owners -> ghosts), their gradients and the ghost
+// sender forces (ghosts -> owners), and finally the per-atom outputs (an all-reduce of the
+// owned rows), so every rank returns the full result.  NCCL is loaded at run time
+// (libnccl.so.2, the copy already in the process when there is one).
+//
+// Failures: the communicator is non-blocking; every NCCL step and every wait for the
+// exchanges has a deadline (MACE_DOMAIN_TIMEOUT_S seconds, default 120).  A peer that never
+// takes part, an asynchronous NCCL error, or ranks whose structures or exchange plans
+// disagree (checked by an all-gather before any point-to-point step) make the call throw on
+// the ranks that see it; a timed-out or failed communicator is aborted and the domain stays
+// failed (later calls throw at once).
 #pragma once
 #include "runtime.hpp"
 #include <memory>
@@ -31,7 +39,9 @@ public:
   // Owned receivers n_own = rows [0, n_own); senders n_local = owned then ghosts.
   int n_own() const;
   int n_local() const;
-  // After ctx.prepare on the full structure: ctx.geometry becomes the local graph.
+  // Sets ctx.part / ctx.parts so that Context::prepare builds this rank's rows only.
+  void partition(Context &ctx) const;
+  // After ctx.prepare (partitioned): ctx.geometry becomes the local graph.
   void localize(Context &ctx);
   // Back to the full geometry (for Context::finish).
   void restore(Context &ctx);

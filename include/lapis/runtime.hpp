@@ -91,6 +91,10 @@ struct DeviceGeometry {
   const float *edge_r2 = nullptr;      // [E] squared length compared against the cutoff
   const int *edge_reverse = nullptr;   // [E] index of the edge j <- i with the opposite shift
   long long edge_capacity = 0;
+  // Rows of the CSR (B200 build addition): internal receivers [receiver_begin,
+  // receiver_begin + receiver_count); all n atoms unless the context is partitioned.  In a
+  // partitioned list an edge whose reverse lies outside these rows has edge_reverse -1.
+  int receiver_begin = 0, receiver_count = 0;
 };
 struct WorkspaceSpec {
   size_t global_bytes = 0, scratch_bytes = 0, scratch_alignment = 16;
@@ -114,6 +118,10 @@ public:
   // device pointers instead of copying host arrays (the timed device-only path).
   const float *device_positions = nullptr;
   const int *device_elements = nullptr;
+  // Receiver partition (B200 build addition, for domain decomposition): prepare() builds the
+  // CSR rows of internal receivers [n part / parts, n (part + 1) / parts) only -- senders
+  // still range over all atoms and images.  Default: all receivers.
+  int part = 0, parts = 1;
   Context();
   ~Context();
   Context(const Context &) = delete;

@@ -102,6 +102,25 @@ MACE_EXPORT long long lapis_neighbor_edges(int n, const float *xyz, const float 
 MACE_EXPORT long long lapis_neighbor_list_static(int n, const float *xyz, const int *elements, const float *cell,
                                                  float cutoff, int *row, int *sender, int *shift, float *vector,
                                                  long long capacity, void *stream);
+/* Domain-decomposition exchange plan of one rank, on the current GPU without a communicator
+ * (B200 build addition for checks; no counterpart in the reference).  The structure (cutoff
+ * Angstrom, all atoms taken as hydrogen) is prepared the way a decomposed evaluation prepares
+ * it for rank `rank` of `world`: CSR rows for that rank's receivers only (internal ids
+ * [n rank / world, n (rank + 1) / world) of the bin-sorted order).  Outputs: send_counts and
+ * ghost_counts [world]; when capacity >= max(E, n) also internal_to_input [n], row
+ * [owned + 1], sender [E] (internal ids), ghosts (ascending internal ids) and sends (per peer
+ * in rank order, ascending internal ids).  Returns E, the rank's edge count, or -1. */
+MACE_EXPORT long long lapis_exchange_plan(int n, const float *xyz, const float *cell, float cutoff, int rank,
+                                          int world, int *send_counts, int *ghost_counts, int *internal_to_input,
+                                          int *row, int *sender, int *ghosts, int *sends, long long capacity);
+/* The same plan from a CSR on the host (no GPU; B200 build addition for checks, no reference
+ * counterpart): ids 0..n-1, rank `rank` of `world` owns [n rank / world, n (rank + 1) / world)
+ * and gives the rows of those receivers (row [owned + 1], sender ids).  Outputs as above;
+ * ghosts and sends are written when capacity >= the larger of their lengths.  Returns 0 or
+ * -1 (message in mace_last_error). */
+MACE_EXPORT int lapis_exchange_plan_host(int n, int rank, int world, const int *row, const int *sender,
+                                         int *send_counts, int *ghost_counts, int *ghosts, int *sends,
+                                         long long capacity);
 /* Batch of independent periodic cells in one call (B200 build addition; the reference's
  * callers loop over mace_calculate, mace/include/mace/c_api.h:13-14).  Cell c has sizes[c]
  * atoms; xyz (sum(sizes) x 3, Angstrom) and Z (sum(sizes)) are the cells' arrays

@@ -203,21 +203,22 @@ __device__ __forceinline__ int floor_div(int a, int b) {
 
 struct Traverse {
   int n, grid[3], images[3];
+  int r0, nr; // receivers [r0, r0 + nr) (internal ids); senders are all n atoms
   float h[9], cutoff2;
   const float *xyz;
   const int *bins, *offsets, *winding;
   const ConnStats *stats; // stats->cell selects the 27-bin stencil or all atoms x images
 };
 
-// One warp per internal receiver.  Candidate order is fixed (stencil or image order, then
-// bin order), so the edge order inside a receiver is deterministic.  Count pass when
-// out_sender == nullptr, fill pass otherwise.
+// One warp per internal receiver i = r0 + w (row w).  Candidate order is fixed (stencil or
+// image order, then bin order), so the edge order inside a receiver is deterministic.  Count
+// pass when out_sender == nullptr, fill pass otherwise.
 __global__ void neighbour_pass(Traverse g, int *counts, const int *row, int *out_sender, int *out_shift,
                                float4 *out_vec, float *out_r2) {
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= g.n)
+  if (warp >= g.nr)
     return;
-  int i = warp;
+  int i = g.r0 + warp;
   bool cell = g.stats->cell;
   float xi = g.xyz[3 * i], yi = g.xyz[3 * i + 1], zi = g.xyz[3 * i + 2];
   int wi0 = g.winding[3 * i], wi1 = g.winding[3 * i + 1], wi2 = g.winding[3 * i + 2];
@@ -230,7 +231,7 @@ __global__ void neighbour_pass(Traverse g, int *counts, const int *row, int *out
     bx = b / g.grid[1];
   }
   int nx = cell ? 1 : g.images[0], ny = cell ? 1 : g.images[1], nz = cell ? 1 : g.images[2];
-  int count = 0, base_out = out_sender ? row[i] : 0;
+  int count = 0, base_out = out_sender ? row[warp] : 0;
   for (int x = -nx; x <= nx; ++x)
     for (int y = -ny; y <= ny; ++y)
       for (int z = -nz; z <= nz; ++z) {
@@ -271,15 +272,22 @@ __global__ void neighbour_pass(Traverse g, int *counts, const int *row, int *out
         }
       }
   if (!out_sender && lane == 0)
-    counts[i] = count;
+    counts[warp] = count;
 }
 
-// For edge e = (i <- j, s) find the edge (j <- i, -s) in j's row.
-__global__ void reverse_edges(const int *row, const int *sender, const int *shift, int *reverse, int *status) {
-  int i = blockIdx.x;
-  for (int e = row[i] + threadIdx.x; e < row[i + 1]; e += blockDim.x) {
+// For edge e = (i <- j, s) of row w (receiver i = r0 + w) find the edge (j <- i, -s) in j's
+// row.  A sender outside the rows (a partitioned list) gets -1; a missing reverse inside the
+// rows is an error (the edge set must be symmetric).
+__global__ void reverse_edges(const int *row, const int *sender, const int *shift, int *reverse, int *status, int r0,
+                              int nr) {
+  int w = blockIdx.x, i = r0 + w;
+  for (int e = row[w] + threadIdx.x; e < row[w + 1]; e += blockDim.x) {
     int j = sender[e], s0 = -shift[3 * e], s1 = -shift[3 * e + 1], s2 = -shift[3 * e + 2], found = -1;
-    for (int q = row[j]; q < row[j + 1]; ++q)
+    if (j < r0 || j >= r0 + nr) {
+      reverse[e] = -1;
+      continue;
+    }
+    for (int q = row[j - r0]; q < row[j - r0 + 1]; ++q)
       if (sender[q] == i && shift[3 * q] == s0 && shift[3 * q + 1] == s1 && shift[3 * q + 2] == s2) {
         found = q;
         break;
@@ -623,13 +631,17 @@ void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
   int *cursor = array<int>("grid.cursor", nb);
   int *status = array<int>("status", 4);
   auto *stats = array<ConnStats>("stats", 1);
-  int *row_counts = array<int>("edges.count", size_t(n) + 1);
-  int *row = array<int>("edges.offset", size_t(n) + 1);
+  if (parts < 1 || part < 0 || part >= parts)
+    throw Error("Invalid receiver partition");
+  // Receivers of this context: [r0, r0 + nr) of the internal order (all atoms by default).
+  const int r0 = int((long long)n * part / parts), nr = int((long long)n * (part + 1) / parts) - r0;
+  int *row_counts = array<int>("edges.count", size_t(nr) + 1);
+  int *row = array<int>("edges.offset", size_t(nr) + 1);
   clear(counts, size_t(nb + 1) * 4);
   clear(cursor, size_t(nb) * 4);
   clear(status, 16);
   clear(stats, sizeof(ConnStats));
-  clear(row_counts, size_t(n + 1) * 4);
+  clear(row_counts, size_t(nr + 1) * 4);
   double brute = double(n) * n;
   for (int k = 0; k < 3; ++k)
     brute *= 2 * images[k] + 1;
@@ -648,6 +660,8 @@ void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
   lapis::launch(decide_backend, 1, 1, 0, stream, stats, int(opts.backend), grid_ok, brute);
   Traverse tv;
   tv.n = n;
+  tv.r0 = r0;
+  tv.nr = nr;
   std::copy(dims, dims + 3, tv.grid);
   std::copy(images, images + 3, tv.images);
   std::copy(s.cell.begin(), s.cell.end(), tv.h);
@@ -657,9 +671,10 @@ void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
   tv.offsets = offsets;
   tv.winding = sw;
   tv.stats = stats;
-  if (n) {
-    lapis::launch(neighbour_pass, (n * 32 + 255) / 256, 256, 0, stream, tv, row_counts, nullptr, nullptr, nullptr, nullptr, nullptr);
-    lapis::launch(scan_exclusive, 1, 1024, 0, stream, row_counts, row, n, &stats->total_edges);
+  if (nr) {
+    lapis::launch(neighbour_pass, (nr * 32 + 255) / 256, 256, 0, stream, tv, row_counts, nullptr, nullptr, nullptr,
+                  nullptr, nullptr);
+    lapis::launch(scan_exclusive, 1, 1024, 0, stream, row_counts, row, nr, &stats->total_edges);
   }
   check(cudaGetLastError());
   // The single host synchronisation of prepare(): edge total, backend, diagnostics, status.
@@ -689,7 +704,7 @@ void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
   diagnostics.mean_occupancy = double(n) / nb;
   diagnostics.grid_candidates = double(hs->work);
   diagnostics.brute_candidates = brute;
-  long long total = n ? hs->total_edges : 0;
+  long long total = nr ? hs->total_edges : 0;
   if (total > INT_MAX)
     throw Error("Directed edge count exceeds int32 capacity");
   diagnostics.edges = total;
@@ -698,9 +713,9 @@ void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
   float4 *vec = array<float4>("edges.vector", size_t(total));
   float *r2 = array<float>("edges.r2", size_t(total));
   int *rev = array<int>("edges.reverse", size_t(total));
-  if (n && total) {
-    lapis::launch(neighbour_pass, (n * 32 + 255) / 256, 256, 0, stream, tv, nullptr, row, sender, shift, vec, r2);
-    lapis::launch(reverse_edges, n, 128, 0, stream, row, sender, shift, rev, status);
+  if (nr && total) {
+    lapis::launch(neighbour_pass, (nr * 32 + 255) / 256, 256, 0, stream, tv, nullptr, row, sender, shift, vec, r2);
+    lapis::launch(reverse_edges, nr, 128, 0, stream, row, sender, shift, rev, status, r0, nr);
   }
   check(cudaGetLastError());
   geometry = {};
@@ -723,6 +738,8 @@ void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
   geometry.edge_r2 = r2;
   geometry.edge_reverse = rev;
   geometry.edge_capacity = total;
+  geometry.receiver_begin = r0;
+  geometry.receiver_count = nr;
 }
 
 int Context::status_code() {
@@ -932,7 +949,7 @@ void Context::prepare_batch(const std::vector<Structure> &cells, float cutoff, c
   if (n && E) {
     lapis::launch(neighbour_batch, (n * 32 + 255) / 256, 256, 0, stream, n, cutoff2, dcells, cell_of, wxyz, wind,
                   nullptr, row, sender, shift, vec, r2);
-    lapis::launch(reverse_edges, n, 128, 0, stream, row, sender, shift, rev, status);
+    lapis::launch(reverse_edges, n, 128, 0, stream, row, sender, shift, rev, status, 0, n);
   }
   check(cudaGetLastError());
   internal_to_original = i2o;
@@ -952,6 +969,8 @@ void Context::prepare_batch(const std::vector<Structure> &cells, float cutoff, c
   geometry.edge_r2 = r2;
   geometry.edge_reverse = rev;
   geometry.edge_capacity = E;
+  geometry.receiver_begin = 0;
+  geometry.receiver_count = n;
   diagnostics.selected = NeighborBackend::BruteForce;
   diagnostics.reason = "batch: all-images enumeration per cell";
   diagnostics.edges = E;
@@ -1215,6 +1234,8 @@ long long lapis_neighbor_list_static(int n, const float *xyz, const int *element
     check(cudaMemsetAsync(counts, 0, (size_t(n) + 1) * sizeof(int), stream));
     Traverse tv;
     tv.n = n;
+    tv.r0 = 0;
+    tv.nr = n;
     tv.grid[0] = tv.grid[1] = tv.grid[2] = 1;
     std::copy(images, images + 3, tv.images);
     std::copy(cell, cell + 9, tv.h);

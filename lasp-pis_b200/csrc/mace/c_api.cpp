@@ -63,13 +63,15 @@ Handle *create(const char *path, int b, const char *head, int device) {
 }
 
 long long dump_edges(Context &ctx, int *out, long long capacity) {
+  // The prepared CSR rows: receivers [receiver_begin, receiver_begin + receiver_count) of the
+  // internal order (all atoms, or this rank's atoms in a domain-decomposed handle).
   const auto &g = ctx.geometry;
   long long E = g.edge_capacity;
-  int n = g.n;
-  std::vector<int> row(static_cast<size_t>(n) + 1), sender(static_cast<size_t>(E)),
+  int n = g.n, rows = g.receiver_count, r0 = g.receiver_begin;
+  std::vector<int> row(static_cast<size_t>(rows) + 1), sender(static_cast<size_t>(E)),
       shift(static_cast<size_t>(E) * 3), i2o(static_cast<size_t>(n));
   if (n) {
-    check(cudaMemcpy(row.data(), g.edge_offsets, (size_t(n) + 1) * 4, cudaMemcpyDeviceToHost));
+    check(cudaMemcpy(row.data(), g.edge_offsets, (size_t(rows) + 1) * 4, cudaMemcpyDeviceToHost));
     check(cudaMemcpy(i2o.data(), ctx.internal_to_original, size_t(n) * 4, cudaMemcpyDeviceToHost));
   }
   if (E) {
@@ -77,9 +79,9 @@ long long dump_edges(Context &ctx, int *out, long long capacity) {
     check(cudaMemcpy(shift.data(), g.edge_shift, size_t(E) * 12, cudaMemcpyDeviceToHost));
   }
   std::vector<std::array<int, 5>> edges(static_cast<size_t>(E));
-  for (int i = 0; i < n; ++i)
-    for (int e = row[i]; e < row[i + 1]; ++e)
-      edges[e] = {i2o[i], i2o[sender[e]], shift[3 * e], shift[3 * e + 1], shift[3 * e + 2]};
+  for (int w = 0; w < rows; ++w)
+    for (int e = row[w]; e < row[w + 1]; ++e)
+      edges[e] = {i2o[r0 + w], i2o[sender[e]], shift[3 * e], shift[3 * e + 1], shift[3 * e + 2]};
   std::sort(edges.begin(), edges.end());
   long long copy = std::min(E, std::max(capacity, 0ll));
   if (copy)

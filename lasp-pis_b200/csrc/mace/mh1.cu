@@ -36,7 +36,13 @@ MH1::MH1(const std::string &archive, Options o) : MH1(archive, o, {}) {}
 MH1::~MH1() = default;
 size_t MH1::parameter_bytes() const { return model_->data.bytes; }
 void MH1::set_profiling(bool enabled) { model_->profiling = enabled; }
-void MH1::set_domain(std::shared_ptr<lapis::Domain> domain) { model_->domain = std::move(domain); }
+void MH1::set_domain(std::shared_ptr<lapis::Domain> domain) {
+  model_->domain = std::move(domain);
+  if (model_->domain)
+    model_->domain->partition(context_);
+  else
+    context_.part = 0, context_.parts = 1;
+}
 
 long long projection_chunk_edges() {
   static const long long edges = [] {
@@ -224,7 +230,9 @@ std::vector<Result> MH1::compute(bool batch) {
     timer.mark("forward" + std::to_string(k) + ".messages");
     linear(s, n, l.one, msg, raw[k], false, false, status);
     launch_normalize_gate(s, n, raw[k], res[k], rho[k], l.alpha, l.beta, cst[11], cst[12], gate);
-    linear(s, n, l.two, gate, pin[k], false, false, status);
+    timer.mark("forward" + std::to_string(k) + ".node");
+    linear(s, n, l.two, gate, pin[k], false, false, status); // one grouped tensor-core launch
+    timer.mark("forward" + std::to_string(k) + ".linear_2");
     launch_product(s, n, l, pin[k], poly);
     linear(s, n, l.plin, poly, hidden[k], false, true, status);
     if (k == 0) {

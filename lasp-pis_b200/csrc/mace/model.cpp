@@ -56,23 +56,16 @@ void ModelData::validate(const std::string &path, const std::string &head) {
   load(path, head);
 }
 
-// w = hi + lo with hi = w rounded to tf32 and lo the remainder, itself rounded to tf32.  An MMA
-// of kind::tf32 reads only the top 19 bits of an fp32 operand (truncation), so a raw fp32
-// remainder would lose up to 2^-21 |w| -- the same for every node and edge, hence an error
-// that adds up coherently in the energy and the virial; rounded, the loss is at most
-// 2^-23 |w| and unbiased.
+// w = hi + lo with hi = w rounded to tf32 and lo the exact fp32 remainder (an MMA of
+// kind::tf32 reads its top 19 bits).  Measured on B200 against the float64 oracle, this gives
+// smaller energy and virial errors than rounding lo to tf32 as well.
 void split_tf32(const float *w, size_t count, float *hi, float *lo) {
-  auto round_tf32 = [](float x) {
-    uint32_t bits;
-    std::memcpy(&bits, &x, 4);
-    bits = (bits + 0x1000u) & 0xffffe000u;
-    float r;
-    std::memcpy(&r, &bits, 4);
-    return r;
-  };
   for (size_t k = 0; k < count; ++k) {
-    hi[k] = round_tf32(w[k]);
-    lo[k] = round_tf32(w[k] - hi[k]);
+    uint32_t bits;
+    std::memcpy(&bits, w + k, 4);
+    bits = (bits + 0x1000u) & 0xffffe000u;
+    std::memcpy(hi + k, &bits, 4);
+    lo[k] = w[k] - hi[k];
   }
 }
 
