@@ -45,10 +45,15 @@ public:
   void localize(Context &ctx);
   // Back to the full geometry (for Context::finish).
   void restore(Context &ctx);
-  // Rows [n_own, n_local) of x ([comps][stride][width] floats) from their owners.
+  // Rows [n_own, n_local) of x ([comps][stride][width] floats) from their owners.  Runs on the
+  // domain's own stream after the work enqueued so far on ctx.stream; call join() before
+  // ctx.stream reads the ghost rows (work that does not read them may run meanwhile).
   void fetch_ghost_rows(Context &ctx, float *x, int comps, int stride, int width);
-  // Adds rows [n_own, n_local) of x into the owners' rows (ghosts -> owners).
+  // Adds rows [n_own, n_local) of x into the owners' rows (ghosts -> owners); asynchronous
+  // like fetch_ghost_rows: join() before ctx.stream reads the owned rows of x.
   void return_ghost_rows(Context &ctx, float *x, int comps, int stride, int width);
+  // ctx.stream waits for the exchanges issued so far.
+  void join(Context &ctx);
   // Owned rows of e [n_own], f [n_own][3], v [n_own][9] into full-structure arrays (internal
   // order), summed over ranks so every rank holds all atoms.  ef, ff, vf must be one contiguous
   // buffer: ff = ef + n, vf = ef + 4 n (n = full atom count).

@@ -248,6 +248,16 @@ struct Domain::Impl {
   std::vector<int> send_count, ghost_off, ghost_count; // per peer
   std::vector<int *> send_list;                        // per peer: local row ids to send (device)
   cudaEvent_t done = nullptr;
+  // Every NCCL operation runs on `exchange`, a stream of the domain: the model stream hands
+  // over with `ready` and waits for `finished` only where it needs the result (join), so the
+  // transfers overlap the model's independent work.
+  cudaStream_t exchange = nullptr;
+  cudaEvent_t ready = nullptr, finished = nullptr;
+  void hand_over(cudaStream_t from) {
+    check(cudaEventRecord(ready, from));
+    check(cudaStreamWaitEvent(exchange, ready, 0));
+  }
+  void mark_finished() { check(cudaEventRecord(finished, exchange)); }
 
   // The communicator becomes unusable: abort it (which also releases NCCL kernels that wait
   // on a peer) and remember why.
@@ -263,6 +273,14 @@ struct Domain::Impl {
     if (failed)
       throw Error("Domain communicator failed earlier: " + failure);
   }
+  // Polling back-off: yield for the first ~20,000 polls (tens of microseconds to a few
+  // milliseconds -- the usual wait, where a sleep would leave the GPU idle), then sleep 50 us.
+  static void pause(long long spins) {
+    if (spins < 20000)
+      std::this_thread::yield();
+    else
+      std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
   // Host side of a non-blocking NCCL step: the call itself, then its completion state polled
   // until it leaves ncclInProgress (deadline: the domain timeout).
   void step(ncclResult_t r, const char *what) {
@@ -270,6 +288,7 @@ struct Domain::Impl {
     if (r != ncclSuccess && r != ncclInProgress)
       fail(std::string(what) + ": " + N.error_string(r));
     auto deadline = std::chrono::steady_clock::now() + std::chrono::duration<double>(timeout_seconds());
+    long long spins = 0;
     for (;;) {
       ncclResult_t st = ncclSuccess;
       ncclResult_t q = N.comm_get_async_error(comm, &st);
@@ -281,7 +300,7 @@ struct Domain::Impl {
         fail(std::string(what) + ": " + N.error_string(st));
       if (std::chrono::steady_clock::now() > deadline)
         fail(std::string(what) + ": timed out after " + std::to_string(timeout_seconds()) + " s");
-      std::this_thread::sleep_for(std::chrono::microseconds(200));
+      pause(spins++);
     }
   }
   // Waits for the work enqueued so far on `s` (the exchanges included) with the domain
@@ -290,6 +309,7 @@ struct Domain::Impl {
     const auto &N = nccl();
     check(cudaEventRecord(done, s));
     auto deadline = std::chrono::steady_clock::now() + std::chrono::duration<double>(timeout_seconds());
+    long long spins = 0;
     for (;;) {
       cudaError_t q = cudaEventQuery(done);
       if (q == cudaSuccess)
@@ -302,7 +322,7 @@ struct Domain::Impl {
       if (std::chrono::steady_clock::now() > deadline)
         fail(std::string(what) + ": a peer did not take part within " + std::to_string(timeout_seconds()) +
              " s (MACE_DOMAIN_TIMEOUT_S)");
-      std::this_thread::sleep_for(std::chrono::microseconds(100));
+      pause(spins++);
     }
   }
 };
@@ -314,6 +334,9 @@ Domain::Domain(int rank, int world, const void *unique_id) : impl_(std::make_uni
   d.rank = rank;
   d.world = world;
   check(cudaEventCreateWithFlags(&d.done, cudaEventDisableTiming));
+  check(cudaEventCreateWithFlags(&d.ready, cudaEventDisableTiming));
+  check(cudaEventCreateWithFlags(&d.finished, cudaEventDisableTiming));
+  check(cudaStreamCreateWithFlags(&d.exchange, cudaStreamNonBlocking));
   ncclUniqueId id;
   std::copy(static_cast<const char *>(unique_id), static_cast<const char *>(unique_id) + sizeof(id.internal),
             id.internal);
@@ -335,6 +358,12 @@ Domain::~Domain() {
   }
   if (impl_->done)
     cudaEventDestroy(impl_->done);
+  if (impl_->ready)
+    cudaEventDestroy(impl_->ready);
+  if (impl_->finished)
+    cudaEventDestroy(impl_->finished);
+  if (impl_->exchange)
+    cudaStreamDestroy(impl_->exchange);
 }
 int Domain::rank() const { return impl_->rank; }
 int Domain::world() const { return impl_->world; }
@@ -445,8 +474,9 @@ void Domain::localize(Context &ctx) {
   int *dmine = ctx.array<int>("domain.check", size_t(fields) * (W + 1));
   check(cudaMemcpyAsync(dmine, mine.data(), size_t(fields) * sizeof(int), cudaMemcpyHostToDevice, s));
   if (W > 1) {
-    d.step(nccl().all_gather(dmine, dmine + fields, size_t(fields), ncclInt32, d.comm, s), "ncclAllGather");
-    d.wait(s, "domain plan check");
+    d.hand_over(s);
+    d.step(nccl().all_gather(dmine, dmine + fields, size_t(fields), ncclInt32, d.comm, d.exchange), "ncclAllGather");
+    d.wait(d.exchange, "domain plan check");
     check(cudaMemcpy(all.data(), dmine + fields, all.size() * sizeof(int), cudaMemcpyDeviceToHost));
   } else {
     all = mine;
@@ -492,7 +522,8 @@ void Domain::fetch_ghost_rows(Context &ctx, float *x, int comps, int stride, int
   auto &d = *impl_;
   d.check_usable();
   const auto &N = nccl();
-  cudaStream_t s = ctx.stream;
+  cudaStream_t s = d.exchange;
+  d.hand_over(ctx.stream);
   std::vector<float *> sbuf(d.world, nullptr), rbuf(d.world, nullptr);
   for (int r = 0; r < d.world; ++r) {
     if (r == d.rank)
@@ -518,13 +549,15 @@ void Domain::fetch_ghost_rows(Context &ctx, float *x, int comps, int stride, int
     if (r != d.rank && d.ghost_count[r])
       lapis::launch(unpack_rows, blocks((long long)d.ghost_count[r] * comps * width), 256, 0, s, d.ghost_count[r], comps,
                     stride, width, static_cast<const int *>(nullptr), d.n_own + d.ghost_off[r], rbuf[r], x, 0);
+  d.mark_finished();
 }
 
 void Domain::return_ghost_rows(Context &ctx, float *x, int comps, int stride, int width) {
   auto &d = *impl_;
   d.check_usable();
   const auto &N = nccl();
-  cudaStream_t s = ctx.stream;
+  cudaStream_t s = d.exchange;
+  d.hand_over(ctx.stream);
   std::vector<float *> sbuf(d.world, nullptr), rbuf(d.world, nullptr);
   for (int r = 0; r < d.world; ++r) {
     if (r == d.rank)
@@ -551,6 +584,12 @@ void Domain::return_ghost_rows(Context &ctx, float *x, int comps, int stride, in
     if (r != d.rank && d.send_count[r])
       lapis::launch(unpack_rows, blocks((long long)d.send_count[r] * comps * width), 256, 0, s, d.send_count[r], comps,
                     stride, width, static_cast<const int *>(d.send_list[r]), 0, rbuf[r], x, 1);
+  d.mark_finished();
+}
+
+void Domain::join(Context &ctx) {
+  auto &d = *impl_;
+  check(cudaStreamWaitEvent(ctx.stream, d.finished, 0));
 }
 
 void Domain::gather_outputs(Context &ctx, const float *e, const float *f, const float *v, float *ef, float *ff,
@@ -564,7 +603,10 @@ void Domain::gather_outputs(Context &ctx, const float *e, const float *f, const 
   if (d.n_own)
     lapis::launch(place_owned, blocks(d.n_own), 256, 0, s, d.n_own, d.o0, e, f, v, ef, ff, vf);
   if (d.world > 1) {
-    d.step(nccl().all_reduce(ef, ef, size_t(n) * 13, ncclFloat32, ncclSum, d.comm, s), "ncclAllReduce");
+    d.hand_over(s);
+    d.step(nccl().all_reduce(ef, ef, size_t(n) * 13, ncclFloat32, ncclSum, d.comm, d.exchange), "ncclAllReduce");
+    d.mark_finished();
+    check(cudaStreamWaitEvent(s, d.finished, 0));
     d.wait(s, "domain output all-reduce");
   }
 }

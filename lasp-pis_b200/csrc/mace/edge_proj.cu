@@ -178,6 +178,15 @@ __global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBl
   }
   __syncthreads();
 
+  // Bulk store of tile t's up-gradient rows (layer-1 backward): rows e0 - e_base .. of the
+  // chunk buffer are contiguous (consecutive edges).  Producer lane 0 only.
+  auto store_ug_rows = [&](int t, unsigned char *st) {
+    int e0 = begin + t * T, cnt = min(T, end - e0);
+    tc::bulk_store(a.ug_edge + size_t(e0 - a.e_base) * IN * 128, smem_u32(st + S::UG), unsigned(cnt) * IN * 512);
+    tc::bulk_commit();
+  };
+  (void)store_ug_rows;
+
   if (warp == kCW) {
     // ---------------- producer ----------------
     // The forward reads edge metadata 32 edges (32 / T tiles) at a time, one edge per lane, so
@@ -205,6 +214,14 @@ __global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBl
         }
         unsigned char *st = smem + s * S::BYTES;
         unsigned sb = smem_u32(st), full = full0 + 8 * s;
+        if constexpr (Bwd && L > 0) {
+          // Tile t - NS, consumed (its up-gradient rows written and fenced): store its rows,
+          // and let the store finish reading the stage before the stage is refilled.
+          if (t >= kStages && lane == 0) {
+            store_ug_rows(t - kStages, st);
+            tc::bulk_wait_read();
+          }
+        }
         int e0 = begin + t * T, cnt = min(T, end - e0), k = lane - (t - c0) * T;
         bool mine = k >= 0 && k < cnt; // this lane holds the tile's edge k
         if (mine)
@@ -232,6 +249,19 @@ __global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBl
         if (lane != 0)
           mbar_arrive(full);
       }
+    }
+    if constexpr (Bwd && L > 0) {
+      // The last NS tiles' rows, once the channel warps are done with them.
+      for (int t = max(0, ntiles - kStages); t < ntiles && run; ++t) {
+        int s = t % kStages;
+        bool ok = mbar_wait(empty0 + 8 * s, (t / kStages) & 1, &abort_flag);
+        if (!__all_sync(0xffffffffu, ok))
+          break;
+        if (lane == 0)
+          store_ug_rows(t, smem + s * S::BYTES);
+      }
+      if (lane == 0)
+        tc::bulk_wait(); // complete before the CTA's shared memory is released
     }
     return;
   }
@@ -374,18 +404,8 @@ __global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBl
     }
     if constexpr (Bwd) {
       if constexpr (L > 0)
-        tc::fence_proxy_async_smem();
+        tc::fence_proxy_async_smem(); // the up-gradient rows, for the producer's bulk store
       asm volatile("bar.sync 1, %0;" ::"r"(kCT) : "memory");
-      if constexpr (L > 0) {
-        // One bulk store of the tile's rows (contiguous: consecutive edges); before the next
-        // tile starts, the store issued NS - 1 = 1 tiles ago has finished reading its stage.
-        static_assert(kStages == 2, "the up-gradient staging assumes a 2-stage ring");
-        if (c == 0) {
-          tc::bulk_store(a.ug_edge + size_t(meta[0].row) * IN * 128, smem_u32(st + S::UG), unsigned(cnt) * IN * 512);
-          tc::bulk_commit();
-          tc::bulk_wait_read1();
-        }
-      }
       if (c < cnt) {
         int e = begin + t * T + c;
         float sum[4];
@@ -408,10 +428,6 @@ __global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBl
       }
     }
     mbar_arrive(empty0 + 8 * s);
-  }
-  if constexpr (Bwd && L > 0) {
-    if (c == 0)
-      tc::bulk_wait(); // the last tiles' up-gradient stores are complete
   }
   if constexpr (!Bwd) {
     if (ok) {

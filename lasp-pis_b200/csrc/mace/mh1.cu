@@ -209,7 +209,7 @@ std::vector<Result> MH1::compute(bool batch) {
       linear(s, ns, l.up, input, up[k], false, false, status);
     else
       linear(s, n, l.up, input, up[k], false, false, status, n, ns);
-    if (dom && k == 1)
+    if (dom && k == 1) // overlaps the res / skip linears, the radial MLP and the projection
       dom->fetch_ghost_rows(c, up[k], l.in_comp, ns, 128);
     linear(s, n, l.res, up[k], res[k], false, false, status, ns);
     // The skip connection goes straight into the layer output; the product linear adds onto it.
@@ -222,6 +222,8 @@ std::vector<Result> MH1::compute(bool batch) {
         tc_gemm(s, int(q.e1 - q.e0), width, 64, 1, ro[k].h + q.e0 * 64, 0, l.radial.out_hi, l.radial.out_lo,
                 proj[k], width, 0, false, status);
         timer.mark("forward" + std::to_string(k) + ".projection");
+        if (dom && k == 1 && &q == &chunks.front())
+          dom->join(c); // the ghosts' up-projected features have arrived
         launch_message_forward_proj(s, k, c.geometry, l, ea, ro[k], q, proj[k], up[k], msg, rho[k], ns);
         timer.mark("forward" + std::to_string(k) + ".messages");
       }
@@ -269,6 +271,7 @@ std::vector<Result> MH1::compute(bool batch) {
   linear(s, n, m.read1up, rdpre, hgrad1, true, false, status);
   timer.mark("readouts");
   float *hgrad = hgrad1;
+  bool dR0_ready = false; // layer 0's dR' computed early (domain runs overlap it with an exchange)
   for (int k = 1; k >= 0; --k) {
     const Layer &l = m.layers[k];
     if (k == 0)
@@ -295,9 +298,11 @@ std::vector<Result> MH1::compute(bool batch) {
       for (auto &q : chunks) {
         int rows = int(q.e1 - q.e0);
         // (cut dh + dcut h) W; with several chunks, (cut h) W is recomputed beside it.
-        if (chunks.size() == 1) // (cut h) W is still in place from the forward pass
-          tc_gemm(s, rows, width, 64, 1, ro[k].dh + q.e0 * 64, 0, l.radial.out_hi, l.radial.out_lo, dR, width, 0,
-                  false, status);
+        if (chunks.size() == 1) { // (cut h) W is still in place from the forward pass
+          if (!(k == 0 && dR0_ready))
+            tc_gemm(s, rows, width, 64, 1, ro[k].dh + q.e0 * 64, 0, l.radial.out_hi, l.radial.out_lo, dR, width, 0,
+                    false, status);
+        }
         else
           tc_gemm(s, rows, width, 64, 2, ro[k].h + q.e0 * 64, (long long)E * 64, l.radial.out_hi,
                   l.radial.out_lo, R, width, (long long)chunk_cap * width, false, status);
@@ -319,7 +324,18 @@ std::vector<Result> MH1::compute(bool batch) {
     if (k == 1) {
       if (dom)
         dom->return_ghost_rows(c, upgrad, l.in_comp, ns, 128);
+      // Independent of the returned gradients: overlaps their exchange.
       linear(s, n, l.skip, hgrad, hgrad0, true, false, status);
+      if (dom && projection && chunks.size() == 1) {
+        // Layer 0's (cut dh + dcut h) W now: the up-gradient rows it overwrites are consumed.
+        const Layer &l0 = m.layers[0];
+        int width0 = l0.paths * 128;
+        tc_gemm(s, int(chunks[0].e1 - chunks[0].e0), width0, 64, 1, ro[0].dh, 0, l0.radial.out_hi, l0.radial.out_lo,
+                proj[0] + size_t(chunk_cap) * width0, width0, 0, false, status);
+        dR0_ready = true;
+      }
+      if (dom)
+        dom->join(c);
       linear(s, n, l.up, upgrad, hgrad0, true, true, status, ns, n);
       hgrad = hgrad0;
     }
@@ -328,6 +344,7 @@ std::vector<Result> MH1::compute(bool batch) {
     launch_force_gather_domain(s, c.geometry, edge_force, force, virial);
     launch_ghost_reactions(s, senders_of, n, edge_force, force);
     dom->return_ghost_rows(c, force, 1, ns, 3);
+    dom->join(c);
   } else {
     launch_force_gather(s, c.geometry, edge_force, force, virial);
   }

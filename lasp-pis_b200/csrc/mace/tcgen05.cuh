@@ -172,8 +172,6 @@ __device__ __forceinline__ void bulk_store(void *dst, unsigned src, unsigned byt
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
                : "memory");
 }
-// At most one of the calling thread's bulk groups still reading shared memory.
-__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 // Generic-proxy shared-memory writes before this fence are visible to later bulk copies.
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 // Wait until the issued bulk copies have read their shared-memory source / fully completed.
