@@ -51,6 +51,9 @@ struct Diagnostics {
   std::string reason;
   long long edges = 0; // directed edges of the last call (B200 build addition)
   int launches = 0;     // kernels launched by the last call (B200 build addition)
+  // How the last MH1 call ran its kernels (B200 build addition): "direct", "recorded" (captured
+  // into a CUDA graph and launched) or "replayed" (the recorded graph launched again).
+  std::string graph = "direct";
   std::vector<std::pair<std::string, float>> stages; // per-stage device ms when profiling
 };
 // Kernel launch counter of the calling thread (reset by Context::prepare).

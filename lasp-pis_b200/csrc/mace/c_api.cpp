@@ -343,7 +343,7 @@ int mace_diagnostics(void *handle, char *buffer, size_t capacity) {
       << ",\"brute_candidates\":" << d.brute_candidates << ",\"context_bytes\":" << d.allocated_bytes
       << ",\"context_peak_bytes\":" << d.peak_bytes << ",\"parameter_bytes\":" << h->model->parameter_bytes()
       << ",\"device_ms\":" << d.device_ms << ",\"edges\":" << d.edges << ",\"device\":" << h->device
-      << ",\"launches\":" << d.launches << ",\"stages\":[";
+      << ",\"launches\":" << d.launches << ",\"graph\":\"" << d.graph << "\",\"stages\":[";
     for (size_t k = 0; k < d.stages.size(); ++k)
       s << (k ? "," : "") << "[\"" << d.stages[k].first << "\"," << d.stages[k].second << "]";
     s << "],\"kernels\":[";
