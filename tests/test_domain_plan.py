@@ -103,7 +103,9 @@ def _gloo_rank(rank, world, port, n, edges, library, skip_send, out):
     import torch
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    # A generous timeout while the ranks start; the exchange runs in a group with a 3 s one.
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=3))
     lib = _lib(library)
     sends, ghosts = host_plan(lib, n, rank, world, *local_rows(edges, n, rank, world))
     try:
@@ -111,14 +113,14 @@ def _gloo_rank(rank, world, port, n, edges, library, skip_send, out):
         for q in range(world):
             if q == rank or (skip_send and rank == 1):
                 continue
-            reqs.append(dist.isend(torch.from_numpy(sends[q].astype(np.int64)), q))
+            reqs.append(dist.isend(torch.from_numpy(sends[q].astype(np.int64)), q, group=group))
         got = {}
         t0 = time.monotonic()
         for q in range(world):
             if q == rank:
                 continue
             buf = torch.zeros(len(ghosts[q]), dtype=torch.int64)
-            dist.recv(buf, q)
+            dist.recv(buf, q, group=group)
             got[q] = buf.numpy()
         for r in reqs:
             r.wait()
