@@ -146,6 +146,13 @@ __global__ void scan_flags(const int *in, int *out, int n) {
   if (t == 1023)
     out[n] = partial[1023];
 }
+// out[r] = ghost_pos[starts[r]] (r <= W), out[W + 1 + r] = peer r's send total.
+__global__ void plan_sizes(int world, int n_own, const int *ghost_pos, const int *starts, const int *ppos, int *out) {
+  for (int r = threadIdx.x; r <= world; r += blockDim.x)
+    out[r] = ghost_pos[starts[r]];
+  for (int r = threadIdx.x; r < world; r += blockDim.x)
+    out[world + 1 + r] = ppos[size_t(r) * (n_own + 1) + n_own];
+}
 __global__ void compact(int n, const int *flag, const int *pos, int base, int *list) {
   int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j < n && flag[j])
@@ -410,14 +417,14 @@ ExchangePlan build_plan(Context &ctx, int rank, int world) {
                   starts, peer);
   for (int r = 0; r < W; ++r)
     lapis::launch(scan_flags, 1, 1024, 0, s, peer + size_t(r) * p.n_own, ppos + size_t(r) * (p.n_own + 1), p.n_own);
-  // Plan sizes (host): ghost block offsets at the ownership bounds, send totals per peer.
-  std::vector<int> pos_at(W + 1), sends(W);
-  for (int r = 0; r <= W; ++r)
-    check(cudaMemcpyAsync(&pos_at[r], p.ghost_pos + p.starts[r], sizeof(int), cudaMemcpyDeviceToHost, s));
-  for (int r = 0; r < W; ++r)
-    check(cudaMemcpyAsync(&sends[r], ppos + size_t(r) * (p.n_own + 1) + p.n_own, sizeof(int),
-                          cudaMemcpyDeviceToHost, s));
+  // Plan sizes (host, one copy): ghost block offsets at the ownership bounds, send totals per
+  // peer.
+  int *sizes = ctx.array<int>("domain.sizes", 2 * size_t(W) + 1);
+  lapis::launch(plan_sizes, 1, 64, 0, s, W, p.n_own, p.ghost_pos, starts, ppos, sizes);
+  std::vector<int> host_sizes(2 * W + 1);
+  check(cudaMemcpyAsync(host_sizes.data(), sizes, host_sizes.size() * sizeof(int), cudaMemcpyDeviceToHost, s));
   check(cudaStreamSynchronize(s)); // local work only: no peer is involved
+  const int *pos_at = host_sizes.data(), *sends = host_sizes.data() + W + 1;
   int n_ghost = pos_at[W];
   p.n_local = p.n_own + n_ghost;
   p.ghost_off.assign(W, 0);
