@@ -142,8 +142,10 @@ __global__ void __launch_bounds__(kOrderThreads) order_bins(int nb, const int *o
   }
 }
 
+// Sorted copies in the internal order; positions both as float[3n] (the public geometry)
+// and as float4 [n] (x, y, z, 0) for the traversal's one 16-byte load per candidate.
 __global__ void gather_atoms(int n, const int *i2o, const float *wxyz, const int *z, const int *bin,
-                             const int *wind, float *sx, int *sz, int *sb, int *sw, int *o2i) {
+                             const int *wind, float *sx, float4 *sx4, int *sz, int *sb, int *sw, int *o2i) {
   int k = blockIdx.x * blockDim.x + threadIdx.x;
   if (k >= n)
     return;
@@ -155,6 +157,7 @@ __global__ void gather_atoms(int n, const int *i2o, const float *wxyz, const int
     sx[3 * k + q] = wxyz[3 * i + q];
     sw[3 * k + q] = wind[3 * i + q];
   }
+  sx4[k] = make_float4(wxyz[3 * i], wxyz[3 * i + 1], wxyz[3 * i + 2], 0.f);
 }
 
 struct ConnStats {
@@ -206,6 +209,7 @@ struct Traverse {
   int r0, nr; // receivers [r0, r0 + nr) (internal ids); senders are all n atoms
   float h[9], cutoff2;
   const float *xyz;
+  const float4 *xyz4; // the same positions as (x, y, z, 0) when set: one 16-byte load each
   const int *bins, *offsets, *winding;
   const ConnStats *stats; // stats->cell selects the 27-bin stencil or all atoms x images
 };
@@ -220,7 +224,13 @@ __global__ void neighbour_pass(Traverse g, int *counts, const int *row, int *out
     return;
   int i = g.r0 + warp;
   bool cell = g.stats->cell;
-  float xi = g.xyz[3 * i], yi = g.xyz[3 * i + 1], zi = g.xyz[3 * i + 2];
+  float xi, yi, zi;
+  if (g.xyz4) {
+    float4 p = g.xyz4[i];
+    xi = p.x, yi = p.y, zi = p.z;
+  } else {
+    xi = g.xyz[3 * i], yi = g.xyz[3 * i + 1], zi = g.xyz[3 * i + 2];
+  }
   int wi0 = g.winding[3 * i], wi1 = g.winding[3 * i + 1], wi2 = g.winding[3 * i + 2];
   int bx = 0, by = 0, bz = 0;
   if (cell) {
@@ -251,9 +261,16 @@ __global__ void neighbour_pass(Traverse g, int *counts, const int *row, int *out
           float dx = 0, dy = 0, dz = 0, r2 = 0;
           if (valid) {
             // Same expression and evaluation order as the reference displacement().
-            dx = g.xyz[3 * j] + sx * g.h[0] + sy * g.h[3] + sz * g.h[6] - xi;
-            dy = g.xyz[3 * j + 1] + sx * g.h[1] + sy * g.h[4] + sz * g.h[7] - yi;
-            dz = g.xyz[3 * j + 2] + sx * g.h[2] + sy * g.h[5] + sz * g.h[8] - zi;
+            float xj, yj, zj;
+            if (g.xyz4) {
+              float4 p = g.xyz4[j];
+              xj = p.x, yj = p.y, zj = p.z;
+            } else {
+              xj = g.xyz[3 * j], yj = g.xyz[3 * j + 1], zj = g.xyz[3 * j + 2];
+            }
+            dx = xj + sx * g.h[0] + sy * g.h[3] + sz * g.h[6] - xi;
+            dy = yj + sx * g.h[1] + sy * g.h[4] + sz * g.h[7] - yi;
+            dz = zj + sx * g.h[2] + sy * g.h[5] + sz * g.h[8] - zi;
             r2 = dx * dx + dy * dy + dz * dz;
             valid = r2 <= g.cutoff2 && !(i == j && sx == 0 && sy == 0 && sz == 0);
           }
@@ -621,6 +638,7 @@ void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
   int *wind = array<int>("prep.winding", size_t(n) * 3);
   int *bin = array<int>("prep.bin", n);
   float *sorted = array<float>("geometry.xyz", size_t(n) * 3);
+  float4 *sorted4 = array<float4>("geometry.xyz4", n);
   int *sz = array<int>("geometry.z", n);
   int *sb = array<int>("geometry.bin", n);
   int *sw = array<int>("geometry.winding", size_t(n) * 3);
@@ -653,8 +671,8 @@ void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
     lapis::launch(place_atoms, blocks, 256, 0, stream, n, bin, offsets, cursor, internal_to_original);
     lapis::launch(order_bins, (nb * 32 + kOrderThreads - 1) / kOrderThreads, kOrderThreads, 0, stream, nb, offsets,
                   internal_to_original);
-    lapis::launch(gather_atoms, blocks, 256, 0, stream, n, internal_to_original, wxyz, in_z, bin, wind, sorted, sz, sb, sw,
-                                             original_to_internal);
+    lapis::launch(gather_atoms, blocks, 256, 0, stream, n, internal_to_original, wxyz, in_z, bin, wind, sorted,
+                  sorted4, sz, sb, sw, original_to_internal);
     lapis::launch(bin_stats, (nb + 255) / 256, 256, 0, stream, nb, dims[0], dims[1], dims[2], offsets, stats);
   }
   lapis::launch(decide_backend, 1, 1, 0, stream, stats, int(opts.backend), grid_ok, brute);
@@ -667,6 +685,7 @@ void Context::prepare(const Structure &s, float cutoff, const Options &opts) {
   std::copy(s.cell.begin(), s.cell.end(), tv.h);
   tv.cutoff2 = cutoff * cutoff;
   tv.xyz = sorted;
+  tv.xyz4 = sorted4;
   tv.bins = sb;
   tv.offsets = offsets;
   tv.winding = sw;
@@ -1241,6 +1260,7 @@ long long lapis_neighbor_list_static(int n, const float *xyz, const int *element
     std::copy(cell, cell + 9, tv.h);
     tv.cutoff2 = cutoff * cutoff;
     tv.xyz = wxyz;
+    tv.xyz4 = nullptr;
     tv.bins = bin;
     tv.offsets = nullptr;
     tv.winding = wind;
