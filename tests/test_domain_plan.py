@@ -174,7 +174,7 @@ def test_rank_that_never_sends_times_out(library, c2_edges):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", ["C2", "C3"])
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_device_plan_matches_host_rules(library, name, world):
     """The device plan of every rank equals the host rules applied to that rank's device rows;
     the ranks' plans agree pairwise; together the ranks' rows hold every edge once."""
