@@ -246,7 +246,7 @@ std::vector<Result> MH1::compute(bool batch) {
   launch_zbl(s, c.geometry, m.constants_dev, m.zbl_radii, m.zbl_c, cst[7], energy, force, virial);
   // Projection path: radial projections on the tensor cores into chunk buffers, tensor
   // products from those (default); otherwise the fused SIMT edge kernels.
-  bool projection = projection_edges() && m.layers[0].radial.out_hi && m.layers[1].radial.out_hi;
+  bool projection = projection_edges() && m.layers[0].radial.out && m.layers[1].radial.out;
   if (dom && !projection)
     throw Error("Domain decomposition requires the tensor-core projection path");
   std::vector<ProjectionChunk> chunks;
@@ -298,8 +298,8 @@ std::vector<Result> MH1::compute(bool batch) {
     if (projection) {
       for (auto &q : chunks) {
         // (cut h) W per edge row and path channel; the edge kernel adds cut b.
-        tc_gemm(s, int(q.e1 - q.e0), width, 64, 1, ro[k].h + q.e0 * 64, 0, l.radial.out_hi, l.radial.out_lo,
-                proj[k], width, 0, false, status);
+        tc_gemm(s, int(q.e1 - q.e0), width, 64, 1, ro[k].h + q.e0 * 64, 0, l.radial.out, proj[k], width, 0, false,
+                status);
         timer.mark("forward" + std::to_string(k) + ".projection");
         if (dom && k == 1 && &q == &chunks.front())
           dom->join(c); // the ghosts' up-projected features have arrived
@@ -379,12 +379,11 @@ std::vector<Result> MH1::compute(bool batch) {
         // (cut dh + dcut h) W; with several chunks, (cut h) W is recomputed beside it.
         if (chunks.size() == 1) { // (cut h) W is still in place from the forward pass
           if (!(k == 0 && dR0_ready))
-            tc_gemm(s, rows, width, 64, 1, ro[k].dh + q.e0 * 64, 0, l.radial.out_hi, l.radial.out_lo, dR, width, 0,
-                    false, status);
+            tc_gemm(s, rows, width, 64, 1, ro[k].dh + q.e0 * 64, 0, l.radial.out, dR, width, 0, false, status);
         }
         else
-          tc_gemm(s, rows, width, 64, 2, ro[k].h + q.e0 * 64, (long long)E * 64, l.radial.out_hi,
-                  l.radial.out_lo, R, width, (long long)chunk_cap * width, false, status);
+          tc_gemm(s, rows, width, 64, 2, ro[k].h + q.e0 * 64, (long long)E * 64, l.radial.out, R, width,
+                  (long long)chunk_cap * width, false, status);
         timer.mark("backward" + std::to_string(k) + ".projection");
         launch_message_backward_proj(s, k, c.geometry, l, ea, ro[k], q, R, dR, up[k], msggrad, rhograd, ug_edge,
                                      edge_force, k == 0, ns);
@@ -409,7 +408,7 @@ std::vector<Result> MH1::compute(bool batch) {
         // Layer 0's (cut dh + dcut h) W now: the up-gradient rows it overwrites are consumed.
         const Layer &l0 = m.layers[0];
         int width0 = l0.paths * 128;
-        tc_gemm(s, int(chunks[0].e1 - chunks[0].e0), width0, 64, 1, ro[0].dh, 0, l0.radial.out_hi, l0.radial.out_lo,
+        tc_gemm(s, int(chunks[0].e1 - chunks[0].e0), width0, 64, 1, ro[0].dh, 0, l0.radial.out,
                 proj[0] + size_t(chunk_cap) * width0, width0, 0, false, status);
         dR0_ready = true;
       }

@@ -11,6 +11,7 @@
 #include "model.hpp"
 #include "checkpoint.hpp"
 #include "product_table.h"
+#include <cuda_fp16.h>
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
@@ -56,17 +57,28 @@ void ModelData::validate(const std::string &path, const std::string &head) {
   load(path, head);
 }
 
-// w = hi + lo with hi = w rounded to tf32 and lo the exact fp32 remainder (an MMA of
-// kind::tf32 reads its top 19 bits).  Measured on B200 against the float64 oracle, this gives
-// smaller energy and virial errors than rounding lo to tf32 as well.
-void split_tf32(const float *w, size_t count, float *hi, float *lo) {
-  for (size_t k = 0; k < count; ++k) {
-    uint32_t bits;
-    std::memcpy(&bits, w + k, 4);
-    bits = (bits + 0x1000u) & 0xffffe000u;
-    std::memcpy(hi + k, &bits, 4);
-    lo[k] = w[k] - hi[k];
+// w 2^exp = hi + lo: hi = round_fp16(w 2^exp), lo = round_fp16(w 2^exp - hi) (the remainder
+// is exact in fp32); exp brings the largest |w| into [2^14, 2^15), so every weight down to
+// 2^-17 of the largest keeps 22 significant bits in normal fp16 numbers.
+int split_f16(const float *w, size_t count, uint16_t *hi, uint16_t *lo) {
+  float m = 0.f;
+  for (size_t k = 0; k < count; ++k)
+    m = std::max(m, std::fabs(w[k]));
+  int exp = 0;
+  if (m > 0.f) {
+    int ex = 0;
+    std::frexp(m, &ex); // m = f 2^ex, f in [0.5, 1)
+    exp = std::min(126, std::max(-126, 15 - ex));
   }
+  float scale = std::ldexp(1.f, exp);
+  for (size_t k = 0; k < count; ++k) {
+    float x = w[k] * scale;
+    __half h = __float2half_rn(x);
+    __half l = __float2half_rn(x - __half2float(h));
+    std::memcpy(hi + k, &h, 2);
+    std::memcpy(lo + k, &l, 2);
+  }
+  return exp;
 }
 
 namespace {
@@ -190,6 +202,16 @@ void ModelData::load(const std::string &path, const std::string &head) {
     bytes += v.size() * 4;
     return device.upload(v.data(), v.size() * 4);
   };
+  // fp16 split planes of a K-major matrix for the tensor-core GEMM.
+  auto up_split = [&](const float *w, size_t count) {
+    std::vector<uint16_t> hi(count), lo(count);
+    TCMatrix m;
+    m.exp = split_f16(w, count, hi.data(), lo.data());
+    bytes += count * 4;
+    m.hi = reinterpret_cast<const uint16_t *>(device.upload(hi.data(), count * 2));
+    m.lo = reinterpret_cast<const uint16_t *>(device.upload(lo.data(), count * 2));
+    return m;
+  };
   auto c = a.get<float>("constants");
   if (c.size() != 14 || c[0] != 6)
     throw Error("Unsupported MH1 constants");
@@ -249,16 +271,12 @@ void ModelData::load(const std::string &path, const std::string &head) {
       if (tc_gemm_supported(p.out_mul, p.in_mul) && tc_gemm_supported(p.in_mul, p.out_mul)) {
         size_t cnt = size_t(p.in_mul) * p.out_mul;
         const float *src = w.data() + p.weight_offset;
-        std::vector<float> wt(cnt), hi(cnt), lo(cnt);
+        std::vector<float> wt(cnt);
         for (int i = 0; i < p.in_mul; ++i)
           for (int o = 0; o < p.out_mul; ++o)
             wt[size_t(o) * p.in_mul + i] = src[size_t(i) * p.out_mul + o];
-        split_tf32(wt.data(), cnt, hi.data(), lo.data());
-        t.fwd_hi = up(hi);
-        t.fwd_lo = up(lo);
-        split_tf32(src, cnt, hi.data(), lo.data());
-        t.bwd_hi = up(hi);
-        t.bwd_lo = up(lo);
+        t.fwd = up_split(wt.data(), cnt);
+        t.bwd = up_split(src, cnt);
       }
       l.tc.push_back(t);
     }
@@ -289,12 +307,8 @@ void ModelData::load(const std::string &path, const std::string &head) {
     std::string out = key + "." + std::to_string(depth * 3);
     auto ow = a.get<float>(out + ".weight");
     r.out_t = up(transposed(ow, outputs, 64, out + ".weight"));
-    if (outputs % 128 == 0) {
-      std::vector<float> hi(ow.size()), lo(ow.size());
-      split_tf32(ow.data(), ow.size(), hi.data(), lo.data());
-      r.out_hi = up(hi);
-      r.out_lo = up(lo);
-    }
+    if (outputs % 128 == 0)
+      r.out = up_split(ow.data(), ow.size());
     r.out_b = up(a.get<float>(out + ".bias"));
     r.depth = depth;
     r.outputs = outputs;

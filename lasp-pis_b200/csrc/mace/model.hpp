@@ -16,11 +16,18 @@ namespace mace {
 struct LinearPath {
   int in_offset, out_offset, in_mul, out_mul, dim, weight_offset;
 };
-// Tensor-core copies of one path's weight W [in_mul][out_mul], split as W = hi + lo with hi
-// rounded to tf32: forward planes are K-major for Y = X W ([out_mul][in_mul]), backward
-// planes for X_grad = Y_grad W^T ([in_mul][out_mul]).  Null when the shape is not eligible.
+// Operand B of the tensor-core GEMM: a K-major matrix [N][K] split as B 2^exp = hi + lo,
+// two fp16 planes (split_f16).
+struct TCMatrix {
+  const uint16_t *hi = nullptr, *lo = nullptr;
+  int exp = 0;
+  explicit operator bool() const { return hi != nullptr; }
+};
+// Tensor-core copies of one path's weight W [in_mul][out_mul]: forward planes are K-major for
+// Y = X W ([out_mul][in_mul]), backward planes for X_grad = Y_grad W^T ([in_mul][out_mul]).
+// Empty when the shape is not eligible.
 struct TCWeights {
-  const float *fwd_hi = nullptr, *fwd_lo = nullptr, *bwd_hi = nullptr, *bwd_lo = nullptr;
+  TCMatrix fwd, bwd;
 };
 struct Linear {
   int input = 0, output = 0;
@@ -37,7 +44,7 @@ struct Radial {
   const float *bias[3], *gamma[3], *beta[3];
   const float *out_t;           // [64][outputs]
   const float *out_b;           // [outputs]
-  const float *out_hi, *out_lo; // [outputs][64] tf32 split of the projection (tensor cores)
+  TCMatrix out;                 // [outputs][64] fp16 split of the projection (tensor cores)
   int depth, outputs;
 };
 struct PolyTerm {
@@ -119,7 +126,6 @@ void launch_message_forward(cudaStream_t, int layer, const lapis::DeviceGeometry
 void launch_message_backward(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &,
                              EdgeArrays, RadialOut, const float *up, const float *message_grad,
                              const float *density_grad, float *ug_edge, float4 *edge_force, bool accumulate);
-CUtensorMap tc_map_2d(const float *base, int cols, long long rows, int box_cols, int box_rows);
 // Projection path (edge_proj.cu): the radial projection R = h W (and dR = dh W) runs as a
 // tensor-core GEMM into a buffer covering the edges of receivers [r0, r1) = [e0, e1); the
 // tensor-product kernels read rows e - e0.
@@ -167,10 +173,10 @@ void launch_ghost_reactions(cudaStream_t, const SenderIndex &, int n_own, const 
 // computed ones (the ghost rows of a domain-decomposed evaluation).
 void linear(cudaStream_t, int n, const Linear &, const float *x, float *y, bool backward = false,
             bool add = false, int *status = nullptr, int nx = 0, int ny = 0);
-// Tensor-core GEMM (tc_gemm.cu): C[z] (+)= A[z] B, B = Bhi + Blo given K-major [N][K].
+// Tensor-core GEMM (tc_gemm.cu): C[z] (+)= A[z] B, B given as its fp16 split, K-major [N][K].
 bool tc_gemm_supported(int N, int K);
-void tc_gemm(cudaStream_t, int M, int N, int K, int batch, const float *A, long long strideA, const float *Bhi,
-             const float *Blo, float *C, int ldc, long long strideC, bool accumulate, int *status);
+void tc_gemm(cudaStream_t, int M, int N, int K, int batch, const float *A, long long strideA, const TCMatrix &B,
+             float *C, int ldc, long long strideC, bool accumulate, int *status);
 // A group of independent tensor-core GEMMs in one persistent launch (per 16 problems).  A
 // spec with `join` set is a further K segment of the previous spec's problem (same C, M, N,
 // batch and mode; its own A, K and B): C (+)= sum over the segments of A_s B_s.
@@ -178,7 +184,7 @@ struct GemmSpec {
   int M, N, K, batch;
   const float *A;
   long long strideA;
-  const float *Bhi, *Blo;
+  TCMatrix B;
   float *C;
   int ldc;
   long long strideC;
@@ -186,8 +192,9 @@ struct GemmSpec {
   bool join = false;
 };
 void tc_gemm_group(cudaStream_t, const GemmSpec *specs, int count, int *status);
-// Host split of a weight matrix into tf32-rounded hi and the fp32 remainder lo.
-void split_tf32(const float *w, size_t count, float *hi, float *lo);
+// Host split of a weight matrix: w 2^exp = hi + lo, both fp16 (bit patterns) rounded to
+// nearest, with exp such that the largest |w| 2^exp lies in [2^14, 2^15).  Returns exp.
+int split_f16(const float *w, size_t count, uint16_t *hi, uint16_t *lo);
 // Use the tensor-core path in linear() (default true; MACE_SIMT_LINEARS=1 disables).
 bool tensor_core_linears();
 // Edge kernels over tensor-core radial projections (default true; false with SIMT linears or

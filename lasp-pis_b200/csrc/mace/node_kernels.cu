@@ -626,16 +626,16 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
   for (size_t q = 0; q < l.paths.size(); ++q) {
     const auto &p = l.paths[q];
     const TCWeights &t = l.tc[q];
-    if (!tc || !(backward ? t.bwd_hi : t.fwd_hi)) {
+    if (!tc || !(backward ? t.bwd : t.fwd)) {
       all_tc = false;
       continue;
     }
     int o0 = backward ? p.in_offset : p.out_offset, o1 = o0 + (backward ? p.in_mul : p.out_mul) * p.dim;
     GemmSpec g = !backward ? GemmSpec{n, p.out_mul, p.in_mul, p.dim, x + size_t(p.in_offset) * nx,
-                                      (long long)nx * p.in_mul, t.fwd_hi, t.fwd_lo, y + size_t(p.out_offset) * ny,
+                                      (long long)nx * p.in_mul, t.fwd, y + size_t(p.out_offset) * ny,
                                       p.out_mul, (long long)ny * p.out_mul, true}
                            : GemmSpec{n, p.in_mul, p.out_mul, p.dim, x + size_t(p.out_offset) * nx,
-                                      (long long)nx * p.out_mul, t.bwd_hi, t.bwd_lo, y + size_t(p.in_offset) * ny,
+                                      (long long)nx * p.out_mul, t.bwd, y + size_t(p.in_offset) * ny,
                                       p.in_mul, (long long)ny * p.in_mul, true};
     Problem *same = nullptr;
     for (auto &pr : problems) {
@@ -681,7 +681,7 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
     const auto &p = l.paths[q];
     const float *w = l.weight + p.weight_offset;
     const TCWeights &t = l.tc[q];
-    if (tc && (backward ? t.bwd_hi : t.fwd_hi))
+    if (tc && (backward ? t.bwd : t.fwd))
       continue;
     if (!backward) {
       if (launch_skinny<false>(s, n, p.out_mul, p.in_mul, p.dim, x + size_t(p.in_offset) * nx, p.in_mul,
@@ -785,8 +785,31 @@ void set_c_api_error(const std::string &message);
 extern "C" int mace_debug_gemm(int M, int N, int K, int batch, const float *A, const float *B, float *C,
                                int accumulate, int mode) {
   using namespace mace;
-  float *hi = nullptr, *lo = nullptr;
+  std::vector<void *> owned; // device buffers of this call
   int *status = nullptr;
+  auto alloc = [&](size_t bytes) {
+    void *p = nullptr;
+    lapis::check(cudaMalloc(&p, bytes));
+    owned.push_back(p);
+    return p;
+  };
+  auto release = [&] {
+    for (void *p : owned)
+      cudaFree(p);
+    owned.clear();
+  };
+  // The fp16 split of a K-major [n][k] host matrix, on the device.
+  auto split = [&](const float *bt, int n, int k) {
+    std::vector<uint16_t> h(size_t(n) * k), l(h.size());
+    TCMatrix m;
+    m.exp = split_f16(bt, h.size(), h.data(), l.data());
+    auto *hd = static_cast<uint16_t *>(alloc(h.size() * 2)), *ld = static_cast<uint16_t *>(alloc(l.size() * 2));
+    lapis::check(cudaMemcpy(hd, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
+    lapis::check(cudaMemcpy(ld, l.data(), l.size() * 2, cudaMemcpyHostToDevice));
+    m.hi = hd;
+    m.lo = ld;
+    return m;
+  };
   try {
     lapis::set_c_api_error("");
     if (M < 0 || N <= 0 || K <= 0 || batch <= 0 || !A || !B || !C)
@@ -798,73 +821,50 @@ extern "C" int mace_debug_gemm(int M, int N, int K, int batch, const float *A, c
       lapis::launch(gemm_kernel<false>, grid, 256, 0, cudaStream_t(0), M, N, K, A, K, (long long)M * K, B, N, C, N,
                     (long long)M * N);
     } else {
-      std::vector<float> b(size_t(K) * N), bt(b.size()), h(b.size()), l(b.size());
+      std::vector<float> b(size_t(K) * N), bt(b.size());
       lapis::check(cudaMemcpy(b.data(), B, b.size() * 4, cudaMemcpyDeviceToHost));
       for (int k = 0; k < K; ++k)
         for (int n = 0; n < N; ++n)
           bt[size_t(n) * K + k] = b[size_t(k) * N + n];
-      split_tf32(bt.data(), bt.size(), h.data(), l.data());
-      lapis::check(cudaMalloc(&hi, h.size() * 4));
-      lapis::check(cudaMalloc(&lo, l.size() * 4));
-      lapis::check(cudaMalloc(&status, 4));
-      lapis::check(cudaMemcpy(hi, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
-      lapis::check(cudaMemcpy(lo, l.data(), l.size() * 4, cudaMemcpyHostToDevice));
+      status = static_cast<int *>(alloc(4));
       lapis::check(cudaMemset(status, 0, 4));
       if (mode == 1) {
-        tc_gemm(cudaStream_t(0), M, N, K, batch, A, (long long)M * K, hi, lo, C, N, (long long)M * N,
-                accumulate != 0, status);
+        TCMatrix m = split(bt.data(), N, K);
+        tc_gemm(cudaStream_t(0), M, N, K, batch, A, (long long)M * K, m, C, N, (long long)M * N, accumulate != 0,
+                status);
       } else if (mode == 3) { // K split into two segments with their own contiguous A and B
         int k0 = (K / 64) * 32, k1 = K - k0;
         if (!k0)
           throw lapis::Error("mode 3 needs K >= 64");
-        std::vector<float> hs[2], ls[2];
+        std::vector<float> ah(size_t(batch) * M * K);
+        lapis::check(cudaMemcpy(ah.data(), A, ah.size() * 4, cudaMemcpyDeviceToHost));
+        GemmSpec g[2];
         for (int q = 0; q < 2; ++q) {
           int kb = q ? k0 : 0, kc = q ? k1 : k0;
-          hs[q].resize(size_t(N) * kc);
-          ls[q].resize(size_t(N) * kc);
+          // Segment q's B is scaled by 2^(8 q) and its A by 2^-(8 q) (products unchanged), so
+          // that the segments carry different B exponents.
+          std::vector<float> bs(size_t(N) * kc), as(size_t(batch) * M * kc);
           for (int n = 0; n < N; ++n)
-            for (int k = 0; k < kc; ++k) {
-              hs[q][size_t(n) * kc + k] = h[size_t(n) * K + kb + k];
-              ls[q][size_t(n) * kc + k] = l[size_t(n) * K + kb + k];
-            }
+            for (int k = 0; k < kc; ++k)
+              bs[size_t(n) * kc + k] = std::ldexp(bt[size_t(n) * K + kb + k], 8 * q);
+          for (size_t r = 0; r < size_t(batch) * M; ++r)
+            for (int k = 0; k < kc; ++k)
+              as[r * kc + k] = std::ldexp(ah[r * K + kb + k], -8 * q);
+          auto *a = static_cast<float *>(alloc(as.size() * 4 + 16));
+          lapis::check(cudaMemcpy(a, as.data(), as.size() * 4, cudaMemcpyHostToDevice));
+          g[q] = GemmSpec{M, N, kc, batch, a, (long long)M * kc, split(bs.data(), N, kc), C, N, (long long)M * N,
+                          accumulate != 0, q == 1};
         }
-        float *seg[2][3] = {};
-        try {
-          for (int q = 0; q < 2; ++q) {
-            int kb = q ? k0 : 0, kc = q ? k1 : k0;
-            lapis::check(cudaMalloc(&seg[q][0], size_t(batch) * M * kc * 4 + 16));
-            lapis::check(cudaMalloc(&seg[q][1], hs[q].size() * 4));
-            lapis::check(cudaMalloc(&seg[q][2], ls[q].size() * 4));
-            lapis::check(cudaMemcpy2D(seg[q][0], size_t(kc) * 4, A + kb, size_t(K) * 4, size_t(kc) * 4,
-                                      size_t(batch) * M, cudaMemcpyDeviceToDevice));
-            lapis::check(cudaMemcpy(seg[q][1], hs[q].data(), hs[q].size() * 4, cudaMemcpyHostToDevice));
-            lapis::check(cudaMemcpy(seg[q][2], ls[q].data(), ls[q].size() * 4, cudaMemcpyHostToDevice));
-          }
-          GemmSpec g[2];
-          for (int q = 0; q < 2; ++q) {
-            int kc = q ? k1 : k0;
-            g[q] = GemmSpec{M, N, kc, batch, seg[q][0], (long long)M * kc, seg[q][1], seg[q][2], C, N, (long long)M * N,
-                            accumulate != 0, q == 1};
-          }
-          tc_gemm_group(cudaStream_t(0), g, 2, status);
-          lapis::check(cudaDeviceSynchronize());
-        } catch (...) {
-          for (auto &q : seg)
-            for (auto *ptr : q)
-              cudaFree(ptr);
-          throw;
-        }
-        for (auto &q : seg)
-          for (auto *ptr : q)
-            cudaFree(ptr);
+        tc_gemm_group(cudaStream_t(0), g, 2, status);
       } else { // grouped: one problem per batch plane, columns split as [128, N - 128]
+        TCMatrix m = split(bt.data(), N, K);
         std::vector<GemmSpec> group;
         for (int z = 0; z < batch; ++z)
           for (int n0 = 0; n0 < N; n0 += (n0 ? N : 128)) {
             int nc = n0 ? N - n0 : std::min(N, 128);
-            group.push_back(GemmSpec{M, nc, K, 1, A + size_t(z) * M * K, (long long)M * K, hi + size_t(n0) * K,
-                                     lo + size_t(n0) * K, C + size_t(z) * M * N + n0, N, (long long)M * N,
-                                     accumulate != 0});
+            TCMatrix part{m.hi + size_t(n0) * K, m.lo + size_t(n0) * K, m.exp};
+            group.push_back(GemmSpec{M, nc, K, 1, A + size_t(z) * M * K, (long long)M * K, part,
+                                     C + size_t(z) * M * N + n0, N, (long long)M * N, accumulate != 0});
           }
         tc_gemm_group(cudaStream_t(0), group.data(), int(group.size()), status);
       }
@@ -874,16 +874,13 @@ extern "C" int mace_debug_gemm(int M, int N, int K, int batch, const float *A, c
     int st = 0;
     if (status)
       lapis::check(cudaMemcpy(&st, status, 4, cudaMemcpyDeviceToHost));
-    cudaFree(hi);
-    cudaFree(lo);
-    cudaFree(status);
+    release();
     if (st)
       throw lapis::Error("tensor-core GEMM reported status " + std::to_string(st));
     return 0;
   } catch (const std::exception &e) {
-    cudaFree(hi);
-    cudaFree(lo);
-    cudaFree(status);
+    cudaDeviceSynchronize();
+    release();
     lapis::set_c_api_error(e.what());
     return -1;
   }

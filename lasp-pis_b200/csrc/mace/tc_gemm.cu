@@ -1,30 +1,32 @@
-// FP32-accurate GEMM on the Blackwell tensor cores (tcgen05, kind::tf32, 3-term split).
+// FP32-accurate GEMM on the Blackwell tensor cores (tcgen05, kind::f16, 3-term fp16 split).
 //
 //   C[z] (+)= A[z] * B      A: [M][K] fp32 row-major per batch z (node or edge features),
-//                           B: given as two K-major tf32 planes Bhi/Blo [N][K] with
-//                              B = Bhi + Blo (split once at model load).
-// A needs no hi plane: an MMA of kind::tf32 reads the top 19 bits of each fp32 operand, so
-// the loaded A tile itself acts as A_hi = trunc_tf32(a), and only
-// A_lo = round_tf32(a - trunc_tf32(a)) is written beside it.  The remainder a - trunc(a) has
-// the sign of a, so it is rounded (not left to the MMA's truncation) to keep the dropped part
-// unbiased.  The tile product is accumulated in TMEM as A_hi*B_hi + A_lo*B_hi + A_hi*B_lo (the
-// dropped parts are below 2^-21 relative and of either sign), so the result carries
-// FP32-level error while the work runs on the tensor pipe.
+//                           B: given as two K-major fp16 planes Bhi/Blo [N][K] with
+//                              B 2^eB = Bhi + Blo (split once at model load, split_f16).
+// Each 128-row x 64-wide K slab of A is split in shared memory the same way, per row: with
+// 2^e the power of two that brings the row's largest |a| into [2^14, 2^15),
+// a 2^e = A_hi + A_lo, A_hi = round_fp16(a 2^e), A_lo = round_fp16(a 2^e - A_hi) (the
+// remainder is exact in fp32).  Each pair carries 22 significant bits, and the scaling keeps
+// every value of the row inside fp16's normal range down to 2^-17 of the row's largest.
+// The slab product A_lo*B_hi + A_hi*B_lo + A_hi*B_hi (the dropped A_lo*B_lo is below 2^-22
+// relative) runs on the fp16 tensor pipe, which has twice the tf32 rate.
 //
 // The tensor pipe adds products into its accumulator with truncation toward zero, which
-// biases long accumulations coherently.  So the dominant A_hi*B_hi term is accumulated
-// FRESH for every 32-wide K slab (4 MMAs) into one of two TMEM buffers and drained into
-// FP32 registers with round-to-nearest adds (overlapping the next slab), while the two
-// correction terms, 2^-11 smaller, accumulate over all of K in a per-tile correction
-// buffer drained once at the end of the tile.
+// biases long accumulations coherently.  So every slab is accumulated FRESH in one of two
+// TMEM buffers, the two correction terms first (their truncation is 2^-11 smaller), then the
+// four A_hi*B_hi steps, and drained into FP32 registers with one fused multiply-add by
+// 2^-(e + eB) (exact) and a round-to-nearest add, overlapping the next slab's MMAs.  The
+// drain first moves each slab result one ulp away from zero, which cancels the measured mean
+// shrinkage of a slab (one ulp on average) and leaves the product unbiased.
 //
 // Persistent: one CTA per SM walks the 128 x 128 output tiles (n fastest, so the CTAs that
-// run together share A tiles in L2) with a continuous pipeline across tiles.  TMEM holds
-// two slab buffers and two correction buffers (512 columns), so the MMAs of tile t+1 run
-// while tile t is drained and stored.  CTA = 12 warps:
-//   warp 0       TMA producer (A, Bhi, Blo per 32-wide K slab, SWIZZLE_128B, 3-stage ring)
-//   warp 1       MMA issuer (one elected thread; UMMA 128 x 128 x 8)
-//   warps 2..3   write A_lo beside the A tile in shared memory
+// run together share A tiles in L2) with a continuous pipeline across tiles.  CTA = 12 warps:
+//   warp 0       TMA producer: per slab the fp32 A tile (two 128 x 32 boxes) and the fp16
+//                Bhi, Blo tiles (128 x 64 each), SWIZZLE_128B, 3-stage ring
+//   warp 1       MMA issuer (one elected thread; UMMA 128 x 128 x 16)
+//   warps 2..3   split A in place: a thread reads whole fp32 rows of the slab and writes the
+//                row's A_hi over its first box and A_lo over its second (the fp16 K-major
+//                SWIZZLE_128B layout has the same 128-byte rows), plus the row's exponent
 //   warps 4..11  drain TMEM into FP32 registers: two warps per TMEM lane quadrant (lane =
 //                output row), each owning 64 of the 128 columns with two 32-column loads in
 //                flight; each writes its part of the tile as two 32 x 32 boxes staged
@@ -36,6 +38,7 @@
 #include "model.hpp"
 #include "tcgen05.cuh"
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <algorithm>
 #include <climits>
 #include <mutex>
@@ -43,23 +46,58 @@
 namespace mace {
 namespace {
 using namespace tc;
-constexpr int kBM = 128, kBN = 128, kBK = 32, kStages = 3;
-constexpr int kTileBytes = kBM * kBK * 4;        // 16 KiB (A, A_lo, Bhi, Blo tiles are equal)
-constexpr int kStageBytes = 4 * kTileBytes;      // A | A_lo | Bhi | Blo
+constexpr int kBM = 128, kBN = 128, kBK = 64, kStages = 3; // kBK: K per slab
+constexpr int kTileBytes = kBM * kBK * 2;        // 16 KiB: one 128 x 64 fp16 operand tile
+constexpr int kStageBytes = 4 * kTileBytes;      // fp32 A (then A_hi | A_lo) | Bhi | Blo
 constexpr int kBoxBytes = 32 * 32 * 4;           // one 32 x 32 output box (4 KiB)
 constexpr int kStagingBytes = 8 * kBoxBytes;     // one box per drain warp
-constexpr int kSmemBytes = 1024 /* align */ + kStages * kStageBytes + kStagingBytes + 128 /* barriers */;
+// Row exponents e + eB of the last kExpSlots slabs (int16 per row).  The split of slab g runs
+// only after the drain of slab g - 5 has released its TMEM buffer (TMA of g waits for the MMAs
+// of g - 3, which wait for the drain of g - 5), so 6 slots are never overwritten early.
+constexpr int kExpSlots = 6;
+constexpr int kExpBytes = kExpSlots * kBM * 2;
+constexpr int kSmemBytes = 1024 /* align */ + kStages * kStageBytes + kStagingBytes + kExpBytes + 256 /* barriers */;
 static_assert(kSmemBytes + 64 <= 232448, "shared memory budget");
-constexpr int kTmemCols = 4 * kBN; // hi*hi slab buffers 0/1, correction buffers 2/3 (512 columns)
+constexpr int kTmemCols = 2 * kBN; // two slab accumulators (256 columns)
 constexpr int kThreads = 384, kDrainThreads = 256;
 constexpr int kStatusGemmTimeout = 7;
 constexpr int kMaxGemmProblems = 16, kMaxGemmSegments = 16;
+constexpr uint32_t kIdesc = idesc_f16(kBM, kBN);
 
-// Instruction descriptor: D fp32, A/B tf32, both K-major, M = 128, N = 128.
-constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(kBN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
+  umma_f16_desc(tmem_d, a, b, kIdesc, accumulate);
+}
 
-__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
-  umma_tf32_desc(tmem_d, a, b, kIdesc, accumulate);
+// Row exponent e: 2^e brings the row's largest magnitude m into [2^14, 2^15), with e and
+// e + eB kept in [-126, 126] so that 2^e and 2^-(e + eB) are normal floats.
+__device__ __forceinline__ int row_exponent(float m, int eb) {
+  int ex = int(__float_as_uint(m) >> 23) & 0xff; // biased exponent (m >= 0)
+  int e = ex ? 141 - ex : (m > 0.f ? 126 : 0);
+  return min(max(e, max(-126, -126 - eb)), min(126, 126 - eb));
+}
+__device__ __forceinline__ float pow2(int e) { return __uint_as_float(uint32_t(127 + e) << 23); }
+// A slab result one ulp larger in magnitude (zero stays zero).  The tensor pipe's
+// accumulation truncates toward zero, and a slab's result measured 8.7e-8 smaller in mean
+// relative magnitude than the exact product, independent of K: one ulp, which is 2^-23 / m
+// of a result with mantissa m in [1, 2), 8.6e-8 on average over log-uniform mantissas.
+// Without this step the shrinkage is coherent across every GEMM output and grows the virial
+// error.
+__device__ __forceinline__ uint32_t away_ulp(uint32_t bits) { return bits + ((bits << 1) != 0u); }
+
+// Eight scaled values as fp16 hi and lo halves, packed for one 16-byte chunk of each plane.
+__device__ __forceinline__ void split8(const float *v, float sc, uint4 &hi, uint4 &lo) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    float x0 = v[2 * p] * sc, x1 = v[2 * p + 1] * sc;
+    __half2 hh = __floats2half2_rn(x0, x1);
+    float2 hf = __half22float2(hh);
+    __half2 ll = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+    h[p] = *reinterpret_cast<uint32_t *>(&hh);
+    l[p] = *reinterpret_cast<uint32_t *>(&ll);
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
 struct TileGrid {
@@ -78,13 +116,13 @@ struct TileGrid {
 // that add into the same output block): C = sum_s A_s B_s accumulates inside the tile.
 struct GemmSegment {
   CUtensorMap a, bhi, blo;
-  int ktiles;
+  int ktiles, eb; // K slabs; B's exponent eB
 };
 struct GemmProblem {
   CUtensorMap a, bhi, blo, c; // first K segment and the output
   TileGrid tg;
-  int ktiles, kt0, accumulate, tile0; // total K tiles, the first segment's; first tile in the group
-  int seg0, nseg;                     // further K segments
+  int ktiles, kt0, eb, accumulate, tile0; // total K slabs, the first segment's and its eB; first tile
+  int seg0, nseg;                         // further K segments
 };
 struct GemmGroup {
   GemmProblem p[kMaxGemmProblems];
@@ -103,15 +141,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char *staging = smem + kStages * kStageBytes;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(staging + kStagingBytes);
-  // bars: full[S] | ready[S] | empty[S] | tfull[2] | tfree[2] | cfull[2] | cfree[2] | done
+  int16_t *exps = reinterpret_cast<int16_t *>(staging + kStagingBytes); // [kExpSlots][kBM]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(staging + kStagingBytes + kExpBytes);
+  // bars: full[S] | ready[S] | empty[S] | tfull[2] | tfree[2] | done | xfull[kExpSlots]
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
   __shared__ int mma_done_issued; // whether the final commit to `done` was issued
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned full0 = smem_u32(bars), ready0 = full0 + 8 * kStages, empty0 = ready0 + 8 * kStages,
-           tfull0 = empty0 + 8 * kStages, tfree0 = tfull0 + 16, cfull0 = tfree0 + 16, cfree0 = cfull0 + 16,
-           done = cfree0 + 16;
+           tfull0 = empty0 + 8 * kStages, tfree0 = tfull0 + 16, done = tfree0 + 16, xfull0 = done + 8;
   if (threadIdx.x == 0) {
     abort_flag = 0;
     mma_done_issued = 0;
@@ -123,10 +161,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull0 + 8 * b, 1);
       mbar_init(tfree0 + 8 * b, kDrainThreads);
-      mbar_init(cfull0 + 8 * b, 1);
-      mbar_init(cfree0 + 8 * b, kDrainThreads);
     }
     mbar_init(done, 1);
+    for (int x = 0; x < kExpSlots; ++x)
+      mbar_init(xfull0 + 8 * x, 64);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -145,45 +183,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int g = 0, q = 0;
       bool ok = true;
+      auto load = [&](const CUtensorMap *a, const CUtensorMap *bhi, const CUtensorMap *blo, int kt, int n0, int m0,
+                      int z) {
+        int s = g % kStages;
+        if (g >= kStages && !(ok = mbar_wait(empty0 + 8 * s, ((g / kStages) - 1) & 1, &abort_flag)))
+          return;
+        unsigned base = smem_u32(smem + s * kStageBytes), full = full0 + 8 * s;
+        mbar_expect_tx(full, kStageBytes);
+        tma_load_3d(base, a, kt * kBK, m0, z, full);
+        tma_load_3d(base + kTileBytes, a, kt * kBK + 32, m0, z, full);
+        tma_load_2d(base + 2 * kTileBytes, bhi, kt * kBK, n0, full);
+        tma_load_2d(base + 3 * kTileBytes, blo, kt * kBK, n0, full);
+        ++g;
+      };
       for (int t = blockIdx.x; t < gg.tiles && ok; t += gridDim.x) {
         const GemmProblem &pr = gg.find(t, q);
         int n0, m0, z;
         pr.tg.coords(t - pr.tile0, n0, m0, z);
-        for (int kt = 0; kt < pr.kt0; ++kt, ++g) {
-          int s = g % kStages;
-          if (g >= kStages && !(ok = mbar_wait(empty0 + 8 * s, ((g / kStages) - 1) & 1, &abort_flag)))
-            break;
-          unsigned base = smem_u32(smem + s * kStageBytes);
-          mbar_expect_tx(full0 + 8 * s, 3 * kTileBytes);
-          tma_load_3d(base, &pr.a, kt * kBK, m0, z, full0 + 8 * s);
-          tma_load_2d(base + 2 * kTileBytes, &pr.bhi, kt * kBK, n0, full0 + 8 * s);
-          tma_load_2d(base + 3 * kTileBytes, &pr.blo, kt * kBK, n0, full0 + 8 * s);
-        }
-        for (int sg = pr.seg0; sg < pr.seg0 + pr.nseg && ok; ++sg) {
-          const GemmSegment &seg = gg.seg[sg];
-          for (int kt = 0; kt < seg.ktiles; ++kt, ++g) {
-            int s = g % kStages;
-            if (g >= kStages && !(ok = mbar_wait(empty0 + 8 * s, ((g / kStages) - 1) & 1, &abort_flag)))
-              break;
-            unsigned base = smem_u32(smem + s * kStageBytes);
-            mbar_expect_tx(full0 + 8 * s, 3 * kTileBytes);
-            tma_load_3d(base, &seg.a, kt * kBK, m0, z, full0 + 8 * s);
-            tma_load_2d(base + 2 * kTileBytes, &seg.bhi, kt * kBK, n0, full0 + 8 * s);
-            tma_load_2d(base + 3 * kTileBytes, &seg.blo, kt * kBK, n0, full0 + 8 * s);
-          }
-        }
+        for (int kt = 0; kt < pr.kt0 && ok; ++kt)
+          load(&pr.a, &pr.bhi, &pr.blo, kt, n0, m0, z);
+        for (int sg = pr.seg0; sg < pr.seg0 + pr.nseg && ok; ++sg)
+          for (int kt = 0; kt < gg.seg[sg].ktiles && ok; ++kt)
+            load(&gg.seg[sg].a, &gg.seg[sg].bhi, &gg.seg[sg].blo, kt, n0, m0, z);
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       bool ok = true;
-      int g = 0, i = 0, q = 0;
-      for (int t = blockIdx.x; t < gg.tiles && ok; t += gridDim.x, ++i) {
-        int ktiles = gg.find(t, q).ktiles, c = i & 1;
-        if (i >= 2 && !(ok = mbar_wait(cfree0 + 8 * c, ((i >> 1) - 1) & 1, &abort_flag)))
-          break;
-        uint32_t corr = tmem + uint32_t((2 + c) * kBN);
+      int g = 0, q = 0;
+      for (int t = blockIdx.x; t < gg.tiles && ok; t += gridDim.x) {
+        int ktiles = gg.find(t, q).ktiles;
         for (int kt = 0; kt < ktiles; ++kt, ++g) {
           int s = g % kStages, b = g & 1;
           if (!(ok = mbar_wait(ready0 + 8 * s, (g / kStages) & 1, &abort_flag)))
@@ -192,55 +222,87 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           tc_fence_after();
           unsigned base = smem_u32(smem + s * kStageBytes);
+          uint32_t d = tmem + uint32_t(b * kBN);
+          // 16-wide K steps are 32 bytes apart inside the 128-byte swizzled rows.
 #pragma unroll
-          for (int j = 0; j < kBK / 8; ++j) {
-            uint64_t a_hi = smem_desc(base + 32 * j), a_lo = smem_desc(base + kTileBytes + 32 * j);
-            uint64_t b_hi = smem_desc(base + 2 * kTileBytes + 32 * j), b_lo = smem_desc(base + 3 * kTileBytes + 32 * j);
-            umma_tf32(tmem + uint32_t(b * kBN), a_hi, b_hi, j ? 1u : 0u);
-            umma_tf32(corr, a_lo, b_hi, (kt | j) ? 1u : 0u);
-            umma_tf32(corr, a_hi, b_lo, 1u);
+          for (int j = 0; j < kBK / 16; ++j) {
+            umma(d, smem_desc(base + kTileBytes + 32 * j), smem_desc(base + 2 * kTileBytes + 32 * j), j ? 1u : 0u);
+            umma(d, smem_desc(base + 32 * j), smem_desc(base + 3 * kTileBytes + 32 * j), 1u);
           }
+#pragma unroll
+          for (int j = 0; j < kBK / 16; ++j)
+            umma(d, smem_desc(base + 32 * j), smem_desc(base + 2 * kTileBytes + 32 * j), 1u);
           umma_commit(tfull0 + 8 * b);
           umma_commit(empty0 + 8 * s);
         }
-        if (ok)
-          umma_commit(cfull0 + 8 * c);
       }
       umma_commit(done);
       mma_done_issued = 1;
     }
   } else if (warp < 4) {
-    // ---------------- A split: A_lo beside the tile (A_hi is the tile itself) ----------------
+    // ---------------- A split, in place: rows t and t + 64 of every slab ----------------
     int t = threadIdx.x - 64, g = 0, q = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < gg.tiles && ok; tile += gridDim.x)
-      for (int kt = 0, ktiles = gg.find(tile, q).ktiles; kt < ktiles; ++kt, ++g) {
+    for (int tile = blockIdx.x; tile < gg.tiles && ok; tile += gridDim.x) {
+      const GemmProblem &pr = gg.find(tile, q);
+      int sg = pr.seg0 - 1, left = pr.kt0, eb = pr.eb;
+      for (int kt = 0; kt < pr.ktiles; ++kt, ++g) {
+        while (!left) { // the slab's K segment and its B exponent
+          ++sg;
+          left = gg.seg[sg].ktiles;
+          eb = gg.seg[sg].eb;
+        }
+        --left;
         int s = g % kStages;
         ok = mbar_wait(full0 + 8 * s, (g / kStages) & 1, &abort_flag);
         if (!__all_sync(0xffffffffu, ok)) {
           ok = false;
           break;
         }
-        const float4 *a = reinterpret_cast<const float4 *>(smem + s * kStageBytes);
-        float4 *lo = reinterpret_cast<float4 *>(smem + s * kStageBytes + kTileBytes);
+        unsigned char *st = smem + s * kStageBytes;
+        int16_t *ex = exps + (g % kExpSlots) * kBM;
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          int r = t + 64 * h, sw = r & 7;
+          unsigned char *ra = st + r * 128, *rb = st + kTileBytes + r * 128; // row r of each box
+          float v[64];
 #pragma unroll
-        for (int q = 0; q < kTileBytes / 16 / 64; ++q) {
-          float4 v = a[t + 64 * q], l;
-          l.x = tf32_hi(v.x - tf32_trunc(v.x)), l.y = tf32_hi(v.y - tf32_trunc(v.y));
-          l.z = tf32_hi(v.z - tf32_trunc(v.z)), l.w = tf32_hi(v.w - tf32_trunc(v.w));
-          lo[t + 64 * q] = l;
+          for (int c = 0; c < 8; ++c) {
+            float4 x = *reinterpret_cast<const float4 *>(ra + ((c ^ sw) << 4));
+            float4 y = *reinterpret_cast<const float4 *>(rb + ((c ^ sw) << 4));
+            v[4 * c] = x.x, v[4 * c + 1] = x.y, v[4 * c + 2] = x.z, v[4 * c + 3] = x.w;
+            v[32 + 4 * c] = y.x, v[33 + 4 * c] = y.y, v[34 + 4 * c] = y.z, v[35 + 4 * c] = y.w;
+          }
+          float m = 0.f;
+#pragma unroll
+          for (int k = 0; k < 64; ++k)
+            m = fmaxf(m, fabsf(v[k]));
+          int e = row_exponent(m, eb);
+          float sc = pow2(e);
+          // fp16 chunk c holds elements 8c .. 8c + 7 of the row: A_hi over the first box,
+          // A_lo over the second, at the same swizzled positions.
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint4 hi, lo;
+            split8(v + 8 * c, sc, hi, lo);
+            *reinterpret_cast<uint4 *>(ra + ((c ^ sw) << 4)) = hi;
+            *reinterpret_cast<uint4 *>(rb + ((c ^ sw) << 4)) = lo;
+          }
+          ex[r] = int16_t(e + eb);
         }
+        mbar_arrive(xfull0 + 8 * (g % kExpSlots)); // the exponents, for the drain
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_arrive(ready0 + 8 * s);
       }
+    }
   } else {
     // ---------------- drain + store: lane = output row, 64 columns per warp ----------------
-    int quarter = warp & 3, col0 = 64 * ((warp - 4) >> 2);
+    int quarter = warp & 3, col0 = 64 * ((warp - 4) >> 2), row = 32 * quarter + lane;
     uint32_t lane_addr = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(col0);
     unsigned char *box = staging + (warp - 4) * kBoxBytes; // this warp's staging box
     bool ok = true;
-    int g = 0, i = 0, q = 0;
-    for (int t = blockIdx.x; t < gg.tiles && ok; t += gridDim.x, ++i) {
+    int g = 0, q = 0;
+    for (int t = blockIdx.x; t < gg.tiles && ok; t += gridDim.x) {
       const GemmProblem &pr = gg.find(t, q);
       int n0, m0, z, ktiles = pr.ktiles;
       pr.tg.coords(t - pr.tile0, n0, m0, z);
@@ -255,10 +317,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        int x = g % kExpSlots;
+        ok = mbar_wait(xfull0 + 8 * x, (g / kExpSlots) & 1, &abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         uint32_t r0[32], r1[32];
         tmem_ld32_async(lane_addr + uint32_t(b * kBN), r0);
         tmem_ld32_async(lane_addr + uint32_t(b * kBN + 32), r1);
+        float inv = pow2(-int(exps[x * kBM + row]));
         tmem_wait_ld();
         tmem_anchor(r0);
         tmem_anchor(r1);
@@ -266,28 +335,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(tfree0 + 8 * b);
 #pragma unroll
         for (int k = 0; k < 32; ++k) {
-          acc[k] += __uint_as_float(r0[k]);
-          acc[32 + k] += __uint_as_float(r1[k]);
+          acc[k] = fmaf(__uint_as_float(away_ulp(r0[k])), inv, acc[k]);
+          acc[32 + k] = fmaf(__uint_as_float(away_ulp(r1[k])), inv, acc[32 + k]);
         }
       }
       if (!ok)
         break;
-      // Correction buffer: added while the two boxes are staged and stored.
-      int c = i & 1;
-      ok = mbar_wait(cfull0 + 8 * c, (i >> 1) & 1, &abort_flag);
-      if (!__all_sync(0xffffffffu, ok)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t r0[32], r1[32];
-      tmem_ld32_async(lane_addr + uint32_t((2 + c) * kBN), r0);
-      tmem_ld32_async(lane_addr + uint32_t((2 + c) * kBN + 32), r1);
-      tmem_wait_ld();
-      tmem_anchor(r0);
-      tmem_anchor(r1);
-      tc_fence_before();
-      mbar_arrive(cfree0 + 8 * c);
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         // The previous store must have read the box before it is rewritten.
@@ -295,14 +348,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           bulk_wait_read();
         __syncwarp();
         // Row `lane` of the box: 16-byte chunk q at position q ^ (lane & 7) (SWIZZLE_128B).
-        unsigned char *row = box + lane * 128;
+        unsigned char *rowp = box + lane * 128;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float *a = acc + 32 * j + 4 * q;
-          const uint32_t *r = (j ? r1 : r0) + 4 * q;
-          *reinterpret_cast<float4 *>(row + ((q ^ (lane & 7)) << 4)) =
-              make_float4(a[0] + __uint_as_float(r[0]), a[1] + __uint_as_float(r[1]),
-                          a[2] + __uint_as_float(r[2]), a[3] + __uint_as_float(r[3]));
+        for (int q4 = 0; q4 < 8; ++q4) {
+          const float *a = acc + 32 * j + 4 * q4;
+          *reinterpret_cast<float4 *>(rowp + ((q4 ^ (lane & 7)) << 4)) = make_float4(a[0], a[1], a[2], a[3]);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
@@ -365,7 +415,7 @@ CUtensorMap make_map(const float *base, int cols, int rows, int rank, int batch,
   CUtensorMap map;
   cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(rows), cuuint64_t(batch)};
   cuuint64_t strides[2] = {cuuint64_t(ld) * 4, cuuint64_t(batch_stride) * 4};
-  cuuint32_t box[3] = {kBK, cuuint32_t(box_rows), 1};
+  cuuint32_t box[3] = {32, cuuint32_t(box_rows), 1};
   cuuint32_t elem[3] = {1, 1, 1};
   CUresult r = encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, cuuint32_t(rank), const_cast<float *>(base), dims,
                          strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -374,25 +424,27 @@ CUtensorMap make_map(const float *base, int cols, int rows, int rank, int batch,
     throw lapis::Error("cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
   return map;
 }
-} // namespace
 
-CUtensorMap tc_map_2d(const float *base, int cols, long long rows, int box_cols, int box_rows) {
-  if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * 4) % 16 || box_cols * 4 > 128 || box_rows > 256)
-    throw lapis::Error("tensor map operand is not 16-byte aligned or the box is too large");
+// Tensor map over an fp16 B plane [N][K], box 64 (K) x 128 (N), SWIZZLE_128B.
+CUtensorMap make_map_f16(const uint16_t *base, int K, int N) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (K * 2) % 16)
+    throw lapis::Error("tensor-core GEMM operand is not 16-byte aligned");
   CUtensorMap map;
-  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
-  cuuint64_t strides[1] = {cuuint64_t(cols) * 4};
-  cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
+  cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(N)};
+  cuuint64_t strides[1] = {cuuint64_t(K) * 2};
+  cuuint32_t box[2] = {kBK, kBN};
   cuuint32_t elem[2] = {1, 1};
-  CUresult r = encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box,
+  CUresult r = encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t *>(base), dims, strides, box,
                          elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     throw lapis::Error("cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
   return map;
 }
+} // namespace
 
-bool tc_gemm_supported(int N, int K) { return N % kBN == 0 && K % kBK == 0 && K >= kBK; }
+// K in multiples of 32: the last slab of a K = 32 mod 64 problem reads zeros past K.
+bool tc_gemm_supported(int N, int K) { return N % kBN == 0 && K % 32 == 0 && K >= 32; }
 
 namespace {
 void check_problem(const GemmSpec &g) {
@@ -435,17 +487,20 @@ void launch_group(cudaStream_t s, const GemmSpec *specs, int count, int *status)
     GemmProblem &p = gg.p[n - 1];
     // A as [batch][M][K] (always a rank-3 map: the kernel issues 3D loads); B as [N][K].
     CUtensorMap a = make_map(g.A, g.K, g.M, 3, g.batch, g.batch > 1 ? g.strideA : (long long)g.M * g.K);
-    CUtensorMap bhi = make_map(g.Bhi, g.K, g.N, 2, 1, 0), blo = make_map(g.Blo, g.K, g.N, 2, 1, 0);
+    CUtensorMap bhi = make_map_f16(g.B.hi, g.K, g.N), blo = make_map_f16(g.B.lo, g.K, g.N);
+    int slabs = (g.K + kBK - 1) / kBK;
     if (!g.join) {
       p.a = a, p.bhi = bhi, p.blo = blo;
-      p.kt0 = g.K / kBK;
+      p.kt0 = slabs;
+      p.eb = g.B.exp;
     } else {
       GemmSegment &sg = gg.seg[ns++];
       sg.a = a, sg.bhi = bhi, sg.blo = blo;
-      sg.ktiles = g.K / kBK;
+      sg.ktiles = slabs;
+      sg.eb = g.B.exp;
       p.nseg += 1;
     }
-    p.ktiles += g.K / kBK;
+    p.ktiles += slabs;
   }
   if (!n)
     return;
@@ -456,10 +511,10 @@ void launch_group(cudaStream_t s, const GemmSpec *specs, int count, int *status)
 }
 } // namespace
 
-// C[z] (+)= A[z] * B  with B = Bhi + Blo given K-major ([N][K]); batch z = 0..batch-1.
-void tc_gemm(cudaStream_t s, int M, int N, int K, int batch, const float *A, long long strideA, const float *Bhi,
-             const float *Blo, float *C, int ldc, long long strideC, bool accumulate, int *status) {
-  GemmSpec g{M, N, K, batch, A, strideA, Bhi, Blo, C, ldc, strideC, accumulate};
+// C[z] (+)= A[z] * B  with B given as its fp16 split (K-major, [N][K]); batch z = 0..batch-1.
+void tc_gemm(cudaStream_t s, int M, int N, int K, int batch, const float *A, long long strideA, const TCMatrix &B,
+             float *C, int ldc, long long strideC, bool accumulate, int *status) {
+  GemmSpec g{M, N, K, batch, A, strideA, B, C, ldc, strideC, accumulate};
   tc_gemm_group(s, &g, 1, status);
 }
 

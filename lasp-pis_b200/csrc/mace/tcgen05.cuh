@@ -1,6 +1,6 @@
 // Blackwell (sm_100a) tensor-core building blocks shared by the GEMM and edge kernels:
 // mbarriers with bounded waits, TMA tile loads, shared-memory matrix descriptors (K-major,
-// SWIZZLE_128B), kind::tf32 UMMA, commits, TMEM loads and the tf32 hi/lo split.
+// SWIZZLE_128B), kind::f16 UMMA, commits and TMEM loads.
 #pragma once
 #include <cuda.h>
 #include <cstdint>
@@ -85,23 +85,6 @@ __device__ __forceinline__ void tmem_anchor(uint32_t (&r)[32]) {
                  "+r"(r[29]), "+r"(r[30]), "+r"(r[31])::"memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-               "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                 "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-                 "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-                 "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
-                 "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-               : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-  tmem_anchor(r);
-#pragma unroll
-  for (int k = 0; k < 32; ++k)
-    v[k] = __uint_as_float(r[k]);
-}
-
 // 32 columns of this warp's 32 lanes without waiting; follow with tmem_wait_ld().
 __device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -114,35 +97,18 @@ __device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32
                : "r"(taddr));
 }
 
-// UMMA: D (TMEM) (+)= A (smem) * B (smem), kind::tf32, instruction descriptor `idesc`.
-__device__ __forceinline__ void umma_tf32_desc(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
-                                               uint32_t accumulate) {
+// UMMA: D (TMEM) (+)= A (smem) * B (smem), kind::f16 (both operands fp16), instruction
+// descriptor `idesc`.
+__device__ __forceinline__ void umma_f16_desc(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                              uint32_t accumulate) {
   asm volatile("{\n\t.reg .pred p;\n\t"
                "setp.ne.b32 p, %4, 0;\n\t"
-               "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+               "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
                "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
 }
-// Instruction descriptor for D fp32, A/B tf32 K-major, shape M x N.
-__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
-}
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
-  uint32_t r[8];
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-#pragma unroll
-  for (int k = 0; k < 8; ++k)
-    v[k] = __uint_as_float(r[k]);
-}
-__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float (&v)[4]) {
-  uint32_t r[4];
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(taddr));
-#pragma unroll
-  for (int k = 0; k < 4; ++k)
-    v[k] = __uint_as_float(r[k]);
+// Instruction descriptor for D fp32, A and B fp16 (format 0), both K-major, shape M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // TMA tensor store / fp32 add-reduction of a shared-memory box into global memory (rows or
@@ -177,11 +143,5 @@ __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.p
 // Wait until the issued bulk copies have read their shared-memory source / fully completed.
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-// Round to tf32 (nearest, ties away) and the exact fp32 remainder.
-__device__ __forceinline__ float tf32_hi(float x) {
-  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xffffe000u);
-}
-// The tf32 value a kind::tf32 MMA reads from an fp32 operand: its top 19 bits (truncation).
-__device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
 } // namespace tc
 } // namespace mace
