@@ -84,15 +84,16 @@ __device__ __forceinline__ float pow2(int e) { return __uint_as_float(uint32_t(1
 // error.
 __device__ __forceinline__ uint32_t away_ulp(uint32_t bits) { return bits + ((bits << 1) != 0u); }
 
-// Eight scaled values as fp16 hi and lo halves, packed for one 16-byte chunk of each plane.
-__device__ __forceinline__ void split8(const float *v, float sc, uint4 &hi, uint4 &lo) {
+// Eight scaled values as fp16 hi and lo halves, packed for one 16-byte chunk of each plane
+// (paired fp32 instructions: x = v sc, lo = x - float(hi), both exact).
+__device__ __forceinline__ void split8(const float *v, float2 sc, uint4 &hi, uint4 &lo) {
   uint32_t h[4], l[4];
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
-    float x0 = v[2 * p] * sc, x1 = v[2 * p + 1] * sc;
-    __half2 hh = __floats2half2_rn(x0, x1);
-    float2 hf = __half22float2(hh);
-    __half2 ll = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+    float2 x = __fmul2_rn(make_float2(v[2 * p], v[2 * p + 1]), sc);
+    __half2 hh = __float22half2_rn(x);
+    float2 r = __ffma2_rn(__half22float2(hh), make_float2(-1.f, -1.f), x);
+    __half2 ll = __float22half2_rn(r);
     h[p] = *reinterpret_cast<uint32_t *>(&hh);
     l[p] = *reinterpret_cast<uint32_t *>(&ll);
   }
@@ -273,12 +274,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             v[4 * c] = x.x, v[4 * c + 1] = x.y, v[4 * c + 2] = x.z, v[4 * c + 3] = x.w;
             v[32 + 4 * c] = y.x, v[33 + 4 * c] = y.y, v[34 + 4 * c] = y.z, v[35 + 4 * c] = y.w;
           }
-          float m = 0.f;
+          // Row maximum as an 8-way tree (short dependency chains).
+          float mx[8];
 #pragma unroll
-          for (int k = 0; k < 64; ++k)
-            m = fmaxf(m, fabsf(v[k]));
-          int e = row_exponent(m, eb);
-          float sc = pow2(e);
+          for (int j = 0; j < 8; ++j)
+            mx[j] = fabsf(v[j]);
+#pragma unroll
+          for (int k = 8; k < 64; ++k)
+            mx[k & 7] = fmaxf(mx[k & 7], fabsf(v[k]));
+#pragma unroll
+          for (int w = 4; w; w >>= 1)
+#pragma unroll
+            for (int j = 0; j < w; ++j)
+              mx[j] = fmaxf(mx[j], mx[j + w]);
+          int e = row_exponent(mx[0], eb);
+          float2 sc = make_float2(pow2(e), pow2(e));
           // fp16 chunk c holds elements 8c .. 8c + 7 of the row: A_hi over the first box,
           // A_lo over the second, at the same swizzled positions.
 #pragma unroll
