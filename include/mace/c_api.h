@@ -69,7 +69,7 @@ MACE_EXPORT long long mace_last_edges(void *handle, int *out, long long capacity
 MACE_EXPORT int mace_profile(void *handle, int enable);
 /* Test hook for the node-linear GEMMs: C[z] (+)= A[z] * B on the current device for z < batch,
  * A [batch][M][K], B [K][N], C [batch][M][N] row-major device arrays; mode 0 runs the FP32
- * SIMT kernel, mode 1 the tensor-core (tcgen05, split-tf32) kernel, mode 2 the same as a
+ * SIMT kernel, mode 1 the tensor-core (tcgen05, fp16-split) kernel, mode 2 the same as a
  * grouped launch (one problem per batch plane, columns split 128 | N - 128), mode 3 with K
  * split into two segments with their own A and B copies (K >= 64).  Blocks; returns 0 or -1.
  * No counterpart in the reference. */

@@ -5,7 +5,7 @@
 // r-derivative dw = cut dR + dcut (R + b), come from dense E x 64 x (P*128) GEMMs per layer
 // over rows the radial kernel has already scaled:
 //     R' = (cut h) W,   dR' = (cut dh + dcut h) W,   then  w = R' + cut b,  dw = dR' + dcut b.
-// They run on the tensor cores (tc_gemm, tf32 hi/lo split with FP32 drains) into an HBM
+// They run on the tensor cores (tc_gemm, fp16 hi/lo split with FP32 drains) into an HBM
 // buffer, chunked by receivers, and the kernels below consume them:
 //   forward   messages and density, as mace/src/mh1.cu:331-389;
 //   backward  tensor-product adjoints, r-tangent and per-edge force, as mh1.cu:390-452.
