@@ -71,7 +71,9 @@ MACE_EXPORT int mace_profile(void *handle, int enable);
  * A [batch][M][K], B [K][N], C [batch][M][N] row-major device arrays; mode 0 runs the FP32
  * SIMT kernel, mode 1 the tensor-core (tcgen05, fp16-split) kernel, mode 2 the same as a
  * grouped launch (one problem per batch plane, columns split 128 | N - 128), mode 3 with K
- * split into two segments with their own A and B copies (K >= 64).  Blocks; returns 0 or -1.
+ * split into two segments with their own A and B copies (K >= 64), mode 4 with A given as
+ * fp16 split planes and per-64 exponents made on the host (K a multiple of 64).  Blocks;
+ * returns 0 or -1.
  * No counterpart in the reference. */
 MACE_EXPORT int mace_debug_gemm(int M, int N, int K, int batch, const float *A, const float *B, float *C,
                                 int accumulate, int mode);

@@ -310,9 +310,18 @@ std::vector<Result> MH1::compute(bool batch) {
       launch_message_forward(s, k, c.geometry, l, ea, ro[k], up[k], msg, rho[k]);
     timer.mark("forward" + std::to_string(k) + ".messages");
     linear(s, n, l.one, msg, raw[k], false, false, status);
-    launch_normalize_gate(s, n, raw[k], res[k], rho[k], l.alpha, l.beta, cst[11], cst[12], gate);
+    // The gate feeds only linear_2: on the tensor cores it is written as the GEMM's split
+    // operand (the same bytes as fp32, plus one exponent per 64 values), so the GEMM skips
+    // its own split.
+    SplitPlanes gs;
+    if (status && linear_takes_split(l.two, false)) {
+      gs.hi = reinterpret_cast<uint16_t *>(gate);
+      gs.lo = gs.hi + size_t(n) * 8192;
+      gs.exp = c.array<int16_t>("mh.t.gate.exp", size_t(n) * 128);
+    }
+    launch_normalize_gate(s, n, raw[k], res[k], rho[k], l.alpha, l.beta, cst[11], cst[12], gate, gs);
     timer.mark("forward" + std::to_string(k) + ".node");
-    linear(s, n, l.two, gate, pin[k], false, false, status); // one grouped tensor-core launch
+    linear(s, n, l.two, gate, pin[k], false, false, status, 0, 0, gs.hi ? &gs : nullptr); // one grouped launch
     timer.mark("forward" + std::to_string(k) + ".linear_2");
     launch_product(s, n, l, pin[k], poly);
     linear(s, n, l.plin, poly, hidden[k], false, true, status);

@@ -23,6 +23,16 @@ struct TCMatrix {
   int exp = 0;
   explicit operator bool() const { return hi != nullptr; }
 };
+// An fp32 array written as the tensor-core GEMM's split operand: element i is
+// (hi[i] + lo[i]) 2^-exp[i / 64], hi and lo fp16 (bit patterns) rounded to nearest, with one
+// exponent per 64 consecutive elements (a row's K slab) that brings the slab's largest
+// magnitude into [2^14, 2^15) (split_exponent).  The GEMM then loads both planes by TMA and
+// skips its own split.
+struct SplitPlanes {
+  uint16_t *hi = nullptr, *lo = nullptr;
+  int16_t *exp = nullptr;
+  explicit operator bool() const { return hi != nullptr; }
+};
 // Tensor-core copies of one path's weight W [in_mul][out_mul]: forward planes are K-major for
 // Y = X W ([out_mul][in_mul]), backward planes for X_grad = Y_grad W^T ([in_mul][out_mul]).
 // Empty when the shape is not eligible.
@@ -171,8 +181,11 @@ void launch_ghost_reactions(cudaStream_t, const SenderIndex &, int n_own, const 
 // product for the backward.  Paths with tensor-core-eligible shapes run on tc_gemm.
 // nx / ny: row stride of x's / y's component blocks (0: n), for arrays with rows beyond the n
 // computed ones (the ghost rows of a domain-decomposed evaluation).
+// xs: x given as SplitPlanes (every path on the tensor cores, input widths multiples of 64).
 void linear(cudaStream_t, int n, const Linear &, const float *x, float *y, bool backward = false,
-            bool add = false, int *status = nullptr, int nx = 0, int ny = 0);
+            bool add = false, int *status = nullptr, int nx = 0, int ny = 0, const SplitPlanes *xs = nullptr);
+// Whether linear() can take its input as SplitPlanes (tensor-core linears, every path eligible).
+bool linear_takes_split(const Linear &, bool backward);
 // Tensor-core GEMM (tc_gemm.cu): C[z] (+)= A[z] B, B given as its fp16 split, K-major [N][K].
 bool tc_gemm_supported(int N, int K);
 void tc_gemm(cudaStream_t, int M, int N, int K, int batch, const float *A, long long strideA, const TCMatrix &B,
@@ -190,6 +203,12 @@ struct GemmSpec {
   long long strideC;
   bool accumulate;
   bool join = false;
+  // A given already split (SplitPlanes, K a multiple of 64): its planes at A's element
+  // offset (batch stride strideA), its exponents (one per row and 64-wide slab, batch stride
+  // strideAexp); A itself is then not read.
+  const uint16_t *Ahi = nullptr, *Alo = nullptr;
+  const int16_t *Aexp = nullptr;
+  long long strideAexp = 0;
 };
 void tc_gemm_group(cudaStream_t, const GemmSpec *specs, int count, int *status);
 // Host split of a weight matrix: w 2^exp = hi + lo, both fp16 (bit patterns) rounded to
@@ -202,8 +221,10 @@ bool tensor_core_linears();
 bool projection_edges();
 // pre = raw / (alpha + beta density) + res is not stored: the backward recomputes it from raw
 // and res (the same FP32 expression, so the same values).  pre_grad may alias res.
+// gs set: the gate goes out as SplitPlanes (the tensor-core linear_2's input) instead of fp32.
 void launch_normalize_gate(cudaStream_t, int n, const float *raw, const float *res, const float *density,
-                           float alpha, float beta, float scalar_scale, float gate_scale, float *gate);
+                           float alpha, float beta, float scalar_scale, float gate_scale, float *gate,
+                           SplitPlanes gs = {});
 void launch_gate_norm_backward(cudaStream_t, int n, const float *res, const float *raw, const float *density,
                                const float *gate_grad, float alpha, float beta, float scalar_scale,
                                float gate_scale, float *pre_grad, float *raw_grad, float *density_grad);

@@ -13,9 +13,13 @@
 // normalisation VJP (backward); the reference launches them separately.
 #include "model.hpp"
 #include "product_table.h"
+#include "tcgen05.cuh"
 #include <type_traits>
 #include "../lapis/launch.cuh"
 #include <cstdlib>
+#include <cuda_fp16.h>
+#include <cmath>
+#include <cstring>
 #include <string>
 #include <vector>
 
@@ -201,12 +205,37 @@ __device__ __forceinline__ void normalized4(const float *raw, const float *res, 
     u[j] = r[j] / den + q[j];
 }
 
-__global__ void normalize_gate_kernel(int n, const float *raw, const float *res, const float *rho, float alpha,
-                                      float beta, float cs, float cg, float *gate) {
-  int q = blockIdx.x * blockDim.x + threadIdx.x;
-  if (q >= n * 128)
+// Four gate values at element k: fp32, or (gs set) as the tensor-core GEMM's split operand.
+// The 16 lanes holding one 64-wide slab of a row (aligned groups of 16) reduce its maximum.
+__device__ __forceinline__ void put4(float *gate, const SplitPlanes &gs, size_t k, const float (&v)[4], int lane) {
+  if (!gs.hi) {
+    st4(gate, k, v);
     return;
-  int i = q >> 7, c = (q & 127) * 4;
+  }
+  float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+  for (int o = 1; o < 16; o <<= 1)
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  int e = tc::split_exponent(m);
+  float2 sc = make_float2(__uint_as_float(uint32_t(127 + e) << 23), __uint_as_float(uint32_t(127 + e) << 23));
+  float2 x0 = __fmul2_rn(make_float2(v[0], v[1]), sc), x1 = __fmul2_rn(make_float2(v[2], v[3]), sc);
+  __half2 h0 = __float22half2_rn(x0), h1 = __float22half2_rn(x1);
+  __half2 l0 = __float22half2_rn(__ffma2_rn(__half22float2(h0), make_float2(-1.f, -1.f), x0));
+  __half2 l1 = __float22half2_rn(__ffma2_rn(__half22float2(h1), make_float2(-1.f, -1.f), x1));
+  *reinterpret_cast<uint2 *>(gs.hi + k) =
+      make_uint2(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1));
+  *reinterpret_cast<uint2 *>(gs.lo + k) =
+      make_uint2(*reinterpret_cast<uint32_t *>(&l0), *reinterpret_cast<uint32_t *>(&l1));
+  if (!(lane & 15))
+    gs.exp[k / 64] = int16_t(e);
+}
+
+__global__ void normalize_gate_kernel(int n, const float *raw, const float *res, const float *rho, float alpha,
+                                      float beta, float cs, float cg, float *gate, SplitPlanes gs) {
+  int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= n * 128) // whole warps: 128 threads per node
+    return;
+  int i = q >> 7, c = (q & 127) * 4, lane = threadIdx.x & 31;
   float den = alpha + beta * rho[i];
   float u[4][4], o[4];
 #pragma unroll
@@ -215,7 +244,7 @@ __global__ void normalize_gate_kernel(int n, const float *raw, const float *res,
 #pragma unroll
   for (int j = 0; j < 4; ++j)
     o[j] = cs * u[0][j] * sigm(u[0][j]);
-  st4(gate, size_t(i) * 512 + c, o);
+  put4(gate, gs, size_t(i) * 512 + c, o, lane);
 #pragma unroll
   for (int l = 1; l <= 3; ++l) {
     float gl[4];
@@ -229,7 +258,7 @@ __global__ void normalize_gate_kernel(int n, const float *raw, const float *res,
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         o[j] = p[j] * cg * gl[j];
-      st4(gate, (size_t(m) * n + i) * 512 + c, o);
+      put4(gate, gs, (size_t(m) * n + i) * 512 + c, o, lane);
     }
   }
 }
@@ -604,8 +633,17 @@ bool projection_edges() {
   return on;
 }
 
+bool linear_takes_split(const Linear &l, bool backward) {
+  if (!tensor_core_linears())
+    return false;
+  for (size_t q = 0; q < l.paths.size(); ++q)
+    if (!(backward ? l.tc[q].bwd : l.tc[q].fwd) || (backward ? l.paths[q].out_mul : l.paths[q].in_mul) % 64)
+      return false;
+  return !l.paths.empty();
+}
+
 void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bool backward, bool add, int *status,
-            int nx, int ny) {
+            int nx, int ny, const SplitPlanes *xs) {
   if (!n)
     return;
   if (!nx)
@@ -613,6 +651,8 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
   if (!ny)
     ny = n;
   bool tc = tensor_core_linears() && status;
+  if (xs && (!tc || !linear_takes_split(l, backward)))
+    throw lapis::Error("linear: a split input needs every path on the tensor cores");
   // Tensor-core paths: paths writing the same output block become one GEMM whose K range
   // concatenates their inputs (segments in path order); the resulting problems go out as
   // grouped launches.  When every path runs on the tensor cores and the blocks tile the
@@ -637,6 +677,13 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
                            : GemmSpec{n, p.in_mul, p.out_mul, p.dim, x + size_t(p.out_offset) * nx,
                                       (long long)nx * p.out_mul, t.bwd, y + size_t(p.in_offset) * ny,
                                       p.in_mul, (long long)ny * p.in_mul, true};
+    if (xs) { // the same elements in the split planes; one exponent per 64 of them
+      size_t off = size_t(backward ? p.out_offset : p.in_offset) * nx;
+      g.Ahi = xs->hi + off;
+      g.Alo = xs->lo + off;
+      g.Aexp = xs->exp + off / 64;
+      g.strideAexp = g.strideA / 64;
+    }
     Problem *same = nullptr;
     for (auto &pr : problems) {
       if (pr.o0 == o0 && pr.o1 == o1 && pr.segs[0].N == g.N && pr.segs[0].batch == g.batch)
@@ -706,10 +753,11 @@ void linear(cudaStream_t s, int n, const Linear &l, const float *x, float *y, bo
 }
 
 void launch_normalize_gate(cudaStream_t s, int n, const float *raw, const float *res, const float *density,
-                           float alpha, float beta, float scalar_scale, float gate_scale, float *gate) {
+                           float alpha, float beta, float scalar_scale, float gate_scale, float *gate,
+                           SplitPlanes gs) {
   if (n)
     lapis::launch(normalize_gate_kernel, blocks_for(size_t(n) * 128, 256), 256, 0, s, n, raw, res, density, alpha, beta,
-                  scalar_scale, gate_scale, gate);
+                  scalar_scale, gate_scale, gate, gs);
 }
 void launch_gate_norm_backward(cudaStream_t s, int n, const float *res, const float *raw, const float *density,
                                const float *gate_grad, float alpha, float beta, float scalar_scale, float gate_scale,
@@ -832,6 +880,40 @@ extern "C" int mace_debug_gemm(int M, int N, int K, int batch, const float *A, c
         TCMatrix m = split(bt.data(), N, K);
         tc_gemm(cudaStream_t(0), M, N, K, batch, A, (long long)M * K, m, C, N, (long long)M * N, accumulate != 0,
                 status);
+      } else if (mode == 4) { // A given as split planes, made here by the host rule
+        if (K % 64)
+          throw lapis::Error("mode 4 needs K a multiple of 64");
+        std::vector<float> ah(size_t(batch) * M * K);
+        lapis::check(cudaMemcpy(ah.data(), A, ah.size() * 4, cudaMemcpyDeviceToHost));
+        std::vector<uint16_t> hi(ah.size()), lo(ah.size());
+        std::vector<int16_t> ex(ah.size() / 64);
+        for (size_t b = 0; b < ex.size(); ++b) {
+          float mx = 0.f;
+          for (int k = 0; k < 64; ++k)
+            mx = std::max(mx, std::fabs(ah[b * 64 + k]));
+          int e = 0;
+          if (mx > 0.f) {
+            int x2 = 0;
+            std::frexp(mx, &x2);
+            e = std::min(100, std::max(-100, 15 - x2));
+          }
+          ex[b] = int16_t(e);
+          for (int k = 0; k < 64; ++k) {
+            float x = std::ldexp(ah[b * 64 + k], e);
+            __half h = __float2half_rn(x), l = __float2half_rn(x - __half2float(h));
+            std::memcpy(&hi[b * 64 + k], &h, 2);
+            std::memcpy(&lo[b * 64 + k], &l, 2);
+          }
+        }
+        auto *hd = static_cast<uint16_t *>(alloc(hi.size() * 2)), *ld = static_cast<uint16_t *>(alloc(lo.size() * 2));
+        auto *xd = static_cast<int16_t *>(alloc(ex.size() * 2));
+        lapis::check(cudaMemcpy(hd, hi.data(), hi.size() * 2, cudaMemcpyHostToDevice));
+        lapis::check(cudaMemcpy(ld, lo.data(), lo.size() * 2, cudaMemcpyHostToDevice));
+        lapis::check(cudaMemcpy(xd, ex.data(), ex.size() * 2, cudaMemcpyHostToDevice));
+        GemmSpec g{M, N, K, batch, A, (long long)M * K, split(bt.data(), N, K), C, N, (long long)M * N,
+                   accumulate != 0};
+        g.Ahi = hd, g.Alo = ld, g.Aexp = xd, g.strideAexp = (long long)M * K / 64;
+        tc_gemm_group(cudaStream_t(0), &g, 1, status);
       } else if (mode == 3) { // K split into two segments with their own contiguous A and B
         int k0 = (K / 64) * 32, k1 = K - k0;
         if (!k0)

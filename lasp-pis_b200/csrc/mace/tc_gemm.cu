@@ -115,15 +115,25 @@ struct TileGrid {
 // their concatenated tile space, so short problems share one pipeline ramp and tail.  A
 // problem's K range may be a concatenation of segments, each with its own A and B (paths
 // that add into the same output block): C = sum_s A_s B_s accumulates inside the tile.
+// A K segment's A operand: fp32 (split in the kernel), or given split (map a over A_hi, alo
+// over A_lo, and the exponents aexp[z * xbatch + row * xrow + slab]).
+struct SplitA {
+  CUtensorMap alo;
+  const int16_t *aexp;
+  long long xbatch;
+  int xrow, presplit;
+};
 struct GemmSegment {
   CUtensorMap a, bhi, blo;
+  SplitA sa;
   int ktiles, eb; // K slabs; B's exponent eB
 };
 struct GemmProblem {
   CUtensorMap a, bhi, blo, c; // first K segment and the output
+  SplitA sa;
   TileGrid tg;
-  int ktiles, kt0, eb, accumulate, tile0; // total K slabs, the first segment's and its eB; first tile
-  int seg0, nseg;                         // further K segments
+  int M, ktiles, kt0, eb, accumulate, tile0; // rows; total K slabs, the first segment's and its eB; first tile
+  int seg0, nseg;                            // further K segments
 };
 struct GemmGroup {
   GemmProblem p[kMaxGemmProblems];
@@ -184,15 +194,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int g = 0, q = 0;
       bool ok = true;
-      auto load = [&](const CUtensorMap *a, const CUtensorMap *bhi, const CUtensorMap *blo, int kt, int n0, int m0,
-                      int z) {
+      auto load = [&](const CUtensorMap *a, const SplitA &sa, const CUtensorMap *bhi, const CUtensorMap *blo, int kt,
+                      int n0, int m0, int z) {
         int s = g % kStages;
         if (g >= kStages && !(ok = mbar_wait(empty0 + 8 * s, ((g / kStages) - 1) & 1, &abort_flag)))
           return;
         unsigned base = smem_u32(smem + s * kStageBytes), full = full0 + 8 * s;
         mbar_expect_tx(full, kStageBytes);
-        tma_load_3d(base, a, kt * kBK, m0, z, full);
-        tma_load_3d(base + kTileBytes, a, kt * kBK + 32, m0, z, full);
+        if (sa.presplit) { // A_hi and A_lo as they will sit after the split
+          tma_load_3d(base, a, kt * kBK, m0, z, full);
+          tma_load_3d(base + kTileBytes, &sa.alo, kt * kBK, m0, z, full);
+        } else { // the two fp32 boxes
+          tma_load_3d(base, a, kt * kBK, m0, z, full);
+          tma_load_3d(base + kTileBytes, a, kt * kBK + 32, m0, z, full);
+        }
         tma_load_2d(base + 2 * kTileBytes, bhi, kt * kBK, n0, full);
         tma_load_2d(base + 3 * kTileBytes, blo, kt * kBK, n0, full);
         ++g;
@@ -202,10 +217,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         int n0, m0, z;
         pr.tg.coords(t - pr.tile0, n0, m0, z);
         for (int kt = 0; kt < pr.kt0 && ok; ++kt)
-          load(&pr.a, &pr.bhi, &pr.blo, kt, n0, m0, z);
+          load(&pr.a, pr.sa, &pr.bhi, &pr.blo, kt, n0, m0, z);
         for (int sg = pr.seg0; sg < pr.seg0 + pr.nseg && ok; ++sg)
           for (int kt = 0; kt < gg.seg[sg].ktiles && ok; ++kt)
-            load(&gg.seg[sg].a, &gg.seg[sg].bhi, &gg.seg[sg].blo, kt, n0, m0, z);
+            load(&gg.seg[sg].a, gg.seg[sg].sa, &gg.seg[sg].bhi, &gg.seg[sg].blo, kt, n0, m0, z);
       }
     }
   } else if (warp == 1) {
@@ -246,13 +261,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int tile = blockIdx.x; tile < gg.tiles && ok; tile += gridDim.x) {
       const GemmProblem &pr = gg.find(tile, q);
-      int sg = pr.seg0 - 1, left = pr.kt0, eb = pr.eb;
+      int n0, m0, z;
+      pr.tg.coords(tile - pr.tile0, n0, m0, z);
+      int sg = pr.seg0 - 1, left = pr.kt0, eb = pr.eb, slabs = pr.kt0;
+      const SplitA *sa = &pr.sa;
       for (int kt = 0; kt < pr.ktiles; ++kt, ++g) {
-        while (!left) { // the slab's K segment and its B exponent
+        while (!left) { // the slab's K segment, its B exponent and its A
           ++sg;
-          left = gg.seg[sg].ktiles;
+          left = slabs = gg.seg[sg].ktiles;
           eb = gg.seg[sg].eb;
+          sa = &gg.seg[sg].sa;
         }
+        int ks = slabs - left; // slab within the segment
         --left;
         int s = g % kStages;
         ok = mbar_wait(full0 + 8 * s, (g / kStages) & 1, &abort_flag);
@@ -262,43 +282,53 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         unsigned char *st = smem + s * kStageBytes;
         int16_t *ex = exps + (g % kExpSlots) * kBM;
+        if (sa->presplit) { // A arrived split: only its exponents, offset by eB
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            int r = t + 64 * h, e = 0;
+            if (m0 + r < pr.M)
+              e = sa->aexp[z * sa->xbatch + (long long)(m0 + r) * sa->xrow + ks];
+            ex[r] = int16_t(min(max(e + eb, -126), 126));
+          }
+        } else {
 #pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
-          int r = t + 64 * h, sw = r & 7;
-          unsigned char *ra = st + r * 128, *rb = st + kTileBytes + r * 128; // row r of each box
-          float v[64];
+          for (int h = 0; h < 2; ++h) {
+            int r = t + 64 * h, sw = r & 7;
+            unsigned char *ra = st + r * 128, *rb = st + kTileBytes + r * 128; // row r of each box
+            float v[64];
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            float4 x = *reinterpret_cast<const float4 *>(ra + ((c ^ sw) << 4));
-            float4 y = *reinterpret_cast<const float4 *>(rb + ((c ^ sw) << 4));
-            v[4 * c] = x.x, v[4 * c + 1] = x.y, v[4 * c + 2] = x.z, v[4 * c + 3] = x.w;
-            v[32 + 4 * c] = y.x, v[33 + 4 * c] = y.y, v[34 + 4 * c] = y.z, v[35 + 4 * c] = y.w;
+            for (int c = 0; c < 8; ++c) {
+              float4 x = *reinterpret_cast<const float4 *>(ra + ((c ^ sw) << 4));
+              float4 y = *reinterpret_cast<const float4 *>(rb + ((c ^ sw) << 4));
+              v[4 * c] = x.x, v[4 * c + 1] = x.y, v[4 * c + 2] = x.z, v[4 * c + 3] = x.w;
+              v[32 + 4 * c] = y.x, v[33 + 4 * c] = y.y, v[34 + 4 * c] = y.z, v[35 + 4 * c] = y.w;
+            }
+            // Row maximum as an 8-way tree (short dependency chains).
+            float mx[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              mx[j] = fabsf(v[j]);
+#pragma unroll
+            for (int k = 8; k < 64; ++k)
+              mx[k & 7] = fmaxf(mx[k & 7], fabsf(v[k]));
+#pragma unroll
+            for (int w = 4; w; w >>= 1)
+#pragma unroll
+              for (int j = 0; j < w; ++j)
+                mx[j] = fmaxf(mx[j], mx[j + w]);
+            int e = row_exponent(mx[0], eb);
+            float2 sc = make_float2(pow2(e), pow2(e));
+            // fp16 chunk c holds elements 8c .. 8c + 7 of the row: A_hi over the first box,
+            // A_lo over the second, at the same swizzled positions.
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              uint4 hi, lo;
+              split8(v + 8 * c, sc, hi, lo);
+              *reinterpret_cast<uint4 *>(ra + ((c ^ sw) << 4)) = hi;
+              *reinterpret_cast<uint4 *>(rb + ((c ^ sw) << 4)) = lo;
+            }
+            ex[r] = int16_t(e + eb);
           }
-          // Row maximum as an 8-way tree (short dependency chains).
-          float mx[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            mx[j] = fabsf(v[j]);
-#pragma unroll
-          for (int k = 8; k < 64; ++k)
-            mx[k & 7] = fmaxf(mx[k & 7], fabsf(v[k]));
-#pragma unroll
-          for (int w = 4; w; w >>= 1)
-#pragma unroll
-            for (int j = 0; j < w; ++j)
-              mx[j] = fmaxf(mx[j], mx[j + w]);
-          int e = row_exponent(mx[0], eb);
-          float2 sc = make_float2(pow2(e), pow2(e));
-          // fp16 chunk c holds elements 8c .. 8c + 7 of the row: A_hi over the first box,
-          // A_lo over the second, at the same swizzled positions.
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint4 hi, lo;
-            split8(v + 8 * c, sc, hi, lo);
-            *reinterpret_cast<uint4 *>(ra + ((c ^ sw) << 4)) = hi;
-            *reinterpret_cast<uint4 *>(rb + ((c ^ sw) << 4)) = lo;
-          }
-          ex[r] = int16_t(e + eb);
         }
         mbar_arrive(xfull0 + 8 * (g % kExpSlots)); // the exponents, for the drain
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -435,6 +465,24 @@ CUtensorMap make_map(const float *base, int cols, int rows, int rank, int batch,
   return map;
 }
 
+// Tensor map over a split A plane [batch][M][K] fp16 (batch stride in elements), box 64 (K) x
+// 128 (rows) x 1, SWIZZLE_128B: the layout the in-kernel split writes.
+CUtensorMap make_map_f16_a(const uint16_t *base, int K, int M, int batch, long long batch_stride) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (K * 2) % 16 || (batch_stride * 2) % 16)
+    throw lapis::Error("tensor-core GEMM split operand is not 16-byte aligned");
+  CUtensorMap map;
+  cuuint64_t dims[3] = {cuuint64_t(K), cuuint64_t(M), cuuint64_t(batch)};
+  cuuint64_t strides[2] = {cuuint64_t(K) * 2, cuuint64_t(batch_stride) * 2};
+  cuuint32_t box[3] = {kBK, kBM, 1};
+  cuuint32_t elem[3] = {1, 1, 1};
+  CUresult r = encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<uint16_t *>(base), dims, strides, box,
+                         elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw lapis::Error("cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+  return map;
+}
+
 // Tensor map over an fp16 B plane [N][K], box 64 (K) x 128 (N), SWIZZLE_128B.
 CUtensorMap make_map_f16(const uint16_t *base, int K, int N) {
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (K * 2) % 16)
@@ -460,6 +508,8 @@ namespace {
 void check_problem(const GemmSpec &g) {
   if (!tc_gemm_supported(g.N, g.K))
     throw lapis::Error("tensor-core GEMM shape unsupported");
+  if (g.Ahi && (g.K % kBK || !g.Alo || !g.Aexp))
+    throw lapis::Error("tensor-core GEMM split operand needs K a multiple of 64, both planes and exponents");
   if ((reinterpret_cast<uintptr_t>(g.C) & 15) || g.ldc % 4 || (g.batch > 1 && g.strideC % 4))
     throw lapis::Error("tensor-core GEMM output is not 16-byte aligned");
 }
@@ -496,16 +546,29 @@ void launch_group(cudaStream_t s, const GemmSpec *specs, int count, int *status)
     }
     GemmProblem &p = gg.p[n - 1];
     // A as [batch][M][K] (always a rank-3 map: the kernel issues 3D loads); B as [N][K].
-    CUtensorMap a = make_map(g.A, g.K, g.M, 3, g.batch, g.batch > 1 ? g.strideA : (long long)g.M * g.K);
+    long long sA = g.batch > 1 ? g.strideA : (long long)g.M * g.K;
+    CUtensorMap a;
+    SplitA sa{};
+    if (g.Ahi) {
+      a = make_map_f16_a(g.Ahi, g.K, g.M, g.batch, sA);
+      sa.alo = make_map_f16_a(g.Alo, g.K, g.M, g.batch, sA);
+      sa.aexp = g.Aexp;
+      sa.xbatch = g.strideAexp;
+      sa.xrow = g.K / kBK;
+      sa.presplit = 1;
+    } else {
+      a = make_map(g.A, g.K, g.M, 3, g.batch, sA);
+    }
     CUtensorMap bhi = make_map_f16(g.B.hi, g.K, g.N), blo = make_map_f16(g.B.lo, g.K, g.N);
     int slabs = (g.K + kBK - 1) / kBK;
     if (!g.join) {
-      p.a = a, p.bhi = bhi, p.blo = blo;
+      p.a = a, p.bhi = bhi, p.blo = blo, p.sa = sa;
+      p.M = g.M;
       p.kt0 = slabs;
       p.eb = g.B.exp;
     } else {
       GemmSegment &sg = gg.seg[ns++];
-      sg.a = a, sg.bhi = bhi, sg.blo = blo;
+      sg.a = a, sg.bhi = bhi, sg.blo = blo, sg.sa = sa;
       sg.ktiles = slabs;
       sg.eb = g.B.exp;
       p.nseg += 1;

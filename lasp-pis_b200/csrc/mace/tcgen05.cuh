@@ -143,5 +143,13 @@ __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.p
 // Wait until the issued bulk copies have read their shared-memory source / fully completed.
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Exponent of one 64-wide slab of a split operand written outside the GEMM: 2^e brings the
+// slab's largest magnitude m into [2^14, 2^15); clamped to [-100, 100] so that the GEMM can
+// add its weights' exponent.
+__device__ __forceinline__ int split_exponent(float m) {
+  int ex = int(__float_as_uint(m) >> 23) & 0xff; // biased exponent (m >= 0)
+  int e = ex ? 141 - ex : (m > 0.f ? 100 : 0);
+  return min(max(e, -100), 100);
+}
 } // namespace tc
 } // namespace mace

@@ -17,11 +17,14 @@ SHAPES = [(1000, 128, 128, 1), (300, 256, 2048, 3), (10000, 512, 512, 1), (130, 
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
-@pytest.mark.parametrize("mode", [0, 1, 2, 3], ids=["simt", "tcgen05", "tcgen05-grouped", "tcgen05-ksegments"])
+@pytest.mark.parametrize("mode", [0, 1, 2, 3, 4],
+                         ids=["simt", "tcgen05", "tcgen05-grouped", "tcgen05-ksegments", "tcgen05-presplit"])
 def test_gemm_matches_fp64(library, shape, mode):
     import torch
     if mode == 3 and shape[2] < 64:
         pytest.skip("K segments need K >= 64")
+    if mode == 4 and shape[2] % 64:
+        pytest.skip("a split operand needs K a multiple of 64")
     lib = ct.CDLL(str(library))
     lib.mace_debug_gemm.argtypes = [ct.c_int] * 4 + [ct.c_void_p] * 3 + [ct.c_int, ct.c_int]
     lib.mace_last_error.restype = ct.c_char_p
@@ -59,7 +62,7 @@ def test_tensor_core_error_close_to_fp32(library):
     assert rms[1] <= 4 * rms[0] + 1e-8, rms
 
 
-@pytest.mark.parametrize("mode", [1, 2, 3], ids=["tcgen05", "tcgen05-grouped", "tcgen05-ksegments"])
+@pytest.mark.parametrize("mode", [1, 2, 3, 4], ids=["tcgen05", "tcgen05-grouped", "tcgen05-ksegments", "tcgen05-presplit"])
 def test_tensor_core_rows_of_any_magnitude(library, mode):
     """Row magnitudes from 1e-25 to 1e25, every 7th row mixing in values 2^-20 smaller, B of
     magnitude 1e-3: the fp16 split scales each row (and B) into fp16's range, so every row
