@@ -25,6 +25,7 @@
 #include "edge_common.cuh"
 #include "model.hpp"
 #include "tcgen05.cuh"
+#include <cuda_fp16.h>
 #include <type_traits>
 
 namespace mace {
@@ -102,6 +103,7 @@ struct ProjArgs {
   const float *up, *bias;
   const float *msg_grad, *rho_grad; // backward inputs
   float *msg, *rho;                 // forward outputs
+  SplitPlanes msg_split;            // forward: msg as the tensor-core linear_1's split operand
   float *ug_edge;                   // backward, layer 1: per-edge up-gradient rows [e - e_base][IN][128]
   float4 *edge_force;               // backward output
   int *status;
@@ -431,9 +433,33 @@ __global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBl
   }
   if constexpr (!Bwd) {
     if (ok) {
+      if (a.msg_split.hi) {
+        // A warp's 64 channels are one 64-wide slab of each message row: its maximum by
+        // shuffles, then the fp16 hi / lo pair of each channel.
+        static_assert(W == 2, "the split message write assumes two channels per thread");
 #pragma unroll
-      for (int k = 0; k < NC; ++k)
-        reinterpret_cast<V *>(a.msg)[(size_t(k) * a.n + i) * CS + c] = acc[k];
+        for (int k = 0; k < NC; ++k) {
+          float2 v = acc[k];
+          float m = fmaxf(fabsf(v.x), fabsf(v.y));
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1)
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          int e = tc::split_exponent(m);
+          float sc = __uint_as_float(uint32_t(127 + e) << 23);
+          float2 x = __fmul2_rn(v, make_float2(sc, sc));
+          __half2 h = __float22half2_rn(x);
+          __half2 l = __float22half2_rn(__ffma2_rn(__half22float2(h), make_float2(-1.f, -1.f), x));
+          size_t el = (size_t(k) * a.n + i) * 128 + 2 * c;
+          *reinterpret_cast<__half2 *>(a.msg_split.hi + el) = h;
+          *reinterpret_cast<__half2 *>(a.msg_split.lo + el) = l;
+          if (lane == 0)
+            a.msg_split.exp[el / 64] = int16_t(e);
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < NC; ++k)
+          reinterpret_cast<V *>(a.msg)[(size_t(k) * a.n + i) * CS + c] = acc[k];
+      }
       if (c == 0)
         a.rho[i] = rsum;
     }
@@ -484,13 +510,14 @@ ProjArgs proj_args(const DeviceGeometry &g, const Layer &l, EdgeArrays ea, Radia
 
 void launch_message_forward_proj(cudaStream_t s, int layer, const DeviceGeometry &g, const Layer &l, EdgeArrays ea,
                                  RadialOut ro, const ProjectionChunk &k, const float *R, const float *up,
-                                 float *message, float *density, int n_up) {
+                                 float *message, float *density, int n_up, SplitPlanes message_split) {
   int blocks = k.r1 - k.r0;
   if (blocks <= 0)
     return;
   ProjArgs a = proj_args(g, l, ea, ro, k, R, up, n_up);
   a.msg = message;
   a.rho = density;
+  a.msg_split = message_split;
   if (layer == 0)
     launch_proj<0, false, false>(s, blocks, a, l.tp);
   else

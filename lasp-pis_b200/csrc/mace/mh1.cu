@@ -295,6 +295,14 @@ std::vector<Result> MH1::compute(bool batch) {
     linear(s, n, l.skip, input, hidden[k], false, false, status, in_rows);
     launch_radial(s, c.geometry, l, pair, ea, ro[k], projection);
     timer.mark("forward" + std::to_string(k) + ".linears/radial");
+    // The messages feed only linear_1: on the projection path and the tensor cores they are
+    // written as the GEMM's split operand.
+    SplitPlanes ms;
+    if (projection && status && linear_takes_split(l.one, false)) {
+      ms.hi = reinterpret_cast<uint16_t *>(msg);
+      ms.lo = ms.hi + size_t(n) * 5120;
+      ms.exp = c.array<int16_t>("mh.t.msg.exp", size_t(n) * 80);
+    }
     if (projection) {
       for (auto &q : chunks) {
         // (cut h) W per edge row and path channel; the edge kernel adds cut b.
@@ -303,13 +311,13 @@ std::vector<Result> MH1::compute(bool batch) {
         timer.mark("forward" + std::to_string(k) + ".projection");
         if (dom && k == 1 && &q == &chunks.front())
           dom->join(c); // the ghosts' up-projected features have arrived
-        launch_message_forward_proj(s, k, c.geometry, l, ea, ro[k], q, proj[k], up[k], msg, rho[k], ns);
+        launch_message_forward_proj(s, k, c.geometry, l, ea, ro[k], q, proj[k], up[k], msg, rho[k], ns, ms);
         timer.mark("forward" + std::to_string(k) + ".messages");
       }
     } else
       launch_message_forward(s, k, c.geometry, l, ea, ro[k], up[k], msg, rho[k]);
     timer.mark("forward" + std::to_string(k) + ".messages");
-    linear(s, n, l.one, msg, raw[k], false, false, status);
+    linear(s, n, l.one, msg, raw[k], false, false, status, 0, 0, ms.hi ? &ms : nullptr);
     // The gate feeds only linear_2: on the tensor cores it is written as the GEMM's split
     // operand (the same bytes as fp32, plus one exponent per 64 values), so the GEMM skips
     // its own split.
@@ -368,9 +376,16 @@ std::vector<Result> MH1::compute(bool batch) {
     launch_product_backward(s, n, l, pin[k], pgrad, pingrad);
     linear(s, n, l.two, pingrad, gategrad, true, false, status);
     float *pregrad = res[k]; // written in place over res[k]
+    // rawgrad feeds only the linear_1 backward: on the tensor cores it is written split.
+    SplitPlanes rs;
+    if (status && linear_takes_split(l.one, true)) {
+      rs.hi = reinterpret_cast<uint16_t *>(rawgrad);
+      rs.lo = rs.hi + size_t(n) * 9728;
+      rs.exp = c.array<int16_t>("mh.b.raw.exp", size_t(n) * 152);
+    }
     launch_gate_norm_backward(s, n, res[k], raw[k], rho[k], gategrad, l.alpha, l.beta, cst[11], cst[12], pregrad,
-                              rawgrad, rhograd);
-    linear(s, n, l.one, rawgrad, msggrad, true, false, status);
+                              rawgrad, rhograd, rs);
+    linear(s, n, l.one, rawgrad, msggrad, true, false, status, 0, 0, rs.hi ? &rs : nullptr);
     if (k == 1) {
       if (dom) { // ghost rows collect the edge kernels' up-gradients for their owners
         c.clear(upgrad, size_t(ns) * 512 * sizeof(float));

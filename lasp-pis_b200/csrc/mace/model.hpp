@@ -143,10 +143,11 @@ struct ProjectionChunk {
   int r0, r1;
   long long e0, e1;
 };
-// n_up: row stride of up / up_grad (senders; 0: the receiver count g.n).
+// n_up: row stride of up / up_grad (senders; 0: the receiver count g.n).  message_split set:
+// the messages go out as SplitPlanes (the tensor-core linear_1's input) instead of fp32.
 void launch_message_forward_proj(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &, EdgeArrays,
                                  RadialOut, const ProjectionChunk &, const float *R, const float *up,
-                                 float *message, float *density, int n_up = 0);
+                                 float *message, float *density, int n_up = 0, SplitPlanes message_split = {});
 // ug_edge (layer 1): the chunk's per-edge up-projection gradients, row e - e0 of [rows][4][128].
 void launch_message_backward_proj(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &,
                                   EdgeArrays, RadialOut, const ProjectionChunk &, const float *R, const float *dR,
@@ -225,9 +226,11 @@ bool projection_edges();
 void launch_normalize_gate(cudaStream_t, int n, const float *raw, const float *res, const float *density,
                            float alpha, float beta, float scalar_scale, float gate_scale, float *gate,
                            SplitPlanes gs = {});
+// raw_grad_split set: raw_grad goes out as SplitPlanes (the tensor-core linear_1 backward's input).
 void launch_gate_norm_backward(cudaStream_t, int n, const float *res, const float *raw, const float *density,
                                const float *gate_grad, float alpha, float beta, float scalar_scale,
-                               float gate_scale, float *pre_grad, float *raw_grad, float *density_grad);
+                               float gate_scale, float *pre_grad, float *raw_grad, float *density_grad,
+                               SplitPlanes raw_grad_split = {});
 void launch_product(cudaStream_t, int n, const Layer &, const float *x, float *y);
 void launch_product_backward(cudaStream_t, int n, const Layer &, const float *x, const float *grad, float *xg);
 void launch_add(cudaStream_t, size_t count, const float *a, float *b, float scale);

@@ -269,9 +269,9 @@ __global__ void normalize_gate_kernel(int n, const float *raw, const float *res,
 __global__ void __launch_bounds__(512, 2) gate_norm_backward_kernel(int n, const float *res, const float *raw,
                                                                  const float *rho, const float *gg, float alpha,
                                                                  float beta, float cs, float cgt, float *pg,
-                                                                 float *rg, float *rho_grad) {
+                                                                 float *rg, float *rho_grad, SplitPlanes rgs) {
   __shared__ float red[4][4];
-  int t = threadIdx.x, slot = t >> 7, c = (t & 127) * 4, i = blockIdx.x * 4 + slot;
+  int t = threadIdx.x, slot = t >> 7, c = (t & 127) * 4, i = blockIdx.x * 4 + slot, lane = t & 31;
   float s = 0.f;
   if (i < n) {
     float den = alpha + beta * rho[i];
@@ -289,7 +289,7 @@ __global__ void __launch_bounds__(512, 2) gate_norm_backward_kernel(int n, const
       ro[j] = g0 / den;
     }
     st4(pg, k0, o);
-    st4(rg, k0, ro);
+    put4(rg, rgs, k0, ro, lane);
 #pragma unroll
     for (int l = 1; l <= 3; ++l) {
       size_t gi = size_t(i) * 2048 + l * 512 + c;
@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(512, 2) gate_norm_backward_kernel(int n, const
           ro[j] = v / den;
         }
         st4(pg, src, o);
-        st4(rg, src, ro);
+        put4(rg, rgs, src, ro, lane);
       }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -324,7 +324,7 @@ __global__ void __launch_bounds__(512, 2) gate_norm_backward_kernel(int n, const
         ro[j] = dg[j] / den;
       }
       st4(pg, gi, o);
-      st4(rg, gi, ro);
+      put4(rg, rgs, gi, ro, lane);
     }
   }
 #pragma unroll
@@ -761,10 +761,10 @@ void launch_normalize_gate(cudaStream_t s, int n, const float *raw, const float 
 }
 void launch_gate_norm_backward(cudaStream_t s, int n, const float *res, const float *raw, const float *density,
                                const float *gate_grad, float alpha, float beta, float scalar_scale, float gate_scale,
-                               float *pre_grad, float *raw_grad, float *density_grad) {
+                               float *pre_grad, float *raw_grad, float *density_grad, SplitPlanes raw_grad_split) {
   if (n)
     lapis::launch(gate_norm_backward_kernel, (n + 3) / 4, 512, 0, s, n, res, raw, density, gate_grad, alpha, beta,
-                  scalar_scale, gate_scale, pre_grad, raw_grad, density_grad);
+                  scalar_scale, gate_scale, pre_grad, raw_grad, density_grad, raw_grad_split);
 }
 size_t product_smem(int count, bool backward) {
   return (size_t(count) * 32 + ((count + 3) & ~3)) * 4 + size_t(kProdWarps) * (backward ? 2 : 1) * kProdV * 32 * 4;
