@@ -3,7 +3,10 @@
 //   C[z] (+)= A[z] * B      A: [M][K] fp32 row-major per batch z (node or edge features),
 //                           B: given as two K-major fp16 planes Bhi/Blo [N][K] with
 //                              B 2^eB = Bhi + Blo (split once at model load, split_f16).
-// Each 128-row x 64-wide K slab of A is split in shared memory the same way, per row: with
+// A may also arrive already split (GemmSpec::Ahi / Alo / Aexp, written by the kernel that
+// produces it): the two fp16 planes are then loaded by TMA where the split would write them,
+// and only the row exponents are read.  Otherwise each 128-row x 64-wide K slab of A is
+// split in shared memory the same way, per row: with
 // 2^e the power of two that brings the row's largest |a| into [2^14, 2^15),
 // a 2^e = A_hi + A_lo, A_hi = round_fp16(a 2^e), A_lo = round_fp16(a 2^e - A_hi) (the
 // remainder is exact in fp32).  Each pair carries 22 significant bits, and the scaling keeps
