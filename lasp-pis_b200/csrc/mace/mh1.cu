@@ -373,8 +373,17 @@ std::vector<Result> MH1::compute(bool batch) {
     if (k == 0)
       linear(s, n, m.read0, one, hgrad, true, true, status);
     linear(s, n, l.plin, hgrad, pgrad, true, false, status);
-    launch_product_backward(s, n, l, pin[k], pgrad, pingrad);
-    linear(s, n, l.two, pingrad, gategrad, true, false, status);
+    // pingrad feeds only the linear_2 backward: on the tensor cores (compiled product tables)
+    // layer 1's is written split.  Layer 0's is not: its 410-term table at 64 channels per
+    // CTA made the product backward 0.1 ms slower than the GEMM gained (same-box A/B at C3).
+    SplitPlanes ps;
+    if (k == 1 && status && l.poly_fixed >= 0 && linear_takes_split(l.two, true)) {
+      ps.hi = reinterpret_cast<uint16_t *>(pingrad);
+      ps.lo = ps.hi + size_t(n) * 8192;
+      ps.exp = c.array<int16_t>("mh.b.pin.exp", size_t(n) * 128);
+    }
+    launch_product_backward(s, n, l, pin[k], pgrad, pingrad, ps);
+    linear(s, n, l.two, pingrad, gategrad, true, false, status, 0, 0, ps.hi ? &ps : nullptr);
     float *pregrad = res[k]; // written in place over res[k]
     // rawgrad feeds only the linear_1 backward: on the tensor cores it is written split.
     SplitPlanes rs;

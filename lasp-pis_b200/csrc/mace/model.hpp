@@ -232,7 +232,10 @@ void launch_gate_norm_backward(cudaStream_t, int n, const float *res, const floa
                                float gate_scale, float *pre_grad, float *raw_grad, float *density_grad,
                                SplitPlanes raw_grad_split = {});
 void launch_product(cudaStream_t, int n, const Layer &, const float *x, float *y);
-void launch_product_backward(cudaStream_t, int n, const Layer &, const float *x, const float *grad, float *xg);
+// xgs set (compiled MH1 tables only): the input gradient goes out as SplitPlanes (the
+// tensor-core linear_2 backward's input) instead of fp32.
+void launch_product_backward(cudaStream_t, int n, const Layer &, const float *x, const float *grad, float *xg,
+                             SplitPlanes xgs = {});
 void launch_add(cudaStream_t, size_t count, const float *a, float *b, float scale);
 void launch_fill(cudaStream_t, size_t count, float *a, float value);
 void launch_readout_act(cudaStream_t, int count, const float *x, const float *grad, float *y, float scale,

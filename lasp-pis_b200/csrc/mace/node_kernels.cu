@@ -505,20 +505,27 @@ template <int L> constexpr bool poly_groups_contiguous() {
 }
 static_assert(poly_groups_contiguous<0>() && poly_groups_contiguous<1>(), "product terms must be (a, b, c)-sorted");
 
-template <int L, bool Bwd>
+// Split (backward only): the input gradient goes out as SplitPlanes.  A CTA then covers 64
+// channels -- one 64-wide slab of each row -- as two halves of 32, each taken by half of the
+// warps; the two warps of a node pair exchange their 32-channel maxima through shared memory.
+template <int L, bool Bwd, bool Split = false>
 __global__ void __launch_bounds__(32 * kPolyWarps, Bwd || L == 0 ? 2 : 3)
-    product_fixed_kernel(int n, const float *coef, const float *x, const float *grad, float *y) {
+    product_fixed_kernel(int n, const float *coef, const float *x, const float *grad, float *y, SplitPlanes ys) {
   // The thread's two nodes travel as float2 pairs, so every FMA and product below is one paired
   // instruction (fma.rn.f32x2 / mul.rn.f32x2: two IEEE operations).
   static_assert(kPolyPair == 2, "paired evaluation assumes two nodes per thread");
+  static_assert(!Split || Bwd, "only the backward writes a split output");
   using PT = PolyTable<L>;
-  extern __shared__ float cs[]; // [NT][32]
-  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, c0 = blockIdx.x * 32;
-  for (int k = threadIdx.x; k < PT::NT * 32; k += blockDim.x)
-    cs[k] = coef[size_t(k >> 5) * 512 + c0 + (k & 31)];
+  constexpr int kCh = Split ? 64 : 32, kSlots = Split ? kPolyWarps / 2 : kPolyWarps; // channels; warps per half
+  extern __shared__ float cs[]; // [NT][kCh]
+  __shared__ float xch[Split ? 2 : 1][kSlots][2][16][2]; // [buffer][slot][half][component][node]: maxima
+  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, half = warp / kSlots, slot = warp % kSlots;
+  int cb = blockIdx.x * kCh, c0 = cb + 32 * half; // the CTA's first channel; this warp's
+  for (int k = threadIdx.x; k < PT::NT * kCh; k += blockDim.x)
+    cs[k] = coef[size_t(k / kCh) * 512 + cb + (k % kCh)];
   __syncthreads();
-  int i0 = blockIdx.y * kProdNodes, i1 = min(n, i0 + kProdNodes);
-  for (int ib = i0 + warp * kPolyPair; ib < i1; ib += kPolyWarps * kPolyPair) {
+  int i0 = blockIdx.y * kProdNodes, i1 = min(n, i0 + kProdNodes), it = 0;
+  for (int ib = i0 + slot * kPolyPair; ib < i1; ib += kSlots * kPolyPair, ++it) {
     bool second = ib + 1 < i1;
     float2 v[17];
 #pragma unroll
@@ -534,7 +541,7 @@ __global__ void __launch_bounds__(32 * kPolyWarps, Bwd || L == 0 ? 2 : 3)
           constexpr int k = decltype(kc)::value;
           constexpr PolyABC t = PT::term(k);
           constexpr int ab0 = ab_head<L>(o, k), a0 = a_head<L>(o, k);
-          float cf = cs[k * 32 + lane];
+          float cf = cs[k * kCh + 32 * half + lane];
           float2 cf2 = make_float2(cf, cf);
           S = k == ab0 ? __fmul2_rn(cf2, v[t.c]) : __ffma2_rn(cf2, v[t.c], S);
           if constexpr (ab_end<L>(o, k))
@@ -560,7 +567,7 @@ __global__ void __launch_bounds__(32 * kPolyWarps, Bwd || L == 0 ? 2 : 3)
           constexpr int k = decltype(kc)::value;
           constexpr PolyABC t = PT::term(k);
           constexpr int ab0 = ab_head<L>(o, k), a0 = a_head<L>(o, k);
-          float cf = cs[k * 32 + lane];
+          float cf = cs[k * kCh + 32 * half + lane];
           float2 cf2 = make_float2(cf, cf);
           if constexpr (k == a0)
             Gva = __fmul2_rn(G, v[t.a]);
@@ -576,11 +583,48 @@ __global__ void __launch_bounds__(32 * kPolyWarps, Bwd || L == 0 ? 2 : 3)
             g[t.a] = __ffma2_rn(G, T, g[t.a]);
         });
       });
+      if constexpr (Split) {
+        float(*mx)[2][16][2] = xch[it & 1]; // [slot][half][component][node]
 #pragma unroll
-      for (int m = 0; m < 16; ++m) {
-        y[(size_t(m) * n + ib) * 512 + c0 + lane] = g[m].x;
-        if (second)
-          y[(size_t(m) * n + ib + 1) * 512 + c0 + lane] = g[m].y;
+        for (int m = 0; m < 16; ++m) {
+          float a = fabsf(g[m].x), b = fabsf(g[m].y);
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+            b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, o));
+          }
+          if (lane == 0)
+            mx[slot][half][m][0] = a, mx[slot][half][m][1] = b;
+        }
+        // The two warps of this node pair (one per half) meet here, once per iteration; the
+        // maxima are double-buffered, so the next iteration's writes cannot race these reads.
+        static_assert(kSlots == 2, "one named barrier per node-pair slot");
+        if (slot == 0)
+          asm volatile("bar.sync 1, 64;" ::: "memory");
+        else
+          asm volatile("bar.sync 2, 64;" ::: "memory");
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            if (q && !second)
+              continue;
+            int e = tc::split_exponent(fmaxf(mx[slot][0][m][q], mx[slot][1][m][q]));
+            float x2 = (q ? g[m].y : g[m].x) * __uint_as_float(uint32_t(127 + e) << 23);
+            __half h = __float2half_rn(x2), l = __float2half_rn(x2 - __half2float(h));
+            size_t el = (size_t(m) * n + ib + q) * 512 + c0 + lane;
+            ys.hi[el] = __half_as_ushort(h);
+            ys.lo[el] = __half_as_ushort(l);
+            if (half == 0 && lane == 0)
+              ys.exp[el / 64] = int16_t(e);
+          }
+      } else {
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+          y[(size_t(m) * n + ib) * 512 + c0 + lane] = g[m].x;
+          if (second)
+            y[(size_t(m) * n + ib + 1) * 512 + c0 + lane] = g[m].y;
+        }
       }
     }
   }
@@ -770,12 +814,15 @@ size_t product_smem(int count, bool backward) {
   return (size_t(count) * 32 + ((count + 3) & ~3)) * 4 + size_t(kProdWarps) * (backward ? 2 : 1) * kProdV * 32 * 4;
 }
 
-template <int L, bool Bwd>
-void launch_product_fixed(cudaStream_t s, int n, const Layer &l, const float *x, const float *grad, float *y) {
-  int smem = PolyTable<L>::NT * 32 * 4;
-  lapis::check(cudaFuncSetAttribute(product_fixed_kernel<L, Bwd>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  dim3 grid(16, (n + kProdNodes - 1) / kProdNodes);
-  lapis::launch(product_fixed_kernel<L, Bwd>, grid, 32 * kPolyWarps, smem, s, n, l.poly_coef_sorted, x, grad, y);
+template <int L, bool Bwd, bool Split = false>
+void launch_product_fixed(cudaStream_t s, int n, const Layer &l, const float *x, const float *grad, float *y,
+                          SplitPlanes ys = {}) {
+  constexpr int kCh = Split ? 64 : 32;
+  int smem = PolyTable<L>::NT * kCh * 4;
+  auto kernel = product_fixed_kernel<L, Bwd, Split>;
+  lapis::check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  dim3 grid(512 / kCh, (n + kProdNodes - 1) / kProdNodes);
+  lapis::launch(kernel, grid, 32 * kPolyWarps, smem, s, n, l.poly_coef_sorted, x, grad, y, ys);
 }
 
 void launch_product(cudaStream_t s, int n, const Layer &l, const float *x, float *y) {
@@ -794,14 +841,23 @@ void launch_product(cudaStream_t s, int n, const Layer &l, const float *x, float
   lapis::launch(product_kernel, grid, 256, smem, s, n, l.poly_abc, l.poly_coef_sorted, l.npoly, l.poly_out_start,
                 l.pouts, x, y);
 }
-void launch_product_backward(cudaStream_t s, int n, const Layer &l, const float *x, const float *grad, float *xg) {
+void launch_product_backward(cudaStream_t s, int n, const Layer &l, const float *x, const float *grad, float *xg,
+                             SplitPlanes xgs) {
   if (!n)
     return;
+  if (xgs.hi && l.poly_fixed < 0)
+    throw lapis::Error("a split product gradient needs the compiled product tables");
   if (l.poly_fixed >= 0) {
-    if (l.poly_fixed == 0)
+    if (xgs.hi) {
+      if (l.poly_fixed == 0)
+        launch_product_fixed<0, true, true>(s, n, l, x, grad, xg, xgs);
+      else
+        launch_product_fixed<1, true, true>(s, n, l, x, grad, xg, xgs);
+    } else if (l.poly_fixed == 0) {
       launch_product_fixed<0, true>(s, n, l, x, grad, xg);
-    else
+    } else {
       launch_product_fixed<1, true>(s, n, l, x, grad, xg);
+    }
     return;
   }
   size_t smem = product_smem(l.npoly, true);
