@@ -440,10 +440,9 @@ __global__ void __launch_bounds__(Lanes<L, Bwd>::kThreads, Lanes<L, Bwd>::kMinBl
 #pragma unroll
         for (int k = 0; k < NC; ++k) {
           float2 v = acc[k];
-          float m = fmaxf(fabsf(v.x), fabsf(v.y));
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1)
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          // Warp maximum as an integer reduction of |v|'s bit patterns (ordered like the values).
+          float m = __uint_as_float(
+              __reduce_max_sync(0xffffffffu, __float_as_uint(fmaxf(fabsf(v.x), fabsf(v.y)))));
           int e = tc::split_exponent(m);
           float sc = __uint_as_float(uint32_t(127 + e) << 23);
           float2 x = __fmul2_rn(v, make_float2(sc, sc));

@@ -585,16 +585,14 @@ __global__ void __launch_bounds__(32 * kPolyWarps, Bwd || L == 0 ? 2 : 3)
       });
       if constexpr (Split) {
         float(*mx)[2][16][2] = xch[it & 1]; // [slot][half][component][node]
+        // Warp maxima of |g| as integer reductions of the bit patterns (ordered like the values
+        // for non-negative floats).
 #pragma unroll
         for (int m = 0; m < 16; ++m) {
-          float a = fabsf(g[m].x), b = fabsf(g[m].y);
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-            b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, o));
-          }
+          unsigned a = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(g[m].x)));
+          unsigned b = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(g[m].y)));
           if (lane == 0)
-            mx[slot][half][m][0] = a, mx[slot][half][m][1] = b;
+            mx[slot][half][m][0] = __uint_as_float(a), mx[slot][half][m][1] = __uint_as_float(b);
         }
         // The two warps of this node pair (one per half) meet here, once per iteration; the
         // maxima are double-buffered, so the next iteration's writes cannot race these reads.
