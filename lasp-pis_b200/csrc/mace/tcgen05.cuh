@@ -145,7 +145,8 @@ __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.w
 __device__ __forceinline__ void bulk_wait() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // Exponent of one 64-wide slab of a split operand written outside the GEMM: 2^e brings the
 // slab's largest magnitude m into [2^14, 2^15); clamped to [-100, 100] so that the GEMM can
-// add its weights' exponent.
+// add its weights' exponent eB (any |eB| <= 26, weights of largest magnitude 2^-12 to 2^40,
+// keeps the sum inside the normal float range).
 __device__ __forceinline__ int split_exponent(float m) {
   int ex = int(__float_as_uint(m) >> 23) & 0xff; // biased exponent (m >= 0)
   int e = ex ? 141 - ex : (m > 0.f ? 100 : 0);
