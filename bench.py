@@ -30,6 +30,7 @@ e2e    the reference-facing C ABI (mace_calculate) with host buffers: the host-t
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import subprocess
@@ -97,24 +98,34 @@ def linear_flops(archive_path, name: str, nodes: int) -> float:
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running.
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    mark_start() / mark_end() bracket the timed region; summary() then keeps the samples
+    taken within one sampling period of it (the GPU is busy with the warm-up right before and
+    the profiled calls right after), so a timed region shorter than the period still gets its
+    samples.  Without marks every sample counts."""
+
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_S = 0.2
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
         self.lines: list[str] = []
+        self.start = self.end = None
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", str(int(self.PERIOD_S * 1000))],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            deadline = time.time() + 5.0  # the first sample, so the timed region is covered
+            while not self.lines and time.time() < deadline and self.proc.poll() is None:
+                time.sleep(0.01)
         except OSError:
             self.proc = None
         return self
@@ -122,6 +133,13 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+
+    def mark_start(self):
+        self.start = time.time()
+
+    def mark_end(self):
+        self.end = time.time()
+        time.sleep(self.PERIOD_S * 1.5)  # the sample that follows the region
 
     def __exit__(self, *args):
         if self.proc:
@@ -132,14 +150,18 @@ class ClockSampler:
         sm, mx, reasons = [], None, set()
         for line in self.lines:
             f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
+            if len(f) < 10:
                 continue
             try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
+                t = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                clock, clock_max = float(f[2]), float(f[3])
             except ValueError:
                 continue
-            for name, flag in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), f[5:9]):
+            if self.start is not None and not (self.start - self.PERIOD_S <= t <= (self.end or t) + self.PERIOD_S):
+                continue
+            sm.append(clock)
+            mx = clock_max
+            for name, flag in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), f[6:10]):
                 if flag.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
@@ -555,10 +577,14 @@ def main():
 
     device_call = lambda: model.calculate_device(n, xyz_d.data_ptr(), z_d.data_ptr(), s.cell)
     with ClockSampler(ranks.local) as clocks:
+        for _ in range(2):  # keeps the GPU busy while the sampler starts
+            device_call()
         ranks.barrier()
+        clocks.mark_start()
         dev_times, _, graph_modes = timed(device_call, args.steps)
         ranks.barrier()
         e2e_times, _, _ = timed(lambda: model.calculate(xyz_h_np, z_h_np, s.cell), args.steps)
+        clocks.mark_end()
         ranks.barrier()
         # Per-stage CUDA events (the roofline kernels' times) from separate, untimed calls:
         # profiling records events between the stages and runs the kernels directly.

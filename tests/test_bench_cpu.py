@@ -52,16 +52,24 @@ def test_workload_config_is_shared(bench):
 
 def test_clock_summary(bench):
     sampler = bench.ClockSampler(0)
+    t0 = "2026/12/02 10:00:00"
     sampler.lines = [
-        "0, 1965, 1965, 700.1, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active",
-        "0, 1890, 1965, 998.7, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
-        "0, 1900, 1965, 990.0, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
+        t0 + ".000, 0, 1965, 1965, 700.1, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active",
+        t0 + ".200, 0, 1890, 1965, 998.7, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
+        t0 + ".400, 0, 1900, 1965, 990.0, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
         "garbage",
-        "0, [N/A], 1965, 0, 0x0, Not Active, Not Active, Not Active, Not Active",
+        t0 + ".600, 0, [N/A], 1965, 0, 0x0, Not Active, Not Active, Not Active, Not Active",
     ]
     s = sampler.summary()
     assert s == {"sm_mhz": 1900.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"], "samples": 3}
-    sampler.lines = ["0, 1200, 1965, 500, 0x8, Active, Not Active, Active, Not Active"]
+    # A marked region keeps the samples within one period (0.2 s) of it.
+    base = bench.datetime.datetime.strptime(t0 + ".000", "%Y/%m/%d %H:%M:%S.%f").timestamp()
+    sampler.start, sampler.end = base + 0.45, base + 0.46  # window [0.25, 0.66]: the .400 sample
+    assert sampler.summary() == {"sm_mhz": 1900.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"], "samples": 1}
+    sampler.start, sampler.end = base + 0.05, base + 0.10  # window [-0.15, 0.30]: .000 and .200
+    assert sampler.summary()["samples"] == 2
+    sampler = bench.ClockSampler(0)
+    sampler.lines = [t0 + ".000, 0, 1200, 1965, 500, 0x8, Active, Not Active, Active, Not Active"]
     assert sampler.summary()["reasons"] == ["hw_slowdown", "sw_thermal_slowdown"]
     assert bench.ClockSampler(0).summary() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
 
