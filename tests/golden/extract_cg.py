@@ -2,7 +2,7 @@
 (mace/src/cg.inc) into tests/golden/cg_e3nn044.txt, one "l1 l2 lo a b c value" row per
 line.  Run once where the reference tree is available:
 
-    python tests/golden/extract_cg.py /root/reference/mace/src/cg.inc
+    python tests/golden/extract_cg.py <reference tree>/mace/src/cg.inc
 """
 import re
 import sys
