@@ -277,6 +277,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         int ks = slabs - left; // slab within the segment
         --left;
+        // A split operand's exponents come from global memory: load them before waiting for the
+        // slab, so the load overlaps the wait.
+        int pe[2] = {0, 0};
+        if (sa->presplit) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            if (m0 + t + 64 * h < pr.M)
+              pe[h] = sa->aexp[z * sa->xbatch + (long long)(m0 + t + 64 * h) * sa->xrow + ks];
+        }
         int s = g % kStages;
         ok = mbar_wait(full0 + 8 * s, (g / kStages) & 1, &abort_flag);
         if (!__all_sync(0xffffffffu, ok)) {
@@ -287,12 +296,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         int16_t *ex = exps + (g % kExpSlots) * kBM;
         if (sa->presplit) { // A arrived split: only its exponents, offset by eB
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            int r = t + 64 * h, e = 0;
-            if (m0 + r < pr.M)
-              e = sa->aexp[z * sa->xbatch + (long long)(m0 + r) * sa->xrow + ks];
-            ex[r] = int16_t(min(max(e + eb, -126), 126));
-          }
+          for (int h = 0; h < 2; ++h)
+            ex[t + 64 * h] = int16_t(min(max(pe[h] + eb, -126), 126));
         } else {
 #pragma unroll 1
           for (int h = 0; h < 2; ++h) {
