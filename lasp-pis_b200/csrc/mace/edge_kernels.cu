@@ -261,8 +261,15 @@ __device__ __forceinline__ void tile_store(float *rows, const float (&a)[4][8], 
 
 // scaled: write cut h and cut dh + dcut h (the projection GEMM then yields w and its r-derivative
 // directly); otherwise h and dh.
-__global__ void __launch_bounds__(kRadialThreads, 1) radial_kernel(long long E, RadialParams R, const int *pair,
-                                                                EdgeArrays ea, RadialOut ro, int scaled) {
+// One grid row (blockIdx.y) per layer: the layers' radial MLPs depend on the geometry only.
+struct RadialLayers {
+  RadialParams p[2];
+  RadialOut o[2];
+};
+__global__ void __launch_bounds__(kRadialThreads, 1) radial_kernel(long long E, const __grid_constant__ RadialLayers RL,
+                                                                const int *pair, EdgeArrays ea, int scaled) {
+  const RadialParams &R = RL.p[blockIdx.y];
+  const RadialOut &ro = RL.o[blockIdx.y];
   extern __shared__ __align__(16) float sm[];
   float *c_in = sm, *d_in = c_in + kRadialIn, *c_w = d_in + kRadialIn, *vecs = c_w + 2 * kRadialW;
   float *c_b = vecs, *c_g = vecs + 3 * kRadialPerm, *c_bt = vecs + 6 * kRadialPerm;
@@ -736,17 +743,23 @@ void launch_edge_geometry(cudaStream_t s, const DeviceGeometry &g, const int *sp
                   species, constants, radii, bessel, ea, pair);
 }
 
-void launch_radial(cudaStream_t s, const DeviceGeometry &g, const Layer &l, const int *pair, EdgeArrays ea,
-                   RadialOut ro, bool scaled) {
+void launch_radial(cudaStream_t s, const DeviceGeometry &g, const Layer *const *layers, const RadialOut *ro,
+                   int count, const int *pair, EdgeArrays ea, bool scaled) {
   long long E = g.edge_capacity;
-  if (!E)
+  if (!E || count < 1)
     return;
+  if (count > 2)
+    throw lapis::Error("launch_radial: at most two layers per launch");
   size_t smem = kRadialSmemFloats * sizeof(float);
   lapis::check(cudaFuncSetAttribute(radial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  RadialLayers rl{};
+  for (int k = 0; k < count; ++k) {
+    rl.p[k] = RadialParams{layers[k]->radial, layers[k]->density};
+    rl.o[k] = ro[k];
+  }
   long long tiles = (E + kRadialEdges - 1) / kRadialEdges;
-  int blocks = int(std::min<long long>(tiles, 148 * 2));
-  lapis::launch(radial_kernel, blocks, kRadialThreads, smem, s, E, RadialParams{l.radial, l.density}, pair, ea, ro,
-                int(scaled));
+  dim3 grid(unsigned(std::min<long long>(tiles, 148 * 2 / count)), unsigned(count));
+  lapis::launch(radial_kernel, grid, kRadialThreads, smem, s, E, rl, pair, ea, int(scaled));
 }
 
 void launch_message_forward(cudaStream_t s, int layer, const DeviceGeometry &g, const Layer &l, EdgeArrays ea,

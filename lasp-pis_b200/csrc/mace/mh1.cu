@@ -268,6 +268,16 @@ std::vector<Result> MH1::compute(bool batch) {
   float *msg = node("mh.t.msg", 5120),
         *gate = node("mh.t.gate", 8192), *poly = node("mh.t.poly", 2048), *node_e = node("mh.t.energy", 1);
   const float *input = x0;
+  // Both layers' radial MLPs depend on the geometry only: one launch, a grid row per layer
+  // (small cells fill twice the SMs of one layer's launch).
+  for (int k = 0; k < 2; ++k) {
+    std::string p = "mh.l" + std::to_string(k);
+    float *hd = c.array<float>(p + ".hd", 2 * E * 64); // h then dh/dr, one GEMM batch apart
+    ro[k] = RadialOut{hd, hd + E * 64, c.array<float2>(p + ".den", E)};
+  }
+  const Layer *radial_layers[2] = {&m.layers[0], &m.layers[1]};
+  launch_radial(s, c.geometry, radial_layers, ro, 2, pair, ea, projection);
+  timer.mark("radial");
   for (int k = 0; k < 2; ++k) {
     const Layer &l = m.layers[k];
     std::string p = "mh.l" + std::to_string(k);
@@ -277,8 +287,6 @@ std::vector<Result> MH1::compute(bool batch) {
     res[k] = node(p + ".res", 9728); // kept: the backward recomputes raw / den + res
     pin[k] = node(p + ".pin", 8192);
     hidden[k] = node(p + ".hidden", k ? 512 : 2048);
-    float *hd = c.array<float>(p + ".hd", 2 * E * 64); // h then dh/dr, one GEMM batch apart
-    ro[k] = RadialOut{hd, hd + E * 64, c.array<float2>(p + ".den", E)};
     int width = l.paths * 128;
     proj[k] = projection ? c.array<float>(p + ".proj", size_t(2 * chunk_cap) * width) : nullptr;
     // Layer 0's sender features depend on the element only, so ghosts compute their own;
@@ -288,13 +296,12 @@ std::vector<Result> MH1::compute(bool batch) {
       linear(s, ns, l.up, input, up[k], false, false, status);
     else
       linear(s, n, l.up, input, up[k], false, false, status, n, ns);
-    if (dom && k == 1) // overlaps the res / skip linears, the radial MLP and the projection
+    if (dom && k == 1) // overlaps the res / skip linears and the projection
       dom->fetch_ghost_rows(c, up[k], l.in_comp, ns, 128);
     linear(s, n, l.res, up[k], res[k], false, false, status, ns);
     // The skip connection goes straight into the layer output; the product linear adds onto it.
     linear(s, n, l.skip, input, hidden[k], false, false, status, in_rows);
-    launch_radial(s, c.geometry, l, pair, ea, ro[k], projection);
-    timer.mark("forward" + std::to_string(k) + ".linears/radial");
+    timer.mark("forward" + std::to_string(k) + ".linears");
     // The messages feed only linear_1: on the projection path and the tensor cores they are
     // written as the GEMM's split operand.
     SplitPlanes ms;

@@ -125,10 +125,11 @@ void launch_zbl(cudaStream_t, const lapis::DeviceGeometry &, const float *consta
 // pair[e] = sender species | receiver species << 16 (written by launch_edge_geometry).
 void launch_edge_geometry(cudaStream_t, const lapis::DeviceGeometry &, const int *species, const float *constants,
                           const float *radii, const float *bessel, EdgeArrays, int *pair);
-// scaled: ro.h / ro.dh receive cut h and cut dh + dcut h (for the projection path, whose GEMMs
-// then produce cut h W and its r-derivative cut dh W + dcut h W).
-void launch_radial(cudaStream_t, const lapis::DeviceGeometry &, const Layer &, const int *pair, EdgeArrays,
-                   RadialOut, bool scaled = false);
+// Radial and density MLPs of `count` (at most two) layers in one launch, a grid row per
+// layer, into ro[k].  scaled: ro.h / ro.dh receive cut h and cut dh + dcut h (for the
+// projection path, whose GEMMs then produce cut h W and its r-derivative cut dh W + dcut h W).
+void launch_radial(cudaStream_t, const lapis::DeviceGeometry &, const Layer *const *layers, const RadialOut *ro,
+                   int count, const int *pair, EdgeArrays, bool scaled = false);
 void launch_message_forward(cudaStream_t, int layer, const lapis::DeviceGeometry &, const Layer &, EdgeArrays,
                             RadialOut, const float *up, float *message, float *density);
 // ug_edge (layer 1): each edge's up-projection gradient, [E][4][128]; summed onto the senders
