@@ -278,6 +278,23 @@ std::vector<Result> MH1::compute(bool batch) {
   const Layer *radial_layers[2] = {&m.layers[0], &m.layers[1]};
   launch_radial(s, c.geometry, radial_layers, ro, 2, pair, ea, projection);
   timer.mark("radial");
+  for (int k = 0; k < 2 && projection; ++k)
+    proj[k] = c.array<float>("mh.l" + std::to_string(k) + ".proj",
+                             size_t(2 * chunk_cap) * m.layers[k].paths * 128);
+  // With one chunk, the projections that depend on the radial rows only -- both layers'
+  // (cut h) W and layer 1's r-derivative -- go out as one grouped launch now.  Layer 0's
+  // r-derivative waits: its half of the buffer holds the layer-1 up-gradient rows first.
+  bool early_projection = projection && chunks.size() == 1;
+  if (early_projection) {
+    int w0 = m.layers[0].paths * 128, w1 = m.layers[1].paths * 128;
+    GemmSpec g[3] = {
+        GemmSpec{int(E), w0, 64, 1, ro[0].h, 0, m.layers[0].radial.out, proj[0], w0, 0, false},
+        GemmSpec{int(E), w1, 64, 1, ro[1].h, 0, m.layers[1].radial.out, proj[1], w1, 0, false},
+        GemmSpec{int(E), w1, 64, 1, ro[1].dh, 0, m.layers[1].radial.out, proj[1] + size_t(chunk_cap) * w1, w1, 0,
+                 false}};
+    tc_gemm_group(s, g, 3, status);
+    timer.mark("projections");
+  }
   for (int k = 0; k < 2; ++k) {
     const Layer &l = m.layers[k];
     std::string p = "mh.l" + std::to_string(k);
@@ -288,7 +305,6 @@ std::vector<Result> MH1::compute(bool batch) {
     pin[k] = node(p + ".pin", 8192);
     hidden[k] = node(p + ".hidden", k ? 512 : 2048);
     int width = l.paths * 128;
-    proj[k] = projection ? c.array<float>(p + ".proj", size_t(2 * chunk_cap) * width) : nullptr;
     // Layer 0's sender features depend on the element only, so ghosts compute their own;
     // layer 1's come from the ghosts' owners.
     int in_rows = k ? n : ns;
@@ -313,8 +329,9 @@ std::vector<Result> MH1::compute(bool batch) {
     if (projection) {
       for (auto &q : chunks) {
         // (cut h) W per edge row and path channel; the edge kernel adds cut b.
-        tc_gemm(s, int(q.e1 - q.e0), width, 64, 1, ro[k].h + q.e0 * 64, 0, l.radial.out, proj[k], width, 0, false,
-                status);
+        if (!early_projection)
+          tc_gemm(s, int(q.e1 - q.e0), width, 64, 1, ro[k].h + q.e0 * 64, 0, l.radial.out, proj[k], width, 0,
+                  false, status);
         timer.mark("forward" + std::to_string(k) + ".projection");
         if (dom && k == 1 && &q == &chunks.front())
           dom->join(c); // the ghosts' up-projected features have arrived
@@ -418,7 +435,7 @@ std::vector<Result> MH1::compute(bool batch) {
         int rows = int(q.e1 - q.e0);
         // (cut dh + dcut h) W; with several chunks, (cut h) W is recomputed beside it.
         if (chunks.size() == 1) { // (cut h) W is still in place from the forward pass
-          if (!(k == 0 && dR0_ready))
+          if (!(k == 0 && dR0_ready) && !(k == 1 && early_projection))
             tc_gemm(s, rows, width, 64, 1, ro[k].dh + q.e0 * 64, 0, l.radial.out, dR, width, 0, false, status);
         }
         else
